@@ -1,0 +1,176 @@
+/*
+ * moe_dp.h -- C ABI of the B200 routed-expert MoE data plane (libmoe_dp.so).
+ *
+ * One call per layer per step takes hidden states, router logits and a layer id and returns the
+ * combined routed-expert output, the surface of npu-offload's
+ *   Model::moe_phase(l, logits, h2)          track2_opt/solar_engine/src/main.rs:149-209
+ *   Runtime._moe(l, h2, Tb, T)               solar_hybrid/runtime.py:338-423
+ * It also exports the reference's lower-level CPU-kernel surfaces so a caller of those can switch
+ * without reshaping its data:
+ *   cpu_moe(x, gus, ds, toks, ws)            solar_hybrid/cpu_moe.cpp:38-96   -> moe_experts()
+ *   ck_moe3(E, base, w, x, out, H, F)        track2_opt/solar_engine/csrc/cpu_kern.c:141-172 -> moe_ck_moe3()
+ *   ck_moe_q8w(E, q, sc, w, x, out, H, F)    cpu_kern.c:306-333               -> moe_ck_moe_q8w()
+ *   ck_place_expert_q8(g, u, d, q, sc, rs)   cpu_kern.c:227-241               -> moe_place_expert_q8()
+ *
+ * Conventions
+ *  - bf16 values are raw uint16_t bits; all matrices are row-major.
+ *  - Every entry point returns 0 (MOE_OK) or a positive MOE_E* status; moe_last_error() gives the
+ *    calling thread's message for its last failing call.  Unlike the reference's void C kernels,
+ *    nothing aborts the process.
+ *  - Pointers are device pointers unless the call takes MOE_F_HOST, in which case hidden / logits /
+ *    x / out / topk / w pointers are host memory: the library copies them through its own pinned
+ *    staging buffers and the call returns after the result has been copied back.
+ *  - Device-pointer calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ *    stream).  Device-side errors (non-finite router input, a bounded wait that gave up) are
+ *    latched in the context and returned by the next MOE_F_SYNC call or by moe_status().
+ *  - One context per GPU per process.  Calls on one context must be serialised by the caller
+ *    (like the reference engine's single caller thread, main.rs:149); distinct contexts are
+ *    independent.
+ */
+#ifndef MOE_DP_H
+#define MOE_DP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_DP_ABI_VERSION 1
+
+/* status codes */
+#define MOE_OK 0
+#define MOE_EINVAL 1      /* bad argument: null pointer, layer/expert/T out of range, shape limits */
+#define MOE_ENONFINITE 2  /* a router probability was NaN (NaN or +inf logit, or all -inf): the
+                             reference panics here (partial_cmp().unwrap(), host.rs.tpl:259) */
+#define MOE_ECUDA 3       /* CUDA runtime error (message has the CUDA error string) */
+#define MOE_ENOMEM 4      /* device or pinned-host allocation failed */
+#define MOE_ESTATE 5      /* context state: routed expert not loaded, expert not local to this rank */
+#define MOE_ETIMEOUT 6    /* a device-side bounded wait gave up (the kernel returned, nothing hung) */
+#define MOE_ECOMM 7       /* expert-parallel exchange failed */
+
+/* router scoring */
+#define MOE_SCORING_SOFTMAX 0 /* host.rs.tpl:247-268: softmax, top-k by p (ties -> lower index), w = p/sum p */
+#define MOE_SCORING_SIGMOID 1 /* host.rs:119-128: sigmoid + correction bias, w = s/(sum s + 1e-20) */
+
+/* flags */
+#define MOE_F_HOST 0x1       /* data pointers are host memory; call is synchronous */
+#define MOE_F_ACCUMULATE 0x2 /* out += result (ck_moe3 semantics, cpu_kern.c:141) instead of out = result */
+#define MOE_F_SYNC 0x4       /* synchronise `stream` before returning and report device-side status */
+
+/* expert storage kinds */
+#define MOE_KIND_NONE 0
+#define MOE_KIND_BF16 1
+#define MOE_KIND_Q8 2
+
+typedef struct moe_config {
+    int32_t hidden;           /* H (multiple of 256) */
+    int32_t inter;            /* F (multiple of 64) */
+    int32_t n_experts;        /* E, 1..256 */
+    int32_t top_k;            /* K, 1..16, <= E */
+    int32_t n_layers;         /* layers held by this context */
+    int32_t max_tokens;       /* largest T per call, 1..4096 */
+    int32_t scoring;          /* MOE_SCORING_* */
+    int32_t device;           /* CUDA device ordinal */
+    int32_t ep_rank;          /* expert-parallel rank of this context (0 when unsharded) */
+    int32_t ep_world;         /* expert-parallel world size (1 when unsharded) */
+    const int32_t* shard_map; /* optional host array [n_layers * n_experts]: owner rank of each
+                                 (layer, expert); NULL with ep_world == 1 means all local */
+} moe_config;
+
+typedef struct moe_ctx moe_ctx;
+
+MOE_API int moe_abi_version(void);
+MOE_API const char* moe_last_error(void);
+
+/* Create / destroy a context on cfg->device.  Replaces the engine start-up that permutes and
+ * uploads expert tables (track2_opt/solar_engine/src/chip.rs:208-233). */
+MOE_API int moe_create(const moe_config* cfg, moe_ctx** out);
+MOE_API int moe_destroy(moe_ctx* ctx);
+
+/* Load one bf16 expert: gate [F,H], up [F,H], down [H,F] -- the tensors of
+ * Weights::expert (track2_opt/solar_engine/src/host.rs:112-116).  The library stores them in its
+ * own HBM table; the caller keeps ownership of its buffers.  flags: MOE_F_HOST if host pointers. */
+MOE_API int moe_load_expert_bf16(moe_ctx* ctx, int layer, int expert, const uint16_t* gate, const uint16_t* up,
+                         const uint16_t* down, int flags);
+
+/* Load one int8 weight-only expert in the ck_place_expert_q8 layout (cpu_kern.c:227-241):
+ * q = [2F rows of H (gate rows, then up rows)][H rows of F (down)], scales = [2F + H] fp32. */
+MOE_API int moe_load_expert_q8(moe_ctx* ctx, int layer, int expert, const int8_t* q, const float* scales, int flags);
+
+/* Re-store an already loaded bf16 expert as int8 weight-only, quantising on the GPU with the
+ * reference's per-row rule (quant_row, cpu_kern.c:218-224) -- bit-identical tables. */
+MOE_API int moe_quantize_expert_q8(moe_ctx* ctx, int layer, int expert);
+
+/* Kind (MOE_KIND_*) of a stored expert, or -1 on bad arguments. */
+MOE_API int moe_expert_kind(moe_ctx* ctx, int layer, int expert);
+
+/* Sigmoid-scoring correction bias for a layer ([E] fp32; e_score_correction_bias, host.rs:120). */
+MOE_API int moe_set_bias(moe_ctx* ctx, int layer, const float* bias, int flags);
+
+/* The hot path.  hidden [T,H] bf16, router_logits [T,E] fp32 -> out [T,H] fp32
+ *   out[t] = sum_k w[t,k] * expert_{idx[t,k]}(hidden[t])
+ * with idx/w from the configured router.  topk_idx [T,K] int32 and topk_w [T,K] fp32 are
+ * optional outputs (NULL to skip).  Replaces moe_phase's route + dispatch + cold CPU experts +
+ * combine (main.rs:150-207) and Runtime._moe (runtime.py:340-423).  Under expert parallelism
+ * (ep_world > 1) every rank passes the same hidden/logits and receives the full combined output. */
+MOE_API int moe_forward(moe_ctx* ctx, int layer, int T, const uint16_t* hidden, const float* router_logits, float* out,
+                int32_t* topk_idx, float* topk_w, int flags, void* stream);
+
+/* Router + token permutation alone (device pointers unless MOE_F_HOST; bias may be NULL):
+ *   topk_idx/topk_w [T,K]; counts [E]; offsets [E+1] (expert-id order); perm [T*K] pair ids
+ *   t*K+k grouped by expert, tokens ascending (runtime.py:343-347); job_order [E] experts in
+ *   first-appearance order (the cpu_moe job list, runtime.py:352-354); n_jobs [1]. */
+MOE_API int moe_route(moe_ctx* ctx, int T, const float* router_logits, const float* bias, int32_t* topk_idx, float* topk_w,
+              int32_t* counts, int32_t* offsets, int32_t* perm, int32_t* job_order, int32_t* n_jobs, int flags,
+              void* stream);
+
+/* cpu_moe surface (cpu_moe.cpp:38-39) with caller-owned expert weights in device memory:
+ *   x [T,H] bf16; job j uses gu[j] = [2F,H] (gate rows then up rows) and d[j] = [H,F];
+ *   its tokens are toks[tok_off[j] .. tok_off[j+1]) with weights ws[...] (host arrays).
+ * out [T,H] fp32 = sum over jobs (zero-filled first unless MOE_F_ACCUMULATE).  n_jobs == 0
+ * gives zeros, like the reference. */
+MOE_API int moe_experts(moe_ctx* ctx, int T, const uint16_t* x, int n_jobs, const uint16_t* const* gu,
+                const uint16_t* const* d, const int64_t* tok_off, const int64_t* toks, const float* ws, float* out,
+                int flags, void* stream);
+
+/* ck_moe3 surface (cpu_kern.c:141-172): one token, base[e] = device pointer to an expert in the
+ * [g F*H][u F*H][d H*F] layout, w [E]; out [H] += sum_e w[e] * expert_e(x).  Always accumulates. */
+MOE_API int moe_ck_moe3(moe_ctx* ctx, int E, const uint16_t* const* base, const float* w, const uint16_t* x, float* out,
+                int flags, void* stream);
+
+/* ck_moe_q8w surface (cpu_kern.c:306-333): int8 weight-only experts q[e] / sc[e] (device
+ * pointers, ck_place_expert_q8 layout), one token, out [H] += sum_e w[e] * expert_e(x). */
+MOE_API int moe_ck_moe_q8w(moe_ctx* ctx, int E, const int8_t* const* q, const float* const* sc, const float* w,
+                   const uint16_t* x, float* out, int flags, void* stream);
+
+/* ck_place_expert_q8 (cpu_kern.c:227-241) on the GPU: g/u [F,H], d [H,F] bf16 -> q, sc [2F+H],
+ * rs [2F+H] row sums (rs may be NULL).  Device pointers unless MOE_F_HOST. */
+MOE_API int moe_place_expert_q8(moe_ctx* ctx, const uint16_t* g, const uint16_t* u, const uint16_t* d, int8_t* q, float* sc,
+                        int32_t* rs, int flags, void* stream);
+
+/* Synchronise `stream`, then return (and clear) the latched device-side status. */
+MOE_API int moe_status(moe_ctx* ctx, void* stream);
+
+/* Number of kernels this context has launched since creation (instrumentation for benchmarks). */
+MOE_API int64_t moe_launch_count(moe_ctx* ctx);
+
+/* Stage timing of moe_forward with CUDA events on the caller's stream (instrumentation; off by
+ * default).  moe_profile(ctx, 1) starts a fresh record; moe_profile_read synchronises and returns
+ * the summed milliseconds per stage (0 router+permutation, 1 gate/up+SwiGLU kernel, 2 down kernel,
+ * 3 combine kernel) over the calls made since, and the number of calls; it then clears the record. */
+MOE_API int moe_profile(moe_ctx* ctx, int enable);
+MOE_API int moe_profile_read(moe_ctx* ctx, double* stage_ms, int n_stages, int64_t* n_calls);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_DP_H */

@@ -1,0 +1,99 @@
+// Shared device helpers for the B200 MoE data plane (sm_100a).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace moe {
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 16;
+constexpr int kMaxTokens = 4096;
+
+// Latched device-side error bits (ctx->dev_err); host maps them to MOE_E* codes.
+constexpr uint32_t kErrNonFinite = 1u;
+constexpr uint32_t kErrTimeout = 2u;
+constexpr uint32_t kErrBadExpert = 4u;
+constexpr uint32_t kErrBadIndex = 8u;
+
+// ExpDesc::kind values (kKindRemote: owned by another expert-parallel rank, skipped here).
+constexpr int kKindNone = 0;
+constexpr int kKindBF16 = 1;
+constexpr int kKindQ8 = 2;
+constexpr int kKindRemote = 3;
+
+// Per (layer, expert) storage descriptor, resident in HBM.
+//   kind 1 (bf16): w1 = [2F,H] gate rows then up rows, w2 = [H,F] down, sc = null
+//   kind 2 (int8): w1 = [2F,H] int8, w2 = [H,F] int8, sc = [2F+H] fp32 row scales
+struct ExpDesc {
+    const void* w1;
+    const void* w2;
+    const float* sc;
+    int32_t kind;
+    int32_t pad;
+};
+
+// One expert job of a forward call: which weights, which pairs.
+//   pairs [p0, p0+n) of the expert-major pair list; pair p -> token tok[p], weight wt[p]
+struct Job {
+    ExpDesc ex;
+    int32_t p0;
+    int32_t n;
+};
+
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+// fp32 -> bf16 bits, round to nearest even with no NaN special case (same bits as the
+// reference's f2bf, solar_hybrid/cpu_moe.cpp:30-34, for every input).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// SwiGLU activation rounded to bf16, the reference's expression order: g / (1 + exp(-g)) * u
+// (cpu_moe.cpp:75).  expf/IEEE division (no fast-math) keep it within an ulp of the host value.
+__device__ __forceinline__ uint16_t swiglu_bf16(float g, float u) { return f2bf(g / (1.f + expf(-g)) * u); }
+
+// Streaming 128-bit load: read-only, no L1 allocation (weights are read exactly once per call).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// 8 bf16 (one uint4) dot 8 bf16, fp32 FMA into acc.
+__device__ __forceinline__ float dot8_bf16(uint4 w, uint4 x, float acc) {
+    acc = fmaf(bf_lo(w.x), bf_lo(x.x), acc);
+    acc = fmaf(bf_hi(w.x), bf_hi(x.x), acc);
+    acc = fmaf(bf_lo(w.y), bf_lo(x.y), acc);
+    acc = fmaf(bf_hi(w.y), bf_hi(x.y), acc);
+    acc = fmaf(bf_lo(w.z), bf_lo(x.z), acc);
+    acc = fmaf(bf_hi(w.z), bf_hi(x.z), acc);
+    acc = fmaf(bf_lo(w.w), bf_lo(x.w), acc);
+    acc = fmaf(bf_hi(w.w), bf_hi(x.w), acc);
+    return acc;
+}
+
+// int8 value k (0..3) of a 32-bit word, exactly as float.
+__device__ __forceinline__ float i8f(uint32_t v, int k) { return (float)(int8_t)(v >> (8 * k)); }
+
+// 4 int8 weights (one u32) dot 4 bf16 activations (two u32), fp32.
+__device__ __forceinline__ float dot4_i8(uint32_t w, uint32_t x01, uint32_t x23, float acc) {
+    acc = fmaf(i8f(w, 0), bf_lo(x01), acc);
+    acc = fmaf(i8f(w, 1), bf_hi(x01), acc);
+    acc = fmaf(i8f(w, 2), bf_lo(x23), acc);
+    acc = fmaf(i8f(w, 3), bf_hi(x23), acc);
+    return acc;
+}
+
+}  // namespace moe

@@ -1,0 +1,790 @@
+// libmoe_dp: context, expert tables and the C ABI declared in include/moe_dp.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/moe_dp.h"
+#include "common.cuh"
+#include "experts.h"
+#include "route.h"
+
+using namespace moe;
+
+static constexpr int kProfMarks = 5;  // before route, after route, after each of the 3 expert kernels
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                              \
+    do {                                                                                            \
+        cudaError_t e_ = (expr);                                                                    \
+        if (e_ != cudaSuccess) return fail(MOE_ECUDA, "%s: %s", #expr, cudaGetErrorString(e_));     \
+    } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Pinned host staging buffer guarded by an event (reuse waits for the previous copy).
+struct Staging {
+    void* host = nullptr;
+    size_t cap = 0;
+    cudaEvent_t ev = nullptr;
+    bool pending = false;
+    int reserve(size_t bytes) {
+        if (pending) {
+            cudaEventSynchronize(ev);
+            pending = false;
+        }
+        if (bytes <= cap) return MOE_OK;
+        if (host) cudaFreeHost(host);
+        host = nullptr;
+        cap = 0;
+        size_t n = align_up(std::max<size_t>(bytes, 1 << 16), 1 << 16);
+        if (cudaMallocHost(&host, n) != cudaSuccess) return fail(MOE_ENOMEM, "pinned staging of %zu bytes", n);
+        cap = n;
+        return MOE_OK;
+    }
+    void mark(cudaStream_t st) {
+        cudaEventRecord(ev, st);
+        pending = true;
+    }
+};
+
+}  // namespace
+
+struct moe_ctx {
+    moe_config cfg{};
+    int dev = 0;
+    int sm_count = 148;
+    std::vector<int32_t> owner;           // [L*E] owning rank
+    std::vector<int32_t> slot;            // [L*E] local slot, -1 if remote
+    std::vector<int32_t> n_local;         // [L]
+    std::vector<void*> arena;             // [L] lazily allocated expert storage
+    size_t stride = 0;                    // bytes per expert slot
+    std::vector<ExpDesc> h_desc;          // [L*E]
+    ExpDesc* d_desc = nullptr;            // [L*E]
+    float* d_bias = nullptr;              // [L*E]
+    std::vector<char> has_bias;           // [L]
+    // routing / pipeline scratch, sized by max_tokens
+    int32_t *d_idx = nullptr, *d_counts = nullptr, *d_offsets = nullptr, *d_perm = nullptr, *d_jobord = nullptr;
+    int32_t *d_nj = nullptr, *d_nlj = nullptr, *d_ptok = nullptr, *d_pairpos = nullptr, *d_comb_off = nullptr;
+    int32_t* d_comb_p = nullptr;
+    float *d_w = nullptr, *d_pw = nullptr;
+    Job* d_jobs = nullptr;
+    uint16_t* d_act = nullptr;
+    float* d_y = nullptr;
+    uint32_t* d_err = nullptr;
+    uint32_t* h_err = nullptr;  // pinned
+    // MOE_F_HOST staging
+    uint16_t* d_hidden = nullptr;
+    float* d_logits = nullptr;
+    float* d_out = nullptr;
+    Staging in_stage, out_stage, job_stage;
+    int64_t launches = 0;
+    uint32_t latched = 0;
+    // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
+    bool prof_on = false;
+    std::vector<cudaEvent_t> prof_ev;  // kProfMarks events per profiled call
+    size_t prof_calls = 0;
+};
+
+namespace {
+
+bool is_pinned_host(const void* p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
+int map_err(uint32_t bits) {
+    if (bits & kErrTimeout) return fail(MOE_ETIMEOUT, "device-side bounded wait gave up");
+    if (bits & kErrNonFinite) return fail(MOE_ENONFINITE, "router logits produced a NaN probability (NaN/+inf logit or all -inf)");
+    if (bits & kErrBadExpert) return fail(MOE_ESTATE, "a routed expert is not loaded on this context");
+    if (bits & kErrBadIndex) return fail(MOE_EINVAL, "corrupted expert index");
+    return MOE_OK;
+}
+
+// Reads and clears the device error word (the stream must be synchronised by the caller after).
+void queue_err_readback(moe_ctx* c, cudaStream_t st) {
+    cudaMemcpyAsync(c->h_err, c->d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+    cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st);
+}
+
+int finish_sync(moe_ctx* c, cudaStream_t st) {
+    queue_err_readback(c, st);
+    CUDA_TRY(cudaStreamSynchronize(st));
+    uint32_t bits = *c->h_err | c->latched;
+    c->latched = 0;
+    return map_err(bits);
+}
+
+template <class T>
+int dalloc(T** p, size_t n) {
+    if (cudaMalloc((void**)p, std::max<size_t>(n, 1) * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MOE_ENOMEM, "cudaMalloc of %zu bytes", n * sizeof(T));
+    }
+    return MOE_OK;
+}
+
+int check_layer_expert(moe_ctx* c, int layer, int expert) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(MOE_EINVAL, "layer %d out of range [0,%d)", layer, c->cfg.n_layers);
+    if (expert < 0 || expert >= c->cfg.n_experts)
+        return fail(MOE_EINVAL, "expert %d out of range [0,%d)", expert, c->cfg.n_experts);
+    if (c->slot[(size_t)layer * c->cfg.n_experts + expert] < 0)
+        return fail(MOE_ESTATE, "expert (%d,%d) is owned by rank %d, not this rank %d", layer, expert,
+                    c->owner[(size_t)layer * c->cfg.n_experts + expert], c->cfg.ep_rank);
+    return MOE_OK;
+}
+
+int ensure_arena(moe_ctx* c, int layer) {
+    if (c->arena[layer]) return MOE_OK;
+    size_t bytes = c->stride * (size_t)std::max(1, c->n_local[layer]);
+    if (cudaMalloc(&c->arena[layer], bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MOE_ENOMEM, "expert table of layer %d (%zu bytes)", layer, bytes);
+    }
+    return MOE_OK;
+}
+
+char* slot_ptr(moe_ctx* c, int layer, int expert) {
+    return (char*)c->arena[layer] + c->stride * (size_t)c->slot[(size_t)layer * c->cfg.n_experts + expert];
+}
+
+int upload_desc(moe_ctx* c, int layer, int expert, const ExpDesc& d) {
+    size_t i = (size_t)layer * c->cfg.n_experts + expert;
+    c->h_desc[i] = d;
+    CUDA_TRY(cudaMemcpy(c->d_desc + i, &d, sizeof(ExpDesc), cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+size_t q8_scale_off(const moe_ctx* c) {
+    return align_up((size_t)3 * c->cfg.inter * c->cfg.hidden, 256);
+}
+
+// Copies n bytes into device memory dst from src (host when host != 0).
+int copy_in(void* dst, const void* src, size_t n, bool host, cudaStream_t st) {
+    CUDA_TRY(cudaMemcpyAsync(dst, src, n, host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
+    return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_DP_ABI_VERSION; }
+
+const char* moe_last_error(void) { return g_err.c_str(); }
+
+int moe_create(const moe_config* cfg, moe_ctx** out) {
+    if (!cfg || !out) return fail(MOE_EINVAL, "null argument");
+    *out = nullptr;
+    const moe_config& k = *cfg;
+    if (k.hidden <= 0 || k.hidden % 64 != 0 || k.hidden > 16384)
+        return fail(MOE_EINVAL, "hidden %d must be a positive multiple of 64, <= 16384", k.hidden);
+    if (k.inter <= 0 || k.inter % 64 != 0 || k.inter > 2048)
+        return fail(MOE_EINVAL, "inter %d must be a positive multiple of 64, <= 2048", k.inter);
+    if (k.n_experts < 1 || k.n_experts > kMaxExperts) return fail(MOE_EINVAL, "n_experts %d not in [1,%d]", k.n_experts, kMaxExperts);
+    if (k.top_k < 1 || k.top_k > kMaxTopK || k.top_k > k.n_experts)
+        return fail(MOE_EINVAL, "top_k %d not in [1,min(%d,E)]", k.top_k, kMaxTopK);
+    if (k.n_layers < 1) return fail(MOE_EINVAL, "n_layers %d < 1", k.n_layers);
+    if (k.max_tokens < 1 || k.max_tokens > kMaxTokens) return fail(MOE_EINVAL, "max_tokens %d not in [1,%d]", k.max_tokens, kMaxTokens);
+    if (k.scoring != MOE_SCORING_SOFTMAX && k.scoring != MOE_SCORING_SIGMOID) return fail(MOE_EINVAL, "unknown scoring %d", k.scoring);
+    if (k.ep_world < 1 || k.ep_rank < 0 || k.ep_rank >= k.ep_world) return fail(MOE_EINVAL, "bad ep rank %d / world %d", k.ep_rank, k.ep_world);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(MOE_ECUDA, "no CUDA device available");
+    }
+    if (k.device < 0 || k.device >= ndev) return fail(MOE_EINVAL, "device %d not in [0,%d)", k.device, ndev);
+    DeviceGuard dg(k.device);
+    moe_ctx* c = new moe_ctx;
+    c->cfg = k;
+    c->cfg.shard_map = nullptr;
+    c->dev = k.device;
+    cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, k.device);
+    const int L = k.n_layers, E = k.n_experts;
+    c->owner.assign((size_t)L * E, 0);
+    c->slot.assign((size_t)L * E, -1);
+    c->n_local.assign(L, 0);
+    for (int l = 0; l < L; l++)
+        for (int e = 0; e < E; e++) {
+            int r = k.shard_map ? k.shard_map[(size_t)l * E + e] : (k.ep_world == 1 ? 0 : e % k.ep_world);
+            if (r < 0 || r >= k.ep_world) {
+                delete c;
+                return fail(MOE_EINVAL, "shard_map[%d][%d] = %d not in [0,%d)", l, e, r, k.ep_world);
+            }
+            c->owner[(size_t)l * E + e] = r;
+            if (r == k.ep_rank) c->slot[(size_t)l * E + e] = c->n_local[l]++;
+        }
+    c->arena.assign(L, nullptr);
+    c->stride = align_up((size_t)3 * k.inter * k.hidden * 2, 256);
+    c->h_desc.assign((size_t)L * E, ExpDesc{nullptr, nullptr, nullptr, kKindNone, 0});
+    for (size_t i = 0; i < c->h_desc.size(); i++)
+        if (c->slot[i] < 0) c->h_desc[i].kind = kKindRemote;
+    c->has_bias.assign(L, 0);
+    const size_t NP = (size_t)k.max_tokens * k.top_k;
+    int st = MOE_OK;
+    if (!st) st = dalloc(&c->d_desc, (size_t)L * E);
+    if (!st) st = dalloc(&c->d_bias, (size_t)L * E);
+    if (!st) st = dalloc(&c->d_idx, NP);
+    if (!st) st = dalloc(&c->d_w, NP);
+    if (!st) st = dalloc(&c->d_counts, E);
+    if (!st) st = dalloc(&c->d_offsets, E + 1);
+    if (!st) st = dalloc(&c->d_perm, NP);
+    if (!st) st = dalloc(&c->d_jobord, E);
+    if (!st) st = dalloc(&c->d_nj, 1);
+    if (!st) st = dalloc(&c->d_nlj, 1);
+    if (!st) st = dalloc(&c->d_ptok, NP);
+    if (!st) st = dalloc(&c->d_pw, NP);
+    if (!st) st = dalloc(&c->d_pairpos, NP);
+    if (!st) st = dalloc(&c->d_comb_off, (size_t)k.max_tokens + 1);
+    if (!st) st = dalloc(&c->d_comb_p, NP);
+    if (!st) st = dalloc(&c->d_jobs, E);
+    if (!st) st = dalloc(&c->d_act, NP * k.inter);
+    if (!st) st = dalloc(&c->d_y, NP * k.hidden);
+    if (!st) st = dalloc(&c->d_err, 1);
+    if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
+    if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
+    if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
+    if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
+    if (!st && (cudaEventCreateWithFlags(&c->in_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&c->out_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&c->job_stage.ev, cudaEventDisableTiming) != cudaSuccess))
+        st = fail(MOE_ECUDA, "event creation failed");
+    if (!st && cudaMemcpy(c->d_desc, c->h_desc.data(), sizeof(ExpDesc) * c->h_desc.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        st = fail(MOE_ECUDA, "descriptor upload failed");
+    if (!st && cudaMemset(c->d_err, 0, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
+    if (!st && cudaMemset(c->d_bias, 0, sizeof(float) * (size_t)L * E) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
+    if (!st) {
+        cudaError_t e = route_set_smem_limits();
+        if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
+    }
+    if (st) {
+        moe_destroy(c);
+        return st;
+    }
+    *out = c;
+    return MOE_OK;
+}
+
+int moe_destroy(moe_ctx* c) {
+    if (!c) return MOE_OK;
+    DeviceGuard dg(c->dev);
+    cudaDeviceSynchronize();
+    for (void* p : c->arena) cudaFree(p);
+    void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
+                  c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
+                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out};
+    for (void* p : ps) cudaFree(p);
+    if (c->h_err) cudaFreeHost(c->h_err);
+    for (cudaEvent_t ev : c->prof_ev) cudaEventDestroy(ev);
+    for (Staging* s : {&c->in_stage, &c->out_stage, &c->job_stage}) {
+        if (s->host) cudaFreeHost(s->host);
+        if (s->ev) cudaEventDestroy(s->ev);
+    }
+    delete c;
+    return MOE_OK;
+}
+
+int moe_load_expert_bf16(moe_ctx* c, int layer, int expert, const uint16_t* gate, const uint16_t* up,
+                         const uint16_t* down, int flags) {
+    int st = check_layer_expert(c, layer, expert);
+    if (st) return st;
+    if (!gate || !up || !down) return fail(MOE_EINVAL, "null weight pointer");
+    DeviceGuard dg(c->dev);
+    if ((st = ensure_arena(c, layer))) return st;
+    const size_t FH = (size_t)c->cfg.inter * c->cfg.hidden;
+    char* base = slot_ptr(c, layer, expert);
+    const bool host = flags & MOE_F_HOST;
+    if ((st = copy_in(base, gate, FH * 2, host, 0))) return st;
+    if ((st = copy_in(base + FH * 2, up, FH * 2, host, 0))) return st;
+    if ((st = copy_in(base + FH * 4, down, FH * 2, host, 0))) return st;
+    CUDA_TRY(cudaStreamSynchronize(0));
+    return upload_desc(c, layer, expert, ExpDesc{base, base + FH * 4, nullptr, kKindBF16, 0});
+}
+
+int moe_load_expert_q8(moe_ctx* c, int layer, int expert, const int8_t* q, const float* scales, int flags) {
+    int st = check_layer_expert(c, layer, expert);
+    if (st) return st;
+    if (!q || !scales) return fail(MOE_EINVAL, "null weight pointer");
+    DeviceGuard dg(c->dev);
+    if ((st = ensure_arena(c, layer))) return st;
+    const size_t H = c->cfg.hidden, F = c->cfg.inter;
+    char* base = slot_ptr(c, layer, expert);
+    const bool host = flags & MOE_F_HOST;
+    if ((st = copy_in(base, q, 3 * F * H, host, 0))) return st;
+    if ((st = copy_in(base + q8_scale_off(c), scales, (2 * F + H) * 4, host, 0))) return st;
+    CUDA_TRY(cudaStreamSynchronize(0));
+    return upload_desc(c, layer, expert,
+                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, 0});
+}
+
+int moe_quantize_expert_q8(moe_ctx* c, int layer, int expert) {
+    int st = check_layer_expert(c, layer, expert);
+    if (st) return st;
+    const size_t i = (size_t)layer * c->cfg.n_experts + expert;
+    if (c->h_desc[i].kind != kKindBF16) return fail(MOE_ESTATE, "expert (%d,%d) is not a loaded bf16 expert", layer, expert);
+    DeviceGuard dg(c->dev);
+    const size_t H = c->cfg.hidden, F = c->cfg.inter;
+    char* base = slot_ptr(c, layer, expert);
+    char* tmp = nullptr;
+    const size_t bytes = q8_scale_off(c) + (2 * F + H) * 4;
+    if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MOE_ENOMEM, "quantisation scratch");
+    }
+    int n = 0;
+    cudaError_t e = launch_quantize_q8((const uint16_t*)base, (const uint16_t*)(base + F * H * 2),
+                                       (const uint16_t*)(base + F * H * 4), (int)H, (int)F, (int8_t*)tmp,
+                                       (float*)(tmp + q8_scale_off(c)), nullptr, 0, &n);
+    c->launches += n;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(base, tmp, bytes, cudaMemcpyDeviceToDevice, 0);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise: %s", cudaGetErrorString(e));
+    return upload_desc(c, layer, expert,
+                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, 0});
+}
+
+int moe_expert_kind(moe_ctx* c, int layer, int expert) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers || expert < 0 || expert >= c->cfg.n_experts) return -1;
+    int k = c->h_desc[(size_t)layer * c->cfg.n_experts + expert].kind;
+    return k == kKindRemote ? MOE_KIND_NONE : k;
+}
+
+int moe_set_bias(moe_ctx* c, int layer, const float* bias, int flags) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers) return fail(MOE_EINVAL, "bad context or layer");
+    DeviceGuard dg(c->dev);
+    if (!bias) {
+        CUDA_TRY(cudaMemset(c->d_bias + (size_t)layer * c->cfg.n_experts, 0, sizeof(float) * c->cfg.n_experts));
+        c->has_bias[layer] = 0;
+        return MOE_OK;
+    }
+    CUDA_TRY(cudaMemcpy(c->d_bias + (size_t)layer * c->cfg.n_experts, bias, sizeof(float) * c->cfg.n_experts,
+                        (flags & MOE_F_HOST) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice));
+    c->has_bias[layer] = 1;
+    return MOE_OK;
+}
+
+static RouteArgs route_args(moe_ctx* c, int T, const float* logits, const float* bias) {
+    RouteArgs a{};
+    a.logits = logits;
+    a.bias = bias;
+    a.T = T;
+    a.E = c->cfg.n_experts;
+    a.K = c->cfg.top_k;
+    a.scoring = c->cfg.scoring;
+    a.idx = c->d_idx;
+    a.w = c->d_w;
+    a.counts = c->d_counts;
+    a.offsets = c->d_offsets;
+    a.perm = c->d_perm;
+    a.job_order = c->d_jobord;
+    a.n_jobs = c->d_nj;
+    a.ptok = c->d_ptok;
+    a.pw = c->d_pw;
+    a.pairpos = c->d_pairpos;
+    a.comb_off = c->d_comb_off;
+    a.comb_p = c->d_comb_p;
+    a.jobs = c->d_jobs;
+    a.n_ljobs = c->d_nlj;
+    a.err = c->d_err;
+    return a;
+}
+
+int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const float* logits, float* out,
+                int32_t* topk_idx, float* topk_w, int flags, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(MOE_EINVAL, "layer %d out of range [0,%d)", layer, c->cfg.n_layers);
+    if (T < 0 || T > c->cfg.max_tokens) return fail(MOE_EINVAL, "T=%d not in [0,%d]", T, c->cfg.max_tokens);
+    if (T > 0 && (!hidden || !logits || !out)) return fail(MOE_EINVAL, "null hidden/logits/out");
+    DeviceGuard dg(c->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool host = flags & MOE_F_HOST;
+    const int H = c->cfg.hidden, E = c->cfg.n_experts, K = c->cfg.top_k;
+    const uint16_t* x = hidden;
+    const float* lg = logits;
+    float* o = out;
+    int s;
+    if (host && T > 0) {
+        const size_t hb = (size_t)T * H * 2, lb = (size_t)T * E * 4;
+        if (is_pinned_host(hidden) && is_pinned_host(logits)) {
+            CUDA_TRY(cudaMemcpyAsync(c->d_hidden, hidden, hb, cudaMemcpyHostToDevice, st));
+            CUDA_TRY(cudaMemcpyAsync(c->d_logits, logits, lb, cudaMemcpyHostToDevice, st));
+        } else {
+            if ((s = c->in_stage.reserve(hb + lb))) return s;
+            memcpy(c->in_stage.host, hidden, hb);
+            memcpy((char*)c->in_stage.host + hb, logits, lb);
+            CUDA_TRY(cudaMemcpyAsync(c->d_hidden, c->in_stage.host, hb, cudaMemcpyHostToDevice, st));
+            CUDA_TRY(cudaMemcpyAsync(c->d_logits, (char*)c->in_stage.host + hb, lb, cudaMemcpyHostToDevice, st));
+            c->in_stage.mark(st);
+        }
+        x = c->d_hidden;
+        lg = c->d_logits;
+        o = c->d_out;
+        if (flags & MOE_F_ACCUMULATE) CUDA_TRY(cudaMemcpyAsync(o, out, (size_t)T * H * 4, cudaMemcpyHostToDevice, st));
+    }
+    int n = 0;
+    cudaEvent_t* marks = nullptr;
+    if (c->prof_on && T > 0) {
+        const size_t need = (c->prof_calls + 1) * kProfMarks;
+        while (c->prof_ev.size() < need) {
+            cudaEvent_t ev;
+            CUDA_TRY(cudaEventCreate(&ev));
+            c->prof_ev.push_back(ev);
+        }
+        marks = &c->prof_ev[c->prof_calls * kProfMarks];
+        c->prof_calls++;
+        CUDA_TRY(cudaEventRecord(marks[0], st));
+    }
+    if (T > 0) {
+        RouteArgs ra = route_args(c, T, lg, c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr);
+        ra.desc = c->d_desc + (size_t)layer * E;
+        cudaError_t e = launch_route(ra, st, &n);
+        if (marks) cudaEventRecord(marks[1], st);
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "route launch: %s", cudaGetErrorString(e));
+        ExpertArgs ea{};
+        ea.x = x;
+        ea.T = T;
+        ea.H = H;
+        ea.F = c->cfg.inter;
+        ea.jobs = c->d_jobs;
+        ea.n_jobs = c->d_nlj;
+        ea.n_jobs_host = -1;
+        ea.n_jobs_max = std::min(E, T * K);
+        ea.max_pairs = T;
+        ea.ptok = c->d_ptok;
+        ea.pw = c->d_pw;
+        ea.act = c->d_act;
+        ea.y = c->d_y;
+        ea.comb_off = c->d_comb_off;
+        ea.comb_p = c->d_comb_p;
+        ea.out = o;
+        ea.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
+        ea.err = c->d_err;
+        e = launch_experts(ea, c->sm_count, st, &n, marks ? marks + 2 : nullptr);
+        c->launches += n;
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
+        const cudaMemcpyKind dk = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+        if (topk_idx) CUDA_TRY(cudaMemcpyAsync(topk_idx, c->d_idx, sizeof(int32_t) * T * K, dk, st));
+        if (topk_w) CUDA_TRY(cudaMemcpyAsync(topk_w, c->d_w, sizeof(float) * T * K, dk, st));
+    }
+    if (host) {
+        if (T > 0) {
+            const size_t ob = (size_t)T * H * 4;
+            if (is_pinned_host(out)) {
+                CUDA_TRY(cudaMemcpyAsync(out, o, ob, cudaMemcpyDeviceToHost, st));
+                return finish_sync(c, st);
+            }
+            if ((s = c->out_stage.reserve(ob))) return s;
+            CUDA_TRY(cudaMemcpyAsync(c->out_stage.host, o, ob, cudaMemcpyDeviceToHost, st));
+            int r = finish_sync(c, st);
+            memcpy(out, c->out_stage.host, ob);
+            return r;
+        }
+        return finish_sync(c, st);
+    }
+    if (flags & MOE_F_SYNC) return finish_sync(c, st);
+    return MOE_OK;
+}
+
+int moe_route(moe_ctx* c, int T, const float* logits, const float* bias, int32_t* topk_idx, float* topk_w,
+              int32_t* counts, int32_t* offsets, int32_t* perm, int32_t* job_order, int32_t* n_jobs, int flags,
+              void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (T < 0 || T > c->cfg.max_tokens) return fail(MOE_EINVAL, "T=%d not in [0,%d]", T, c->cfg.max_tokens);
+    if (T > 0 && !logits) return fail(MOE_EINVAL, "null logits");
+    DeviceGuard dg(c->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool host = flags & MOE_F_HOST;
+    const int E = c->cfg.n_experts, K = c->cfg.top_k;
+    const float* lg = logits;
+    const float* b = bias;
+    if (host) {
+        if (T > 0) CUDA_TRY(cudaMemcpyAsync(c->d_logits, logits, sizeof(float) * T * E, cudaMemcpyHostToDevice, st));
+        lg = c->d_logits;
+        if (bias) {
+            CUDA_TRY(cudaMemcpyAsync(c->d_out, bias, sizeof(float) * E, cudaMemcpyHostToDevice, st));
+            b = c->d_out;
+        }
+    }
+    RouteArgs ra = route_args(c, T, lg, b);
+    ra.desc = nullptr;
+    ra.jobs = nullptr;
+    ra.n_ljobs = nullptr;
+    int n = 0;
+    cudaError_t e = launch_route(ra, st, &n);
+    c->launches += n;
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "route launch: %s", cudaGetErrorString(e));
+    const cudaMemcpyKind dk = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    const size_t NP = (size_t)T * K;
+    if (topk_idx && NP) CUDA_TRY(cudaMemcpyAsync(topk_idx, c->d_idx, 4 * NP, dk, st));
+    if (topk_w && NP) CUDA_TRY(cudaMemcpyAsync(topk_w, c->d_w, 4 * NP, dk, st));
+    if (counts) CUDA_TRY(cudaMemcpyAsync(counts, c->d_counts, 4 * E, dk, st));
+    if (offsets) CUDA_TRY(cudaMemcpyAsync(offsets, c->d_offsets, 4 * (E + 1), dk, st));
+    if (perm && NP) CUDA_TRY(cudaMemcpyAsync(perm, c->d_perm, 4 * NP, dk, st));
+    if (job_order) CUDA_TRY(cudaMemcpyAsync(job_order, c->d_jobord, 4 * E, dk, st));
+    if (n_jobs) CUDA_TRY(cudaMemcpyAsync(n_jobs, c->d_nj, 4, dk, st));
+    if (host || (flags & MOE_F_SYNC)) return finish_sync(c, st);
+    return MOE_OK;
+}
+
+// Shared body of the explicit-job surfaces (cpu_moe, ck_moe3, ck_moe_q8w).
+static int run_jobs(moe_ctx* c, int T, const uint16_t* x, const std::vector<Job>& jobs,
+                    const std::vector<int32_t>& ptok, const float* pw_src, bool pw_host, const std::vector<int32_t>& comb_off,
+                    const std::vector<int32_t>& comb_p, float* out, int flags, cudaStream_t st) {
+    const int H = c->cfg.hidden;
+    const size_t NP = ptok.size();
+    if (NP > (size_t)c->cfg.max_tokens * c->cfg.top_k)
+        return fail(MOE_EINVAL, "%zu routed pairs exceed the context capacity %d (max_tokens * top_k)", NP,
+                    c->cfg.max_tokens * c->cfg.top_k);
+    if ((size_t)T > (size_t)c->cfg.max_tokens) return fail(MOE_EINVAL, "T=%d exceeds max_tokens", T);
+    const bool host = flags & MOE_F_HOST;
+    const size_t jb = jobs.size() * sizeof(Job), pb = NP * 4, cb = comb_off.size() * 4, qb = comb_p.size() * 4;
+    int s;
+    if ((s = c->job_stage.reserve(jb + pb + cb + qb + (pw_host ? pb : 0) + 64))) return s;
+    char* hp = (char*)c->job_stage.host;
+    memcpy(hp, jobs.data(), jb);
+    memcpy(hp + jb, ptok.data(), pb);
+    memcpy(hp + jb + pb, comb_off.data(), cb);
+    memcpy(hp + jb + pb + cb, comb_p.data(), qb);
+    if (jb) CUDA_TRY(cudaMemcpyAsync(c->d_jobs, hp, jb, cudaMemcpyHostToDevice, st));
+    if (pb) CUDA_TRY(cudaMemcpyAsync(c->d_ptok, hp + jb, pb, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(c->d_comb_off, hp + jb + pb, cb, cudaMemcpyHostToDevice, st));
+    if (qb) CUDA_TRY(cudaMemcpyAsync(c->d_comb_p, hp + jb + pb + cb, qb, cudaMemcpyHostToDevice, st));
+    if (pb) {
+        if (pw_host) {
+            memcpy(hp + jb + pb + cb + qb, pw_src, pb);
+            CUDA_TRY(cudaMemcpyAsync(c->d_pw, hp + jb + pb + cb + qb, pb, cudaMemcpyHostToDevice, st));
+        } else {
+            CUDA_TRY(cudaMemcpyAsync(c->d_pw, pw_src, pb, cudaMemcpyDeviceToDevice, st));
+        }
+    }
+    c->job_stage.mark(st);
+    const uint16_t* xd = x;
+    float* od = out;
+    if (host) {
+        CUDA_TRY(cudaMemcpyAsync(c->d_hidden, x, (size_t)T * H * 2, cudaMemcpyHostToDevice, st));
+        xd = c->d_hidden;
+        od = c->d_out;
+        if (flags & MOE_F_ACCUMULATE) CUDA_TRY(cudaMemcpyAsync(od, out, (size_t)T * H * 4, cudaMemcpyHostToDevice, st));
+    }
+    ExpertArgs ea{};
+    ea.x = xd;
+    ea.T = T;
+    ea.H = H;
+    ea.F = c->cfg.inter;
+    ea.jobs = c->d_jobs;
+    ea.n_jobs = nullptr;
+    ea.n_jobs_host = (int)jobs.size();
+    ea.n_jobs_max = (int)jobs.size();
+    int mp = 0;
+    for (const Job& j : jobs) mp = std::max(mp, j.n);
+    ea.max_pairs = mp;
+    ea.ptok = c->d_ptok;
+    ea.pw = c->d_pw;
+    ea.act = c->d_act;
+    ea.y = c->d_y;
+    ea.comb_off = c->d_comb_off;
+    ea.comb_p = c->d_comb_p;
+    ea.out = od;
+    ea.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
+    ea.err = c->d_err;
+    int n = 0;
+    cudaError_t e = launch_experts(ea, c->sm_count, st, &n, nullptr);
+    c->launches += n;
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
+    if (host) {
+        CUDA_TRY(cudaMemcpyAsync(out, od, (size_t)T * H * 4, cudaMemcpyDeviceToHost, st));
+        return finish_sync(c, st);
+    }
+    if (flags & MOE_F_SYNC) return finish_sync(c, st);
+    return MOE_OK;
+}
+
+int moe_experts(moe_ctx* c, int T, const uint16_t* x, int n_jobs, const uint16_t* const* gu, const uint16_t* const* d,
+                const int64_t* tok_off, const int64_t* toks, const float* ws, float* out, int flags, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (T < 0 || n_jobs < 0) return fail(MOE_EINVAL, "negative T or n_jobs");
+    if (T > 0 && (!x || !out)) return fail(MOE_EINVAL, "null x/out");
+    if (n_jobs > 0 && (!gu || !d || !tok_off || !toks || !ws)) return fail(MOE_EINVAL, "null job arrays");
+    DeviceGuard dg(c->dev);
+    const int F = c->cfg.inter;
+    std::vector<Job> jobs(n_jobs);
+    std::vector<int32_t> ptok;
+    std::vector<std::vector<int32_t>> per_tok(T);
+    if (n_jobs > 0 && tok_off[0] != 0) return fail(MOE_EINVAL, "tok_off[0] must be 0");
+    for (int j = 0; j < n_jobs; j++) {
+        if (!gu[j] || !d[j]) return fail(MOE_EINVAL, "null weights for job %d", j);
+        const int64_t a = tok_off[j], b = tok_off[j + 1];
+        if (b < a) return fail(MOE_EINVAL, "tok_off not monotone at job %d", j);
+        jobs[j] = Job{ExpDesc{gu[j], d[j], nullptr, kKindBF16, 0}, (int32_t)a, (int32_t)(b - a)};
+        for (int64_t i = a; i < b; i++) {
+            if (toks[i] < 0 || toks[i] >= T) return fail(MOE_EINVAL, "token %lld of job %d out of range [0,%d)", (long long)toks[i], j, T);
+            per_tok[toks[i]].push_back((int32_t)i);
+            ptok.push_back((int32_t)toks[i]);
+        }
+    }
+    (void)F;
+    std::vector<int32_t> comb_off(T + 1, 0), comb_p;
+    for (int t = 0; t < T; t++) {
+        comb_off[t + 1] = comb_off[t] + (int32_t)per_tok[t].size();
+        comb_p.insert(comb_p.end(), per_tok[t].begin(), per_tok[t].end());
+    }
+    return run_jobs(c, T, x, jobs, ptok, ws, true, comb_off, comb_p, out, flags, (cudaStream_t)stream);
+}
+
+static int single_token_jobs(moe_ctx* c, int E, std::vector<Job>& jobs, std::vector<int32_t>& ptok,
+                             std::vector<int32_t>& comb_off, std::vector<int32_t>& comb_p) {
+    (void)c;
+    jobs.resize(E);
+    ptok.assign(E, 0);
+    comb_off = {0, E};
+    comb_p.resize(E);
+    for (int e = 0; e < E; e++) comb_p[e] = e;
+    return MOE_OK;
+}
+
+int moe_ck_moe3(moe_ctx* c, int E, const uint16_t* const* base, const float* w, const uint16_t* x, float* out, int flags,
+                void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (E <= 0) return MOE_OK;  // cpu_kern.c:142: no experts, nothing to add
+    if (!base || !w || !x || !out) return fail(MOE_EINVAL, "null argument");
+    DeviceGuard dg(c->dev);
+    const size_t FH = (size_t)c->cfg.inter * c->cfg.hidden;
+    std::vector<Job> jobs;
+    std::vector<int32_t> ptok, co, cp;
+    single_token_jobs(c, E, jobs, ptok, co, cp);
+    for (int e = 0; e < E; e++) {
+        if (!base[e]) return fail(MOE_EINVAL, "null base[%d]", e);
+        jobs[e] = Job{ExpDesc{base[e], base[e] + 2 * FH, nullptr, kKindBF16, 0}, e, 1};
+    }
+    return run_jobs(c, 1, x, jobs, ptok, w, (flags & MOE_F_HOST) != 0, co, cp, out, flags | MOE_F_ACCUMULATE,
+                    (cudaStream_t)stream);
+}
+
+int moe_ck_moe_q8w(moe_ctx* c, int E, const int8_t* const* q, const float* const* sc, const float* w, const uint16_t* x,
+                   float* out, int flags, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (E <= 0) return MOE_OK;  // cpu_kern.c:307
+    if (!q || !sc || !w || !x || !out) return fail(MOE_EINVAL, "null argument");
+    DeviceGuard dg(c->dev);
+    const size_t FH = (size_t)c->cfg.inter * c->cfg.hidden;
+    std::vector<Job> jobs;
+    std::vector<int32_t> ptok, co, cp;
+    single_token_jobs(c, E, jobs, ptok, co, cp);
+    for (int e = 0; e < E; e++) {
+        if (!q[e] || !sc[e]) return fail(MOE_EINVAL, "null q/sc[%d]", e);
+        jobs[e] = Job{ExpDesc{q[e], q[e] + 2 * FH, sc[e], kKindQ8, 0}, e, 1};
+    }
+    return run_jobs(c, 1, x, jobs, ptok, w, (flags & MOE_F_HOST) != 0, co, cp, out, flags | MOE_F_ACCUMULATE,
+                    (cudaStream_t)stream);
+}
+
+int moe_place_expert_q8(moe_ctx* c, const uint16_t* g, const uint16_t* u, const uint16_t* d, int8_t* q, float* sc,
+                        int32_t* rs, int flags, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (!g || !u || !d || !q || !sc) return fail(MOE_EINVAL, "null argument");
+    DeviceGuard dg(c->dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t H = c->cfg.hidden, F = c->cfg.inter, FH = F * H, R = 2 * F + H;
+    int n = 0;
+    if (!(flags & MOE_F_HOST)) {
+        cudaError_t e = launch_quantize_q8(g, u, d, (int)H, (int)F, q, sc, rs, st, &n);
+        c->launches += n;
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise launch: %s", cudaGetErrorString(e));
+        if (flags & MOE_F_SYNC) return finish_sync(c, st);
+        return MOE_OK;
+    }
+    char* tmp = nullptr;
+    const size_t bytes = FH * 2 * 3 + 3 * FH + R * 8;
+    if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(MOE_ENOMEM, "quantisation scratch");
+    }
+    uint16_t* dg_ = (uint16_t*)tmp;
+    int8_t* dq = (int8_t*)(tmp + FH * 6);
+    float* dsc = (float*)(tmp + FH * 6 + 3 * FH);
+    int32_t* drs = (int32_t*)(tmp + FH * 6 + 3 * FH + R * 4);
+    cudaError_t e = cudaMemcpyAsync(dg_, g, FH * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dg_ + FH, u, FH * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dg_ + 2 * FH, d, FH * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = launch_quantize_q8(dg_, dg_ + FH, dg_ + 2 * FH, (int)H, (int)F, dq, dsc, drs, st, &n);
+    c->launches += n;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(q, dq, 3 * FH, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(sc, dsc, R * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && rs) e = cudaMemcpyAsync(rs, drs, R * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise: %s", cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+int moe_status(moe_ctx* c, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    DeviceGuard dg(c->dev);
+    return finish_sync(c, (cudaStream_t)stream);
+}
+
+int64_t moe_launch_count(moe_ctx* c) { return c ? c->launches : -1; }
+
+int moe_profile(moe_ctx* c, int enable) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    c->prof_on = enable != 0;
+    c->prof_calls = 0;
+    return MOE_OK;
+}
+
+int moe_profile_read(moe_ctx* c, double* stage_ms, int n_stages, int64_t* n_calls) {
+    if (!c || !stage_ms || n_stages < 1) return fail(MOE_EINVAL, "bad argument");
+    DeviceGuard dg(c->dev);
+    for (int i = 0; i < n_stages; i++) stage_ms[i] = 0.0;
+    for (size_t k = 0; k < c->prof_calls; k++) {
+        cudaEvent_t* m = &c->prof_ev[k * kProfMarks];
+        CUDA_TRY(cudaEventSynchronize(m[kProfMarks - 1]));
+        for (int i = 0; i < n_stages && i < kProfMarks - 1; i++) {
+            float ms = 0.f;
+            CUDA_TRY(cudaEventElapsedTime(&ms, m[i], m[i + 1]));
+            stage_ms[i] += ms;
+        }
+    }
+    if (n_calls) *n_calls = (int64_t)c->prof_calls;
+    c->prof_calls = 0;
+    return MOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,311 @@
+// Router (fused softmax or sigmoid+bias / top-k / renormalise) and the deterministic token->expert
+// permutation for the B200 MoE data plane.
+//
+// Router semantics: npu-kernels/npu_kernels/rngd/layer_template/src/host.rs.tpl:247-268 (softmax)
+// and track2_opt/solar_engine/src/host.rs:119-128 (sigmoid + correction bias):
+//   softmax: m = max v; e_i = exp(v_i - m); z = sum_i e_i in index order; p_i = e_i / z;
+//            top-k by p, ties -> lower index; w_k = p_k / sum_k p_k (sequential, no epsilon)
+//   sigmoid: s_i = 1 / (1 + exp(-v_i)); key_i = s_i + bias_i; top-k by key; w_k = s_k / (sum s + 1e-20)
+// The exponential is evaluated in double and rounded once to fp32 (a correctly rounded expf), so the
+// fp32 probabilities -- and therefore the top-k order including rounding ties -- match a host that
+// uses a correctly rounded expf.  The two sums are sequential in the reference's order.
+//
+// Permutation semantics: solar_hybrid/runtime.py:343-354 -- pairs (t, k) grouped per expert with
+// tokens ascending; experts listed in first-appearance order of the t-major, k-minor scan.
+#include "common.cuh"
+#include "route.h"
+
+namespace moe {
+
+// Lexicographic "better" for the top-k scan: larger key, then lower index.  A NaN key never beats
+// a real candidate but does replace the empty sentinel, so every round still yields a valid index.
+__device__ __forceinline__ bool better(float ka, int ia, float kb, int ib) {
+    if (ib < 0) return ia >= 0;
+    if (ia < 0) return false;
+    return ka > kb || (ka == kb && ia < ib);
+}
+
+// One warp routes one token.  ev: per-warp shared scratch of E floats.
+__device__ void route_token_warp(const RouteArgs& a, int t, float* ev) {
+    const int lane = threadIdx.x & 31;
+    const int E = a.E, K = a.K;
+    const float* v = a.logits + (size_t)t * E;
+    constexpr int S = kMaxExperts / 32;
+    float key[S];
+    bool bad = false;
+    if (a.scoring == 0) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            int i = lane + 32 * s;
+            if (i < E) {
+                float x = v[i];
+                m = x > m ? x : m;  // f32::max fold: NaN never replaces the running max
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float y = __shfl_xor_sync(0xffffffffu, m, o);
+            m = y > m ? y : m;
+        }
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            int i = lane + 32 * s;
+            if (i < E) ev[i] = (float)exp((double)(v[i] - m));
+        }
+        __syncwarp();
+        float z = 0.f;
+        if (lane == 0)
+            for (int i = 0; i < E; i++) z += ev[i];
+        z = __shfl_sync(0xffffffffu, z, 0);
+        __syncwarp();
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            int i = lane + 32 * s;
+            key[s] = -INFINITY;
+            if (i < E) {
+                float p = __fdiv_rn(ev[i], z);
+                key[s] = p;
+                ev[i] = p;  // weight value of expert i
+                bad |= (p != p);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            int i = lane + 32 * s;
+            key[s] = -INFINITY;
+            if (i < E) {
+                float sg = __fdiv_rn(1.0f, 1.0f + (float)exp(-(double)v[i]));
+                float k = sg + (a.bias ? a.bias[i] : 0.f);
+                key[s] = k;
+                ev[i] = sg;
+                bad |= (k != k);
+            }
+        }
+    }
+    __syncwarp();
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.err, kErrNonFinite);
+
+    unsigned taken = 0;  // bit s: expert lane + 32 s already selected
+    int sel[kMaxTopK];
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; k++) sel[k] = 0;
+    for (int k = 0; k < K; k++) {
+        float bk = -INFINITY;
+        int bi = -1;
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            int i = lane + 32 * s;
+            if (i < E && !((taken >> s) & 1u) && better(key[s], i, bk, bi)) {
+                bk = key[s];
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ok, oi, bk, bi)) {
+                bk = ok;
+                bi = oi;
+            }
+        }
+        bi = __shfl_sync(0xffffffffu, bi, 0);  // one winner for every lane even with NaN keys
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+#pragma unroll
+        for (int kk = 0; kk < kMaxTopK; kk++)
+            if (kk == k) sel[kk] = bi;
+    }
+    if (lane == 0) {
+        float tot = 0.f;
+        for (int k = 0; k < K; k++) tot += ev[sel[k]];
+        if (a.scoring != 0) tot += 1e-20f;
+        for (int k = 0; k < K; k++) {
+            a.idx[(size_t)t * K + k] = sel[k];
+            a.w[(size_t)t * K + k] = __fdiv_rn(ev[sel[k]], tot);
+        }
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(256) route_topk_kernel(RouteArgs a) {
+    __shared__ float ev[8][kMaxExperts];
+    const int warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * 8 + warp;
+    if (t < a.T) route_token_warp(a, t, ev[warp]);
+}
+
+// Counting-sort permutation of the routed pairs; one 1024-thread block.  Shared use:
+// counts/firstpos/jrank [E] ints, plus 8-bit copies of idx [T*K].
+__device__ void permute_block(const RouteArgs& a, unsigned char* idx8) {
+    __shared__ int counts[kMaxExperts];
+    __shared__ int firstpos[kMaxExperts];
+    __shared__ int offs[kMaxExperts + 1];
+    __shared__ int jrank[kMaxExperts];
+    __shared__ int lrank[kMaxExperts];
+    const int E = a.E, K = a.K, T = a.T, NP = T * K;
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const int lane = tid & 31, warp = tid >> 5, nwarps = nth >> 5;
+    for (int e = tid; e < E; e += nth) {
+        counts[e] = 0;
+        firstpos[e] = 0x7fffffff;
+    }
+    __syncthreads();
+    for (int q = tid; q < NP; q += nth) {
+        int e = a.idx[q];
+        if (e < 0 || e >= E) {  // only reachable through a corrupted idx buffer
+            atomicOr(a.err, kErrBadIndex);
+            e = 0;
+        }
+        idx8[q] = (unsigned char)e;
+        atomicAdd(&counts[e], 1);
+        atomicMin(&firstpos[e], q);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int e = 0; e < E; e++) {
+            offs[e] = acc;
+            acc += counts[e];
+        }
+        offs[E] = acc;
+    }
+    // job rank = rank of the first appearance among active experts (runtime.py:343-354)
+    for (int e = tid; e < E; e += nth) {
+        int r = -1, lr = -1;
+        if (counts[e] > 0) {
+            r = 0;
+            lr = 0;
+            for (int e2 = 0; e2 < E; e2++)
+                if (counts[e2] > 0 && firstpos[e2] < firstpos[e]) {
+                    r++;
+                    if (a.desc == nullptr || a.desc[e2].kind != kKindRemote) lr++;
+                }
+        }
+        jrank[e] = r;
+        lrank[e] = lr;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int nj = 0, nl = 0;
+        for (int e = 0; e < E; e++)
+            if (counts[e] > 0) {
+                nj++;
+                if (a.desc == nullptr || a.desc[e].kind != kKindRemote) nl++;
+            }
+        if (a.n_jobs) *a.n_jobs = nj;
+        if (a.n_ljobs) *a.n_ljobs = nl;
+    }
+    for (int e = tid; e < E; e += nth) {
+        if (a.counts) a.counts[e] = counts[e];
+        if (a.offsets) a.offsets[e] = offs[e];
+        if (counts[e] > 0) {
+            if (a.job_order) a.job_order[jrank[e]] = e;
+            if (a.jobs && lrank[e] >= 0 && (a.desc == nullptr || a.desc[e].kind != kKindRemote)) {
+                Job jb;
+                if (a.desc) {
+                    jb.ex = a.desc[e];
+                    if (jb.ex.kind != kKindBF16 && jb.ex.kind != kKindQ8) atomicOr(a.err, kErrBadExpert);
+                } else {
+                    jb.ex = ExpDesc{nullptr, nullptr, nullptr, 0, 0};
+                }
+                jb.p0 = offs[e];
+                jb.n = jb.ex.kind == kKindBF16 || jb.ex.kind == kKindQ8 ? counts[e] : 0;
+                a.jobs[lrank[e]] = jb;
+            }
+        }
+    }
+    if (tid == 0 && a.offsets) a.offsets[E] = offs[E];
+    __syncthreads();
+    // stable placement: warp per expert, tokens ascending via ballot ranks
+    for (int e = warp; e < E; e += nwarps) {
+        if (counts[e] == 0) continue;
+        int base = offs[e];
+        for (int t0 = 0; t0 < T; t0 += 32) {
+            int t = t0 + lane;
+            int kk = -1;
+            if (t < T)
+                for (int k = 0; k < K; k++)
+                    if (idx8[t * K + k] == e) kk = k;
+            unsigned bal = __ballot_sync(0xffffffffu, kk >= 0);
+            if (kk >= 0) {
+                int pos = base + __popc(bal & ((1u << lane) - 1u));
+                int q = t * K + kk;
+                if (a.perm) a.perm[pos] = q;
+                if (a.ptok) a.ptok[pos] = t;
+                if (a.pw) a.pw[pos] = a.w[q];
+                if (a.pairpos) a.pairpos[q] = pos;
+            }
+            base += __popc(bal);
+        }
+    }
+    __syncthreads();
+    // per-token pair list in job order (the order the reference accumulates, cpu_moe.cpp:81-93);
+    // pairs of experts owned by another rank are marked -1
+    if (a.comb_p) {
+        for (int t = tid; t < T; t += nth) {
+            int rk[kMaxTopK], pp[kMaxTopK];
+            for (int k = 0; k < K; k++) {
+                int e = idx8[t * K + k];
+                rk[k] = jrank[e];
+                bool remote = a.desc != nullptr && a.desc[e].kind == kKindRemote;
+                pp[k] = remote ? -1 : a.pairpos[t * K + k];
+            }
+            for (int i = 1; i < K; i++) {  // insertion sort by job rank
+                int r = rk[i], p = pp[i], j = i - 1;
+                while (j >= 0 && rk[j] > r) {
+                    rk[j + 1] = rk[j];
+                    pp[j + 1] = pp[j];
+                    j--;
+                }
+                rk[j + 1] = r;
+                pp[j + 1] = p;
+            }
+            for (int k = 0; k < K; k++) a.comb_p[t * K + k] = pp[k];
+            a.comb_off[t] = t * K;
+            if (t == T - 1) a.comb_off[T] = T * K;
+        }
+        if (T == 0 && tid == 0) a.comb_off[0] = 0;
+    }
+}
+
+__global__ void __launch_bounds__(1024) permute_kernel(RouteArgs a) {
+    extern __shared__ unsigned char idx8[];
+    permute_block(a, idx8);
+}
+
+// Small batches: routing and permutation in one launch.
+__global__ void __launch_bounds__(1024) route_fused_kernel(RouteArgs a) {
+    extern __shared__ unsigned char dyn[];
+    float* ev = reinterpret_cast<float*>(dyn);  // [32][kMaxExperts]
+    unsigned char* idx8 = dyn + 32 * kMaxExperts * sizeof(float);
+    const int warp = threadIdx.x >> 5;
+    for (int t = warp; t < a.T; t += 32) route_token_warp(a, t, ev + warp * kMaxExperts);
+    __syncthreads();
+    permute_block(a, idx8);
+}
+
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
+    if (a.T <= 64) {
+        size_t sm = 32 * kMaxExperts * sizeof(float) + (size_t)a.T * a.K;
+        route_fused_kernel<<<1, 1024, sm, st>>>(a);
+        if (launches) *launches += 1;
+        return cudaGetLastError();
+    }
+    if (a.T > 0) route_topk_kernel<<<(a.T + 7) / 8, 256, 0, st>>>(a);
+    size_t sm = (size_t)a.T * a.K;
+    permute_kernel<<<1, 1024, sm, st>>>(a);
+    if (launches) *launches += a.T > 0 ? 2 : 1;
+    return cudaGetLastError();
+}
+
+cudaError_t route_set_smem_limits() {
+    cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kMaxTokens * kMaxTopK);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                32 * kMaxExperts * sizeof(float) + 64 * kMaxTopK);
+}
+
+}  // namespace moe

@@ -1,0 +1,333 @@
+"""Host-side API of the B200 routed-expert MoE data plane (a thin layer over the C ABI).
+
+* ``MoEDataPlane`` -- one context per GPU: expert tables resident in HBM, and the per-layer hot path
+  ``forward(layer, hidden, logits) -> out`` (the surface of the reference engine's
+  ``Model::moe_phase``, track2_opt/solar_engine/src/main.rs:149-209, and of ``Runtime._moe``,
+  solar_hybrid/runtime.py:338-423).
+* ``gpu_moe`` / ``set_threads`` -- drop-in replacements for ``cpu_moe_ext.cpu_moe`` /
+  ``cpu_moe_ext.set_threads`` (solar_hybrid/cpu_moe.cpp:38-105): same arguments, same result
+  layout, same error on H or F not a multiple of 32.
+
+PyTorch only provides device memory and streams here; every computation runs in libmoe_dp.so.
+"""
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (MOE_F_ACCUMULATE, MOE_F_HOST, MOE_F_SYNC, MOE_SCORING_SIGMOID, MOE_SCORING_SOFTMAX, MoeConfig,
+                   check, lib)
+
+__all__ = ["MoEDataPlane", "gpu_moe", "set_threads", "as_bf16"]
+
+
+def _vp(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def as_bf16(a, device=None):
+    """numpy uint16 (bf16 bits) or torch bf16 -> contiguous torch bf16 tensor (optionally moved)."""
+    if isinstance(a, np.ndarray):
+        assert a.dtype == np.uint16, a.dtype
+        t = torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+    else:
+        t = a
+        if t.dtype == torch.int16 or t.dtype == torch.uint16:
+            t = t.view(torch.bfloat16)
+        assert t.dtype == torch.bfloat16, t.dtype
+    if device is not None:
+        t = t.to(device, non_blocking=False)
+    return t.contiguous()
+
+
+def _as(a, dtype, device=None):
+    t = torch.as_tensor(a) if not isinstance(a, torch.Tensor) else a
+    t = t.to(dtype)
+    if device is not None:
+        t = t.to(device)
+    return t.contiguous()
+
+
+def _stream_ptr(stream, device):
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+class MoEDataPlane:
+    """Expert tables + routed-expert forward for ``n_layers`` MoE layers on one GPU.
+
+    Expert-parallel use: pass ``ep_rank`` / ``ep_world`` (and optionally a ``shard_map`` of shape
+    [n_layers, n_experts] giving each expert's owner rank); ``forward`` then returns this rank's
+    partial sum over its local experts, which npu_offload_b200.parallel combines across ranks.
+    """
+
+    def __init__(self, hidden, inter, n_experts, top_k=8, n_layers=1, max_tokens=64, scoring="softmax", device=0,
+                 ep_rank=0, ep_world=1, shard_map=None):
+        self.H, self.F, self.E, self.K, self.L = int(hidden), int(inter), int(n_experts), int(top_k), int(n_layers)
+        self.max_tokens = int(max_tokens)
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.scoring = scoring
+        sc = {"softmax": MOE_SCORING_SOFTMAX, "sigmoid": MOE_SCORING_SIGMOID}[scoring]
+        self._shard = None
+        if shard_map is not None:
+            self._shard = np.ascontiguousarray(np.asarray(shard_map, dtype=np.int32).reshape(-1))
+        cfg = MoeConfig(self.H, self.F, self.E, self.K, self.L, self.max_tokens, sc, self.device.index or 0,
+                        int(ep_rank), int(ep_world),
+                        None if self._shard is None else self._shard.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+        self.ep_rank, self.ep_world = int(ep_rank), int(ep_world)
+        h = ctypes.c_void_p()
+        check(lib().moe_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self._h = h
+
+    # ---- lifetime ----
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def handle(self):
+        return self._h
+
+    def owner(self, layer, expert):
+        if self._shard is not None:
+            return int(self._shard[layer * self.E + expert])
+        return 0 if self.ep_world == 1 else expert % self.ep_world
+
+    # ---- expert tables ----
+    def load_expert(self, layer, expert, gate, up, down):
+        """gate/up [F,H], down [H,F] bf16 (torch, host or device, or numpy uint16 bits)."""
+        g, u, d = (as_bf16(a) for a in (gate, up, down))
+        assert g.shape == (self.F, self.H) and u.shape == (self.F, self.H) and d.shape == (self.H, self.F)
+        flags = 0 if g.is_cuda else MOE_F_HOST
+        if not g.is_cuda:
+            u, d = u.cpu(), d.cpu()
+        else:
+            u, d = u.to(g.device), d.to(g.device)
+        check(lib().moe_load_expert_bf16(self._h, layer, expert, _vp(g), _vp(u), _vp(d), flags))
+
+    def load_expert_q8(self, layer, expert, q, scales):
+        """q int8 [3*F*H] in the ck_place_expert_q8 layout, scales fp32 [2F+H]."""
+        qt = _as(q, torch.int8)
+        st = _as(scales, torch.float32, qt.device)
+        flags = 0 if qt.is_cuda else MOE_F_HOST
+        check(lib().moe_load_expert_q8(self._h, layer, expert, _vp(qt), _vp(st), flags))
+
+    def quantize_expert_q8(self, layer, expert):
+        check(lib().moe_quantize_expert_q8(self._h, layer, expert))
+
+    def expert_kind(self, layer, expert):
+        return lib().moe_expert_kind(self._h, layer, expert)
+
+    def set_bias(self, layer, bias):
+        if bias is None:
+            check(lib().moe_set_bias(self._h, layer, None, 0))
+            return
+        b = _as(bias, torch.float32)
+        check(lib().moe_set_bias(self._h, layer, _vp(b), 0 if b.is_cuda else MOE_F_HOST))
+
+    # ---- hot path ----
+    def forward(self, layer, hidden, logits, out=None, return_topk=False, accumulate=False, stream=None, sync=False):
+        """hidden [T,H] bf16, logits [T,E] fp32 (device tensors) -> out [T,H] fp32 on the device.
+
+        Asynchronous on ``stream`` (default: torch's current stream) unless ``sync``."""
+        x = as_bf16(hidden)
+        lg = _as(logits, torch.float32)
+        T = x.shape[0]
+        assert x.is_cuda and lg.is_cuda and x.shape[1] == self.H and lg.shape == (T, self.E)
+        if out is None:
+            out = torch.empty(T, self.H, dtype=torch.float32, device=x.device)
+        idx = w = None
+        if return_topk:
+            idx = torch.empty(T, self.K, dtype=torch.int32, device=x.device)
+            w = torch.empty(T, self.K, dtype=torch.float32, device=x.device)
+        flags = (MOE_F_ACCUMULATE if accumulate else 0) | (MOE_F_SYNC if sync else 0)
+        check(lib().moe_forward(self._h, layer, T, _vp(x), _vp(lg), _vp(out), _vp(idx), _vp(w), flags,
+                                _stream_ptr(stream, x.device)))
+        return (out, idx, w) if return_topk else out
+
+    def forward_host(self, layer, hidden, logits, out=None, return_topk=False):
+        """Host buffers in and out (numpy or CPU tensors; pinned ones are copied directly)."""
+        x = as_bf16(hidden)
+        lg = _as(logits, torch.float32)
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty(T, self.H, dtype=torch.float32)
+        idx = w = None
+        if return_topk:
+            idx = torch.empty(T, self.K, dtype=torch.int32)
+            w = torch.empty(T, self.K, dtype=torch.float32)
+        check(lib().moe_forward(self._h, layer, T, _vp(x), _vp(lg), _vp(out), _vp(idx), _vp(w), MOE_F_HOST,
+                                _stream_ptr(None, self.device)))
+        return (out, idx, w) if return_topk else out
+
+    def route(self, logits, bias=None, stream=None):
+        """Router + permutation on the GPU; returns a dict of host numpy arrays (synchronous)."""
+        lg = _as(logits, torch.float32, self.device)
+        T = lg.shape[0]
+        b = None if bias is None else _as(bias, torch.float32, self.device)
+        dev = self.device
+        r = dict(idx=torch.empty(T, self.K, dtype=torch.int32, device=dev),
+                 w=torch.empty(T, self.K, dtype=torch.float32, device=dev),
+                 counts=torch.empty(self.E, dtype=torch.int32, device=dev),
+                 offsets=torch.empty(self.E + 1, dtype=torch.int32, device=dev),
+                 perm=torch.empty(max(1, T * self.K), dtype=torch.int32, device=dev),
+                 job_order=torch.empty(self.E, dtype=torch.int32, device=dev),
+                 n_jobs=torch.empty(1, dtype=torch.int32, device=dev))
+        status = lib().moe_route(self._h, T, _vp(lg), _vp(b), _vp(r["idx"]), _vp(r["w"]), _vp(r["counts"]),
+                                 _vp(r["offsets"]), _vp(r["perm"]), _vp(r["job_order"]), _vp(r["n_jobs"]), MOE_F_SYNC,
+                                 _stream_ptr(stream, dev))
+        res = {k: v.cpu().numpy() for k, v in r.items()}
+        res["perm"] = res["perm"][:T * self.K]
+        res["job_order"] = res["job_order"][:int(res["n_jobs"][0])]
+        res["status"] = status
+        return res
+
+    # ---- reference CPU-kernel surfaces ----
+    def experts(self, x, gus, ds, toks, ws, out=None, accumulate=False, stream=None):
+        """cpu_moe surface with device-resident weights: out[T,H] fp32 (device)."""
+        xd = as_bf16(x, self.device)
+        T = xd.shape[0]
+        gus = [as_bf16(g, self.device) for g in gus]
+        ds = [as_bf16(d, self.device) for d in ds]
+        n = len(gus)
+        off = np.zeros(n + 1, np.int64)
+        for j, t in enumerate(toks):
+            off[j + 1] = off[j] + len(t)
+        tk = np.ascontiguousarray(np.concatenate([np.asarray(_cpu(t), np.int64) for t in toks]) if n else np.zeros(1, np.int64))
+        wv = np.ascontiguousarray(np.concatenate([np.asarray(_cpu(w), np.float32) for w in ws]) if n else np.zeros(1, np.float32))
+        gp = (ctypes.c_void_p * max(1, n))(*[g.data_ptr() for g in gus])
+        dp = (ctypes.c_void_p * max(1, n))(*[d.data_ptr() for d in ds])
+        if out is None:
+            out = torch.empty(T, self.H, dtype=torch.float32, device=self.device)
+        flags = MOE_F_ACCUMULATE if accumulate else 0
+        check(lib().moe_experts(self._h, T, _vp(xd), n, gp, dp, off.ctypes.data_as(ctypes.c_void_p),
+                                tk.ctypes.data_as(ctypes.c_void_p), wv.ctypes.data_as(ctypes.c_void_p), _vp(out),
+                                flags, _stream_ptr(stream, self.device)))
+        self._keep = (gus, ds)
+        return out
+
+    def ck_moe3(self, bases, w, x, out, stream=None):
+        """ck_moe3: out[H] += sum_e w[e] * expert_e(x); bases = device bf16 tensors [3*F*H]."""
+        n = len(bases)
+        bp = (ctypes.c_void_p * max(1, n))(*[b.data_ptr() for b in bases])
+        wd = _as(w, torch.float32, self.device)
+        xd = as_bf16(x, self.device)
+        check(lib().moe_ck_moe3(self._h, n, bp, _vp(wd), _vp(xd), _vp(out), 0, _stream_ptr(stream, self.device)))
+        return out
+
+    def ck_moe_q8w(self, qs, scs, w, x, out, stream=None):
+        n = len(qs)
+        qp = (ctypes.c_void_p * max(1, n))(*[q.data_ptr() for q in qs])
+        sp = (ctypes.c_void_p * max(1, n))(*[s.data_ptr() for s in scs])
+        wd = _as(w, torch.float32, self.device)
+        xd = as_bf16(x, self.device)
+        check(lib().moe_ck_moe_q8w(self._h, n, qp, sp, _vp(wd), _vp(xd), _vp(out), 0, _stream_ptr(stream, self.device)))
+        return out
+
+    def place_expert_q8(self, g, u, d, stream=None):
+        """ck_place_expert_q8 on the GPU -> (q int8 [3FH], sc fp32 [2F+H], rs int32 [2F+H]) device tensors."""
+        g, u, d = (as_bf16(a, self.device) for a in (g, u, d))
+        q = torch.empty(3 * self.F * self.H, dtype=torch.int8, device=self.device)
+        sc = torch.empty(2 * self.F + self.H, dtype=torch.float32, device=self.device)
+        rs = torch.empty(2 * self.F + self.H, dtype=torch.int32, device=self.device)
+        check(lib().moe_place_expert_q8(self._h, _vp(g), _vp(u), _vp(d), _vp(q), _vp(sc), _vp(rs), MOE_F_SYNC,
+                                        _stream_ptr(stream, self.device)))
+        return q, sc, rs
+
+    def status(self, stream=None):
+        return lib().moe_status(self._h, _stream_ptr(stream, self.device))
+
+    @property
+    def launch_count(self):
+        return int(lib().moe_launch_count(self._h))
+
+    def profile(self, enable=True):
+        check(lib().moe_profile(self._h, int(bool(enable))))
+
+    def profile_read(self, n_stages=4):
+        """Summed ms per stage (route, gate/up, down, combine) of the profiled forwards, and their count."""
+        ms = (ctypes.c_double * n_stages)()
+        n = ctypes.c_int64()
+        check(lib().moe_profile_read(self._h, ms, n_stages, ctypes.byref(n)))
+        return list(ms), int(n.value)
+
+
+def _cpu(t):
+    return t.cpu() if isinstance(t, torch.Tensor) else t
+
+
+# ---------------- cpu_moe_ext drop-in ----------------
+_planes = {}
+_wcache = {}
+
+
+def _plane_for(device, H, F, pairs, T):
+    key = (device.index, H, F)
+    p = _planes.get(key)
+    if p is None or p.max_tokens * p.K < pairs or p.max_tokens < T:
+        if p is not None:
+            p.close()
+        mt = 64
+        while mt * 16 < pairs or mt < T:
+            mt *= 2
+        # scratch capacity is max_tokens * top_k pairs (top_k=16 needs n_experts >= 16)
+        p = MoEDataPlane(H, F, n_experts=16, top_k=16, n_layers=1, max_tokens=min(mt, 4096), device=device)
+        _planes[key] = p
+    return p
+
+
+def _device_weight(t, device):
+    if t.is_cuda:
+        return as_bf16(t)
+    key = (t.data_ptr(), t.numel(), str(device))
+    d = _wcache.get(key)
+    if d is None:
+        d = as_bf16(t, device)
+        _wcache[key] = d
+    return d
+
+
+def gpu_moe(x, gus, ds, toks, ws):
+    """Drop-in for ``cpu_moe_ext.ext.cpu_moe`` (solar_hybrid/cpu_moe.cpp:38-96).
+
+    x [T,H] bf16; gus[e] [2F,H] bf16 (gate rows then up rows); ds[e] [H,F] bf16; toks[e] int64 token
+    rows; ws[e] fp32 routing weights.  Returns out [T,H] fp32 = sum_e ws[e] * expert_e(x[toks[e]]),
+    on x's device (a CPU x gives a CPU result, as the reference does).  CPU weight tensors are copied
+    to the GPU once and cached by storage address; pass CUDA tensors to avoid the cache.
+    """
+    T, H = x.shape
+    E = len(gus)
+    if E == 0:
+        return torch.zeros(T, H, dtype=torch.float32, device=x.device)
+    F = ds[0].shape[1]
+    if H % 32 != 0 or F % 32 != 0:
+        raise RuntimeError("H,F must be multiples of 32")
+    if H % 256 != 0 or F % 64 != 0:
+        raise RuntimeError("gpu_moe needs H % 256 == 0 and F % 64 == 0")
+    device = x.device if x.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    pairs = sum(len(t) for t in toks)
+    plane = _plane_for(device, H, F, pairs, T)
+    g = [_device_weight(a, device) for a in gus]
+    d = [_device_weight(a, device) for a in ds]
+    out = plane.experts(x, g, d, toks, ws)
+    return out if x.is_cuda else out.cpu()
+
+
+def set_threads(n):
+    """Accepted for compatibility with cpu_moe_ext.set_threads; the GPU path has no host thread pool."""
+    return None

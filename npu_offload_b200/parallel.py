@@ -1,0 +1,46 @@
+"""Expert parallelism across the GPUs of one box (one process per GPU, torch.distributed).
+
+The shard map is npu-offload's placement plan turned into ownership: experts are ranked by
+popularity (profile counts, moe_offload/placement.py:15-16 ``ranks``) and dealt round-robin to the
+ranks (the alternating assignment of solar_hybrid/runtime.py:522-533), so every rank gets a
+balanced mix of hot and cold experts.  ``top`` (contiguous rank blocks, placement.py:22-24) is
+available for comparison.
+
+Per layer every rank routes the same tokens (identical inputs give bit-identical top-k on every
+rank), runs its local experts and produces a partial [T,H] fp32 sum; one exchange (an NCCL
+all-reduce of the partials) completes the combine.
+"""
+import numpy as np
+
+
+def ranks_by_count(counts):
+    """Experts ordered hottest first; ties to the lower id (moe_offload/placement.py:15-16)."""
+    counts = np.asarray(counts)
+    return sorted(range(len(counts)), key=lambda e: (-counts[e], e))
+
+
+def shard_map(counts_per_layer, world, policy="stripe"):
+    """[layers][E] owner rank for each expert.
+
+    stripe: popularity rank r goes to rank r % world (balanced hot/cold mix per rank).
+    top:    ranks take contiguous popularity blocks of E/world experts (placement.py "top")."""
+    counts_per_layer = np.asarray(counts_per_layer)
+    L, E = counts_per_layer.shape
+    out = np.zeros((L, E), np.int32)
+    per = -(-E // world)
+    for l in range(L):
+        order = ranks_by_count(counts_per_layer[l])
+        for r, e in enumerate(order):
+            out[l, e] = r % world if policy == "stripe" else min(r // per, world - 1)
+    return out
+
+
+def local_experts(smap, layer, rank):
+    return [int(e) for e in np.nonzero(np.asarray(smap)[layer] == rank)[0]]
+
+
+def allreduce_partial(out, group=None):
+    """Sum the per-rank partial outputs in place (NCCL over NVLink when the group is NCCL)."""
+    import torch.distributed as dist
+    dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
+    return out
