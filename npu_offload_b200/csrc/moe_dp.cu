@@ -432,6 +432,8 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
     if (layer < 0 || layer >= c->cfg.n_layers) return fail(MOE_EINVAL, "layer %d out of range [0,%d)", layer, c->cfg.n_layers);
     if (T < 0 || T > c->cfg.max_tokens) return fail(MOE_EINVAL, "T=%d not in [0,%d]", T, c->cfg.max_tokens);
     if (T > 0 && (!hidden || !logits || !out)) return fail(MOE_EINVAL, "null hidden/logits/out");
+    if (!(flags & MOE_F_HOST) && (((uintptr_t)hidden | (uintptr_t)logits | (uintptr_t)out) & 15u))
+        return fail(MOE_EINVAL, "hidden/logits/out must be 16-byte aligned");
     DeviceGuard dg(c->dev);
     cudaStream_t st = (cudaStream_t)stream;
     const bool host = flags & MOE_F_HOST;
@@ -569,6 +571,12 @@ static int run_jobs(moe_ctx* c, int T, const uint16_t* x, const std::vector<Job>
                     const std::vector<int32_t>& comb_p, float* out, int flags, cudaStream_t st) {
     const int H = c->cfg.hidden;
     const size_t NP = ptok.size();
+    if (jobs.size() > (size_t)c->cfg.n_experts)
+        return fail(MOE_EINVAL, "%zu expert jobs exceed the context capacity n_experts=%d", jobs.size(), c->cfg.n_experts);
+    for (const Job& j : jobs)
+        if (((uintptr_t)j.ex.w1 | (uintptr_t)j.ex.w2 | (uintptr_t)j.ex.sc) & 15u)
+            return fail(MOE_EINVAL, "expert weight pointers must be 16-byte aligned");
+    if (((uintptr_t)x | (uintptr_t)out) & 15u) return fail(MOE_EINVAL, "x/out must be 16-byte aligned");
     if (NP > (size_t)c->cfg.max_tokens * c->cfg.top_k)
         return fail(MOE_EINVAL, "%zu routed pairs exceed the context capacity %d (max_tokens * top_k)", NP,
                     c->cfg.max_tokens * c->cfg.top_k);

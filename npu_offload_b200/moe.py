@@ -276,17 +276,22 @@ _planes = {}
 _wcache = {}
 
 
-def _plane_for(device, H, F, pairs, T):
+def _plane_for(device, H, F, pairs, T, n_jobs):
     key = (device.index, H, F)
     p = _planes.get(key)
-    if p is None or p.max_tokens * p.K < pairs or p.max_tokens < T:
+    if p is None or p.max_tokens * p.K < pairs or p.max_tokens < T or p.E < n_jobs:
         if p is not None:
             p.close()
         mt = 64
         while mt * 16 < pairs or mt < T:
             mt *= 2
         # scratch capacity is max_tokens * top_k pairs (top_k=16 needs n_experts >= 16)
-        p = MoEDataPlane(H, F, n_experts=16, top_k=16, n_layers=1, max_tokens=min(mt, 4096), device=device)
+        ne = 16
+        while ne < n_jobs:
+            ne *= 2
+        if ne > 256:
+            raise RuntimeError("gpu_moe supports at most 256 experts per call")
+        p = MoEDataPlane(H, F, n_experts=ne, top_k=16, n_layers=1, max_tokens=min(mt, 4096), device=device)
         _planes[key] = p
     return p
 
@@ -321,7 +326,7 @@ def gpu_moe(x, gus, ds, toks, ws):
         raise RuntimeError("gpu_moe needs H % 256 == 0 and F % 64 == 0")
     device = x.device if x.is_cuda else torch.device("cuda", torch.cuda.current_device())
     pairs = sum(len(t) for t in toks)
-    plane = _plane_for(device, H, F, pairs, T)
+    plane = _plane_for(device, H, F, pairs, T, E)
     g = [_device_weight(a, device) for a in gus]
     d = [_device_weight(a, device) for a in ds]
     out = plane.experts(x, g, d, toks, ws)
