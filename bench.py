@@ -459,6 +459,7 @@ def our_arm(args):
         ev, h2d, d2h = e2e_run(stack, max(1, args.steps // 4), min(args.warmup, 3), ws)
         e2e = {"value": ev, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
+    ucount_main, ubytes_main = stack.ucount.copy(), stack.ubytes.copy()
     sweep = []
     for tb in [int(v) for v in args.sweep.split(",") if v.strip()]:
         if tb == T:
@@ -502,8 +503,8 @@ def our_arm(args):
                            "weights_gb": round(L * E * EXPERT_BYTES / 1e9, 1),
                            "parallelism": f"ep{ws}" if ws > 1 else "single",
                            "l2": "no flush: each step streams its routed experts (~%.1f GB/step/GPU) >> 126 MB L2"
-                                 % (stack.ubytes.mean() * L / 1e9),
-                           "experts_per_layer": float(stack.ucount.mean())},
+                                 % (ubytes_main.mean() * L / 1e9),
+                           "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
                 "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep}
         print(json.dumps(line), flush=True)

@@ -169,6 +169,22 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 MOE_API int moe_profile(moe_ctx* ctx, int enable);
 MOE_API int moe_profile_read(moe_ctx* ctx, double* stage_ms, int n_stages, int64_t* n_calls);
 
+/* ck_moe3 without any allocation, for callers that may not call cudaMalloc (for example a server
+ * whose own allocator already owns all of HBM, or code running where an allocation could block or
+ * fail): it needs no moe_ctx (whose creation allocates) and allocates nothing, neither device nor
+ * pinned host memory.  No counterpart in the reference: it is the ck_moe3 surface above
+ * (out [H] += sum_e w[e] * expert_e(x), base[e] in the [g F*H][u F*H][d H*F] layout; base is a host
+ * array of device pointers, w / x / out are device pointers) with its working memory held in a
+ * 1 MiB file-scope device array inside libmoe_dp.so, which every GPU that loads the library keeps
+ * until the process exits.  Limits: E <= 16 and E * (2F + 4H) bytes plus tables within the 1 MiB
+ * (H = 4096, F = 1280 fits 16 experts); larger calls return MOE_EINVAL.  Runs on the calling
+ * thread's current device, asynchronously on `stream`.  All calls on a device share that array:
+ * calls that overlap on the GPU race, so keep them on one stream or synchronise between them.  The
+ * first call on each device looks the array's address up (cudaGetSymbolAddress) and should be made
+ * before any stream capture. */
+MOE_API int moe_ck_moe3_noalloc(int E, const uint16_t* const* base, const float* w, const uint16_t* x, float* out,
+                                int H, int F, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,7 @@ _SIGS = {
     "moe_place_expert_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
     "moe_status": (_i, [_vp, _vp]),
     "moe_launch_count": (ctypes.c_int64, [_vp]),
+    "moe_ck_moe3_noalloc": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _vp]),
     "moe_profile": (_i, [_vp, _i]),
     "moe_profile_read": (_i, [_vp, ctypes.POINTER(ctypes.c_double), _i, ctypes.POINTER(ctypes.c_int64)]),
 }

@@ -81,6 +81,11 @@ struct Staging {
 
 }  // namespace
 
+namespace moe {
+// Error reporting for entry points defined in other translation units of the library.
+int internal_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace moe
+
 struct moe_ctx {
     moe_config cfg{};
     int dev = 0;

@@ -143,7 +143,8 @@ def test_solar_golden_cpu_moe_surface(golden):
             out = p.experts(g[f"T{T}_x"], gus, ds, toks, ws)
             assert_close(out.cpu().numpy(), g[f"T{T}_out"], what=f"cpu_moe surface T={T}")
             if T == 1:
-                bases = [torch.from_numpy(np.concatenate([a, b, c]).reshape(-1).view(np.int16)).cuda() for a, b, c in Wn]
+                bases = [torch.from_numpy(np.concatenate([a.ravel(), b.ravel(), c.ravel()]).view(np.int16)).cuda()
+                         for a, b, c in Wn]
                 acc = torch.full((H,), 0.5, device="cuda")
                 p.ck_moe3(bases, g["ck_moe3_w"], g["T1_x"][0], acc)
                 torch.cuda.synchronize()
