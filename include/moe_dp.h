@@ -162,10 +162,37 @@ MOE_API int moe_status(moe_ctx* ctx, void* stream);
 /* Number of kernels this context has launched since creation (instrumentation for benchmarks). */
 MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 
+/* Context options (moe_set_option):
+ *   MOE_OPT_FUSED_DECODE        1 (default): batches of T <= 16 run as one fused persistent kernel
+ *                               (routing + expert GEMV + combine); 0: the multi-kernel path.
+ *   MOE_OPT_WAIT_TIMEOUT_US     bound on every device-side wait of the fused kernel (default 1 s);
+ *                               a wait that runs out makes the call report MOE_ETIMEOUT.
+ *   MOE_OPT_INJECT_WAIT_TIMEOUT test hook: 1 makes the fused kernel wait for a readiness count that
+ *                               is never published, so the bounded-wait error path can be tested
+ *                               without faulting or hanging the GPU.
+ *   MOE_OPT_RING_STAGES         tuning: cap on the fused kernel's shared-memory ring depth (4..16;
+ *                               0 = as deep as shared memory allows, the default).
+ *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
+ *                               globaltimer stamps (0 start, 1 prologue done, 2 gate/up stages
+ *                               issued, 3 all stages issued, 4 activations staged, 5 first warp done
+ *                               with gate/up, 6 down consumed, 7 end, 8 routed, 9 grouped, 10 job
+ *                               list, 11 partition, 12 all jobs published, 13 all warps done with
+ *                               gate/up); read them with moe_timeline_read. */
+#define MOE_OPT_FUSED_DECODE 1
+#define MOE_OPT_WAIT_TIMEOUT_US 2
+#define MOE_OPT_INJECT_WAIT_TIMEOUT 3
+#define MOE_OPT_TIMELINE 4
+#define MOE_OPT_RING_STAGES 5
+MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
+
+/* Copies up to cap stamps ([SM count][16], see MOE_OPT_TIMELINE) to host memory (synchronises). */
+MOE_API int moe_timeline_read(moe_ctx* ctx, uint64_t* out, int cap);
+
 /* Stage timing of moe_forward with CUDA events on the caller's stream (instrumentation; off by
  * default).  moe_profile(ctx, 1) starts a fresh record; moe_profile_read synchronises and returns
  * the summed milliseconds per stage (0 router+permutation, 1 gate/up+SwiGLU kernel, 2 down kernel,
- * 3 combine kernel) over the calls made since, and the number of calls; it then clears the record. */
+ * 3 combine kernel; with the fused decode kernel everything is stage 1) over the calls made since,
+ * and the number of calls; it then clears the record. */
 MOE_API int moe_profile(moe_ctx* ctx, int enable);
 MOE_API int moe_profile_read(moe_ctx* ctx, double* stage_ms, int n_stages, int64_t* n_calls);
 

@@ -21,16 +21,32 @@ constexpr int kKindBF16 = 1;
 constexpr int kKindQ8 = 2;
 constexpr int kKindRemote = 3;
 
+// Gate/up row layouts of ExpDesc::w1.
+//   kLayoutSplit:       [F gate rows][F up rows] (the reference's [Wg; Wu], cpu_moe.cpp:4)
+//   kLayoutInterleaved: [F][gate row | up row]   (expert tables held by a context: one
+//                       contiguous 2-row unit per f, streamed with a single bulk copy)
+constexpr int kLayoutSplit = 0;
+constexpr int kLayoutInterleaved = 1;
+
 // Per (layer, expert) storage descriptor, resident in HBM.
-//   kind 1 (bf16): w1 = [2F,H] gate rows then up rows, w2 = [H,F] down, sc = null
-//   kind 2 (int8): w1 = [2F,H] int8, w2 = [H,F] int8, sc = [2F+H] fp32 row scales
+//   kind 1 (bf16): w1 = 2F rows of H (layout above), w2 = [H,F] down, sc = null
+//   kind 2 (int8): w1 = 2F rows of H int8, w2 = [H,F] int8, sc = [2F+H] fp32 row scales
+//                  (scale f: gate row f, F+f: up row f, 2F+h: down row h)
 struct ExpDesc {
     const void* w1;
     const void* w2;
     const float* sc;
     int32_t kind;
-    int32_t pad;
+    int32_t layout;
 };
+
+// Element offsets of gate row f and up row f inside w1.
+__host__ __device__ __forceinline__ size_t gate_row(const ExpDesc& d, int f, int H, int F) {
+    return d.layout == kLayoutInterleaved ? (size_t)f * 2 * H : (size_t)f * H;
+}
+__host__ __device__ __forceinline__ size_t up_row(const ExpDesc& d, int f, int H, int F) {
+    return d.layout == kLayoutInterleaved ? (size_t)f * 2 * H + H : (size_t)(F + f) * H;
+}
 
 // One expert job of a forward call: which weights, which pairs.
 //   pairs [p0, p0+n) of the expert-major pair list; pair p -> token tok[p], weight wt[p]

@@ -44,8 +44,8 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
 #pragma unroll
             for (int i = 0; i < kTB; i++) ag[i] = au[i] = 0.f;
             if (jb.ex.kind == kKindBF16) {
-                const uint16_t* rg = (const uint16_t*)jb.ex.w1 + (size_t)f * H;
-                const uint16_t* ru = rg + (size_t)F * H;
+                const uint16_t* rg = (const uint16_t*)jb.ex.w1 + gate_row(jb.ex, f, H, F);
+                const uint16_t* ru = (const uint16_t*)jb.ex.w1 + up_row(jb.ex, f, H, F);
                 for (int c = lane * 8; c < H; c += 1024) {
                     uint4 wg[4], wu[4];
 #pragma unroll
@@ -68,8 +68,8 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(ExpertArgs a) {
                     }
                 }
             } else {
-                const int8_t* qg = (const int8_t*)jb.ex.w1 + (size_t)f * H;
-                const int8_t* qu = qg + (size_t)F * H;
+                const int8_t* qg = (const int8_t*)jb.ex.w1 + gate_row(jb.ex, f, H, F);
+                const int8_t* qu = (const int8_t*)jb.ex.w1 + up_row(jb.ex, f, H, F);
                 for (int c = lane * 16; c < H; c += 1024) {
                     uint4 wg[2], wu[2];
 #pragma unroll
@@ -241,9 +241,13 @@ cudaError_t launch_experts(const ExpertArgs& a, int sm_count, cudaStream_t st, i
     return cudaGetLastError();
 }
 
-// quant_row (cpu_kern.c:218-224) per row: one warp per row.
-__global__ void __launch_bounds__(256) quantize_q8_kernel(const uint16_t* g, const uint16_t* u, const uint16_t* d, int H,
-                                                          int F, int8_t* q, float* sc, int32_t* rs) {
+// quant_row (cpu_kern.c:218-224) per row: one warp per row.  Input gate row f at g + f*gu_pitch,
+// up row f at u + f*gu_pitch, down row h at d + h*F; output gate row f at q + f*q_pitch, up row f at
+// q + f*q_pitch + q_up_off, down row h at q + q_down_off + h*F; scales / row sums in the reference's
+// row order (gate rows, up rows, down rows).
+__global__ void __launch_bounds__(256) quantize_q8_kernel(const uint16_t* g, const uint16_t* u, size_t gu_pitch,
+                                                          const uint16_t* d, int H, int F, int8_t* q, size_t q_pitch,
+                                                          size_t q_up_off, size_t q_down_off, float* sc, int32_t* rs) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int rows = 2 * F + H;
     if (warp >= rows) return;
@@ -251,12 +255,12 @@ __global__ void __launch_bounds__(256) quantize_q8_kernel(const uint16_t* g, con
     int8_t* dst;
     int n;
     if (warp < F) {
-        src = g + (size_t)warp * H; dst = q + (size_t)warp * H; n = H;
+        src = g + (size_t)warp * gu_pitch; dst = q + (size_t)warp * q_pitch; n = H;
     } else if (warp < 2 * F) {
-        src = u + (size_t)(warp - F) * H; dst = q + (size_t)warp * H; n = H;
+        src = u + (size_t)(warp - F) * gu_pitch; dst = q + (size_t)(warp - F) * q_pitch + q_up_off; n = H;
     } else {
         const int h = warp - 2 * F;
-        src = d + (size_t)h * F; dst = q + (size_t)2 * F * H + (size_t)h * F; n = F;
+        src = d + (size_t)h * F; dst = q + q_down_off + (size_t)h * F; n = F;
     }
     float m = 0.f;
     for (int i = lane; i < n; i += 32) m = fmaxf(m, fabsf(bf2f(src[i])));
@@ -280,9 +284,15 @@ __global__ void __launch_bounds__(256) quantize_q8_kernel(const uint16_t* g, con
 }
 
 cudaError_t launch_quantize_q8(const uint16_t* g, const uint16_t* u, const uint16_t* d, int H, int F, int8_t* q,
-                               float* sc, int32_t* rs, cudaStream_t st, int* launches) {
+                               float* sc, int32_t* rs, cudaStream_t st, int* launches, int interleaved) {
     const int rows = 2 * F + H;
-    quantize_q8_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(g, u, d, H, F, q, sc, rs);
+    const size_t FH = (size_t)F * H;
+    if (interleaved)
+        quantize_q8_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(g, u, 2 * (size_t)H, d, H, F, q, 2 * (size_t)H,
+                                                                    (size_t)H, 2 * FH, sc, rs);
+    else
+        quantize_q8_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(g, u, (size_t)H, d, H, F, q, (size_t)H, FH, 2 * FH,
+                                                                    sc, rs);
     *launches += 1;
     return cudaGetLastError();
 }

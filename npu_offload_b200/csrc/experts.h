@@ -28,7 +28,10 @@ struct ExpertArgs {
 cudaError_t launch_experts(const ExpertArgs& a, int sm_count, cudaStream_t st, int* launches, cudaEvent_t* marks);
 
 // ck_place_expert_q8 on the device: quant_row applied to the 2F gate/up rows and H down rows.
+// interleaved = 0: g/u are separate [F,H] arrays and q gets the reference layout
+// ([F gate][F up][H down] rows); 1: g/u are the rows of an interleaved [F][gate|up] table
+// (u = g + H) and q gets the same interleaved layout followed by the H down rows.
 cudaError_t launch_quantize_q8(const uint16_t* g, const uint16_t* u, const uint16_t* d, int H, int F, int8_t* q,
-                               float* sc, int32_t* rs, cudaStream_t st, int* launches);
+                               float* sc, int32_t* rs, cudaStream_t st, int* launches, int interleaved);
 
 }  // namespace moe

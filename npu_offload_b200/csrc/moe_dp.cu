@@ -10,6 +10,7 @@
 
 #include "../../include/moe_dp.h"
 #include "common.cuh"
+#include "decode.h"
 #include "experts.h"
 #include "route.h"
 
@@ -116,6 +117,16 @@ struct moe_ctx {
     Staging in_stage, out_stage, job_stage;
     int64_t launches = 0;
     uint32_t latched = 0;
+    // fused decode kernel state
+    uint32_t* d_ctr = nullptr;  // [2 * kDecodeMaxPairs] readiness counters
+    DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
+    uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
+    uint32_t epoch = 0;
+    bool fused = true;
+    uint64_t timeout_ns = 1000000000ull;
+    int inject_timeout = 0;
+    uint64_t* d_timeline = nullptr;  // [sm_count][kTimelineSlots] when MOE_OPT_TIMELINE is on
+    int ns_cap = 0;
     // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_ev;  // kProfMarks events per profiled call
@@ -285,6 +296,12 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
+    if (!st) st = dalloc(&c->d_ctr, 2 * (size_t)kDecodeMaxPairs);
+    if (!st) st = dalloc(&c->d_plan, 2);
+    if (!st) st = dalloc(&c->d_plan_flag, 2);
+    if (!st && cudaMemset(c->d_plan_flag, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
+    if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 2 * kDecodeMaxPairs) != cudaSuccess)
+        st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && (cudaEventCreateWithFlags(&c->in_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&c->out_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
@@ -294,6 +311,14 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
         st = fail(MOE_ECUDA, "descriptor upload failed");
     if (!st && cudaMemset(c->d_err, 0, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMemset(c->d_bias, 0, sizeof(float) * (size_t)L * E) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
+    if (!st) {
+        cudaError_t e = plan_set_smem_limit();
+        if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
+    }
+    if (!st) {
+        cudaError_t e = decode_set_smem_limit();
+        if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
+    }
     if (!st) {
         cudaError_t e = route_set_smem_limits();
         if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
@@ -311,9 +336,11 @@ int moe_destroy(moe_ctx* c) {
     DeviceGuard dg(c->dev);
     cudaDeviceSynchronize();
     for (void* p : c->arena) cudaFree(p);
+    if (c->d_timeline) cudaFree(c->d_timeline);
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
                   c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
-                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out};
+                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
+                  c->d_plan_flag};
     for (void* p : ps) cudaFree(p);
     if (c->h_err) cudaFreeHost(c->h_err);
     for (cudaEvent_t ev : c->prof_ev) cudaEventDestroy(ev);
@@ -332,14 +359,15 @@ int moe_load_expert_bf16(moe_ctx* c, int layer, int expert, const uint16_t* gate
     if (!gate || !up || !down) return fail(MOE_EINVAL, "null weight pointer");
     DeviceGuard dg(c->dev);
     if ((st = ensure_arena(c, layer))) return st;
-    const size_t FH = (size_t)c->cfg.inter * c->cfg.hidden;
+    const size_t H = c->cfg.hidden, F = c->cfg.inter, FH = F * H;
     char* base = slot_ptr(c, layer, expert);
-    const bool host = flags & MOE_F_HOST;
-    if ((st = copy_in(base, gate, FH * 2, host, 0))) return st;
-    if ((st = copy_in(base + FH * 2, up, FH * 2, host, 0))) return st;
-    if ((st = copy_in(base + FH * 4, down, FH * 2, host, 0))) return st;
+    const cudaMemcpyKind kind = (flags & MOE_F_HOST) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    // stored interleaved: gate row f and up row f adjacent ([F][gate|up]), then the down rows
+    CUDA_TRY(cudaMemcpy2DAsync(base, 4 * H, gate, 2 * H, 2 * H, F, kind, 0));
+    CUDA_TRY(cudaMemcpy2DAsync(base + 2 * H, 4 * H, up, 2 * H, 2 * H, F, kind, 0));
+    if ((st = copy_in(base + FH * 4, down, FH * 2, (flags & MOE_F_HOST) != 0, 0))) return st;
     CUDA_TRY(cudaStreamSynchronize(0));
-    return upload_desc(c, layer, expert, ExpDesc{base, base + FH * 4, nullptr, kKindBF16, 0});
+    return upload_desc(c, layer, expert, ExpDesc{base, base + FH * 4, nullptr, kKindBF16, kLayoutInterleaved});
 }
 
 int moe_load_expert_q8(moe_ctx* c, int layer, int expert, const int8_t* q, const float* scales, int flags) {
@@ -351,11 +379,15 @@ int moe_load_expert_q8(moe_ctx* c, int layer, int expert, const int8_t* q, const
     const size_t H = c->cfg.hidden, F = c->cfg.inter;
     char* base = slot_ptr(c, layer, expert);
     const bool host = flags & MOE_F_HOST;
-    if ((st = copy_in(base, q, 3 * F * H, host, 0))) return st;
+    const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    // reference layout [F gate][F up][H down] rows -> interleaved [F][gate|up], then down rows
+    CUDA_TRY(cudaMemcpy2DAsync(base, 2 * H, q, H, H, F, kind, 0));
+    CUDA_TRY(cudaMemcpy2DAsync(base + H, 2 * H, q + F * H, H, H, F, kind, 0));
+    if ((st = copy_in(base + 2 * F * H, q + 2 * F * H, F * H, host, 0))) return st;
     if ((st = copy_in(base + q8_scale_off(c), scales, (2 * F + H) * 4, host, 0))) return st;
     CUDA_TRY(cudaStreamSynchronize(0));
     return upload_desc(c, layer, expert,
-                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, 0});
+                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutInterleaved});
 }
 
 int moe_quantize_expert_q8(moe_ctx* c, int layer, int expert) {
@@ -373,16 +405,16 @@ int moe_quantize_expert_q8(moe_ctx* c, int layer, int expert) {
         return fail(MOE_ENOMEM, "quantisation scratch");
     }
     int n = 0;
-    cudaError_t e = launch_quantize_q8((const uint16_t*)base, (const uint16_t*)(base + F * H * 2),
-                                       (const uint16_t*)(base + F * H * 4), (int)H, (int)F, (int8_t*)tmp,
-                                       (float*)(tmp + q8_scale_off(c)), nullptr, 0, &n);
+    // the bf16 table is interleaved; quantise into the same interleaved int8 layout
+    cudaError_t e = launch_quantize_q8((const uint16_t*)base, (const uint16_t*)base + H, (const uint16_t*)(base + F * H * 4),
+                                       (int)H, (int)F, (int8_t*)tmp, (float*)(tmp + q8_scale_off(c)), nullptr, 0, &n, 1);
     c->launches += n;
     if (e == cudaSuccess) e = cudaMemcpyAsync(base, tmp, bytes, cudaMemcpyDeviceToDevice, 0);
     if (e == cudaSuccess) e = cudaStreamSynchronize(0);
     cudaFree(tmp);
     if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise: %s", cudaGetErrorString(e));
     return upload_desc(c, layer, expert,
-                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, 0});
+                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutInterleaved});
 }
 
 int moe_expert_kind(moe_ctx* c, int layer, int expert) {
@@ -478,7 +510,65 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         c->prof_calls++;
         CUDA_TRY(cudaEventRecord(marks[0], st));
     }
-    if (T > 0) {
+    DecodeArgs da{};
+    size_t dsmem = 0;
+    bool use_fused = false;
+    const int dgrid = c->sm_count - 1;  // one SM stays free for the next call's plan kernel
+    if (T > 0 && c->fused && dgrid >= 1) {
+        da.x = x;
+        da.out = o;
+        da.act = c->d_act;
+        da.ctr = c->d_ctr;
+        da.err = c->d_err;
+        da.T = T;
+        da.E = E;
+        da.K = K;
+        da.H = H;
+        da.F = c->cfg.inter;
+        da.scoring = c->cfg.scoring;
+        da.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
+        da.timeout_ns = c->timeout_ns;
+        da.inject_timeout = c->inject_timeout;
+        da.timeline = c->d_timeline;
+        da.ns_cap = c->ns_cap;
+        use_fused = plan_decode(da, dgrid, &dsmem);
+    }
+    if (use_fused) {
+        const uint32_t epoch = c->epoch++;
+        PlanArgs pa{};
+        pa.logits = lg;
+        pa.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
+        pa.desc = c->d_desc + (size_t)layer * E;
+        pa.plan = c->d_plan + (epoch & 1);
+        pa.flag = c->d_plan_flag + (epoch & 1);
+        pa.stamp = epoch + 1;
+        pa.idx_out = c->d_idx;
+        pa.w_out = c->d_w;
+        pa.err = c->d_err;
+        pa.T = T;
+        pa.E = E;
+        pa.K = K;
+        pa.H = H;
+        pa.F = c->cfg.inter;
+        pa.scoring = c->cfg.scoring;
+        pa.G = dgrid;
+        pa.slot_bytes = da.slot_bytes;
+        pa.rs_bf16 = da.rs_bf16;
+        pa.rs_q8 = da.rs_q8;
+        cudaError_t e = launch_plan(pa, st);
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "plan launch: %s", cudaGetErrorString(e));
+        if (marks) cudaEventRecord(marks[1], st);
+        da.plan = pa.plan;
+        da.flag = pa.flag;
+        da.stamp = pa.stamp;
+        da.epoch = epoch;
+        e = launch_decode(da, dgrid, dsmem, st);
+        c->launches += 2;
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
+        if (marks)
+            for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
+    }
+    if (T > 0 && !use_fused) {
         RouteArgs ra = route_args(c, T, lg, c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr);
         ra.desc = c->d_desc + (size_t)layer * E;
         cudaError_t e = launch_route(ra, st, &n);
@@ -506,6 +596,8 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         e = launch_experts(ea, c->sm_count, st, &n, marks ? marks + 2 : nullptr);
         c->launches += n;
         if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
+    }
+    if (T > 0) {
         const cudaMemcpyKind dk = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
         if (topk_idx) CUDA_TRY(cudaMemcpyAsync(topk_idx, c->d_idx, sizeof(int32_t) * T * K, dk, st));
         if (topk_w) CUDA_TRY(cudaMemcpyAsync(topk_w, c->d_w, sizeof(float) * T * K, dk, st));
@@ -737,7 +829,7 @@ int moe_place_expert_q8(moe_ctx* c, const uint16_t* g, const uint16_t* u, const 
     const size_t H = c->cfg.hidden, F = c->cfg.inter, FH = F * H, R = 2 * F + H;
     int n = 0;
     if (!(flags & MOE_F_HOST)) {
-        cudaError_t e = launch_quantize_q8(g, u, d, (int)H, (int)F, q, sc, rs, st, &n);
+        cudaError_t e = launch_quantize_q8(g, u, d, (int)H, (int)F, q, sc, rs, st, &n, 0);
         c->launches += n;
         if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise launch: %s", cudaGetErrorString(e));
         if (flags & MOE_F_SYNC) return finish_sync(c, st);
@@ -756,7 +848,7 @@ int moe_place_expert_q8(moe_ctx* c, const uint16_t* g, const uint16_t* u, const 
     cudaError_t e = cudaMemcpyAsync(dg_, g, FH * 2, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(dg_ + FH, u, FH * 2, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(dg_ + 2 * FH, d, FH * 2, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = launch_quantize_q8(dg_, dg_ + FH, dg_ + 2 * FH, (int)H, (int)F, dq, dsc, drs, st, &n);
+    if (e == cudaSuccess) e = launch_quantize_q8(dg_, dg_ + FH, dg_ + 2 * FH, (int)H, (int)F, dq, dsc, drs, st, &n, 0);
     c->launches += n;
     if (e == cudaSuccess) e = cudaMemcpyAsync(q, dq, 3 * FH, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(sc, dsc, R * 4, cudaMemcpyDeviceToHost, st);
@@ -774,6 +866,51 @@ int moe_status(moe_ctx* c, void* stream) {
 }
 
 int64_t moe_launch_count(moe_ctx* c) { return c ? c->launches : -1; }
+
+int moe_set_option(moe_ctx* c, int option, int64_t value) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    switch (option) {
+        case MOE_OPT_FUSED_DECODE:
+            c->fused = value != 0;
+            return MOE_OK;
+        case MOE_OPT_WAIT_TIMEOUT_US:
+            if (value < 1000 || value > 60000000) return fail(MOE_EINVAL, "wait timeout %lld us not in [1e3, 6e7]", (long long)value);
+            c->timeout_ns = (uint64_t)value * 1000ull;
+            return MOE_OK;
+        case MOE_OPT_INJECT_WAIT_TIMEOUT:
+            c->inject_timeout = value != 0;
+            return MOE_OK;
+        case MOE_OPT_RING_STAGES:
+            if (value < 0 || value > 16) return fail(MOE_EINVAL, "ring stages %lld not in [0,16]", (long long)value);
+            c->ns_cap = (int)value;
+            return MOE_OK;
+        case MOE_OPT_TIMELINE: {
+            DeviceGuard dg(c->dev);
+            if (value && !c->d_timeline) {
+                int st = dalloc(&c->d_timeline, (size_t)c->sm_count * kTimelineSlots);
+                if (st) return st;
+                CUDA_TRY(cudaMemset(c->d_timeline, 0, sizeof(uint64_t) * c->sm_count * kTimelineSlots));
+            } else if (!value && c->d_timeline) {
+                cudaDeviceSynchronize();
+                cudaFree(c->d_timeline);
+                c->d_timeline = nullptr;
+            }
+            return MOE_OK;
+        }
+        default:
+            return fail(MOE_EINVAL, "unknown option %d", option);
+    }
+}
+
+int moe_timeline_read(moe_ctx* c, uint64_t* out, int cap) {
+    if (!c || !out) return fail(MOE_EINVAL, "bad argument");
+    if (!c->d_timeline) return fail(MOE_ESTATE, "timeline recording is off (MOE_OPT_TIMELINE)");
+    DeviceGuard dg(c->dev);
+    const int n = std::min(cap, c->sm_count * kTimelineSlots);
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(out, c->d_timeline, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
+    return MOE_OK;
+}
 
 int moe_profile(moe_ctx* c, int enable) {
     if (!c) return fail(MOE_EINVAL, "null context");

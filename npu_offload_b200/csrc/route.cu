@@ -1,139 +1,26 @@
-// Router (fused softmax or sigmoid+bias / top-k / renormalise) and the deterministic token->expert
-// permutation for the B200 MoE data plane.
-//
-// Router semantics: npu-kernels/npu_kernels/rngd/layer_template/src/host.rs.tpl:247-268 (softmax)
-// and track2_opt/solar_engine/src/host.rs:119-128 (sigmoid + correction bias):
-//   softmax: m = max v; e_i = exp(v_i - m); z = sum_i e_i in index order; p_i = e_i / z;
-//            top-k by p, ties -> lower index; w_k = p_k / sum_k p_k (sequential, no epsilon)
-//   sigmoid: s_i = 1 / (1 + exp(-v_i)); key_i = s_i + bias_i; top-k by key; w_k = s_k / (sum s + 1e-20)
-// The exponential is evaluated in double and rounded once to fp32 (a correctly rounded expf), so the
-// fp32 probabilities -- and therefore the top-k order including rounding ties -- match a host that
-// uses a correctly rounded expf.  The two sums are sequential in the reference's order.
+// Router kernels (fused softmax or sigmoid+bias / top-k / renormalise; per-token math in
+// route_core.cuh) and the deterministic token->expert permutation for the B200 MoE data plane.
 //
 // Permutation semantics: solar_hybrid/runtime.py:343-354 -- pairs (t, k) grouped per expert with
 // tokens ascending; experts listed in first-appearance order of the t-major, k-minor scan.
 #include "common.cuh"
 #include "route.h"
+#include "route_core.cuh"
 
 namespace moe {
 
-// Lexicographic "better" for the top-k scan: larger key, then lower index.  A NaN key never beats
-// a real candidate but does replace the empty sentinel, so every round still yields a valid index.
-__device__ __forceinline__ bool better(float ka, int ia, float kb, int ib) {
-    if (ib < 0) return ia >= 0;
-    if (ia < 0) return false;
-    return ka > kb || (ka == kb && ia < ib);
-}
-
-// One warp routes one token.  ev: per-warp shared scratch of E floats.
-__device__ void route_token_warp(const RouteArgs& a, int t, float* ev) {
-    const int lane = threadIdx.x & 31;
-    const int E = a.E, K = a.K;
-    const float* v = a.logits + (size_t)t * E;
-    constexpr int S = kMaxExperts / 32;
-    float key[S];
-    bool bad = false;
-    if (a.scoring == 0) {
-        float m = -INFINITY;
-#pragma unroll
-        for (int s = 0; s < S; s++) {
-            int i = lane + 32 * s;
-            if (i < E) {
-                float x = v[i];
-                m = x > m ? x : m;  // f32::max fold: NaN never replaces the running max
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float y = __shfl_xor_sync(0xffffffffu, m, o);
-            m = y > m ? y : m;
-        }
-#pragma unroll
-        for (int s = 0; s < S; s++) {
-            int i = lane + 32 * s;
-            if (i < E) ev[i] = (float)exp((double)(v[i] - m));
-        }
-        __syncwarp();
-        float z = 0.f;
-        if (lane == 0)
-            for (int i = 0; i < E; i++) z += ev[i];
-        z = __shfl_sync(0xffffffffu, z, 0);
-        __syncwarp();
-#pragma unroll
-        for (int s = 0; s < S; s++) {
-            int i = lane + 32 * s;
-            key[s] = -INFINITY;
-            if (i < E) {
-                float p = __fdiv_rn(ev[i], z);
-                key[s] = p;
-                ev[i] = p;  // weight value of expert i
-                bad |= (p != p);
-            }
-        }
-    } else {
-#pragma unroll
-        for (int s = 0; s < S; s++) {
-            int i = lane + 32 * s;
-            key[s] = -INFINITY;
-            if (i < E) {
-                float sg = __fdiv_rn(1.0f, 1.0f + (float)exp(-(double)v[i]));
-                float k = sg + (a.bias ? a.bias[i] : 0.f);
-                key[s] = k;
-                ev[i] = sg;
-                bad |= (k != k);
-            }
-        }
-    }
-    __syncwarp();
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.err, kErrNonFinite);
-
-    unsigned taken = 0;  // bit s: expert lane + 32 s already selected
-    int sel[kMaxTopK];
-#pragma unroll
-    for (int k = 0; k < kMaxTopK; k++) sel[k] = 0;
-    for (int k = 0; k < K; k++) {
-        float bk = -INFINITY;
-        int bi = -1;
-#pragma unroll
-        for (int s = 0; s < S; s++) {
-            int i = lane + 32 * s;
-            if (i < E && !((taken >> s) & 1u) && better(key[s], i, bk, bi)) {
-                bk = key[s];
-                bi = i;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (better(ok, oi, bk, bi)) {
-                bk = ok;
-                bi = oi;
-            }
-        }
-        bi = __shfl_sync(0xffffffffu, bi, 0);  // one winner for every lane even with NaN keys
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-#pragma unroll
-        for (int kk = 0; kk < kMaxTopK; kk++)
-            if (kk == k) sel[kk] = bi;
-    }
-    if (lane == 0) {
-        float tot = 0.f;
-        for (int k = 0; k < K; k++) tot += ev[sel[k]];
-        if (a.scoring != 0) tot += 1e-20f;
-        for (int k = 0; k < K; k++) {
-            a.idx[(size_t)t * K + k] = sel[k];
-            a.w[(size_t)t * K + k] = __fdiv_rn(ev[sel[k]], tot);
-        }
-    }
-    __syncwarp();
+// One warp routes one token t into the global idx/w arrays (scr: the warp's shared scratch).
+__device__ __forceinline__ void route_token_warp(const RouteArgs& a, int t, float* scr) {
+    const bool bad = route_token(a.logits + (size_t)t * a.E, a.bias, a.E, a.K, a.scoring, a.idx + (size_t)t * a.K,
+                                 a.w + (size_t)t * a.K, scr);
+    if (bad && (threadIdx.x & 31) == 0) atomicOr(a.err, kErrNonFinite);
 }
 
 __global__ void __launch_bounds__(256) route_topk_kernel(RouteArgs a) {
-    __shared__ float ev[8][kMaxExperts];
+    __shared__ __align__(16) float scr[8][2 * kMaxExperts];
     const int warp = threadIdx.x >> 5;
     const int t = blockIdx.x * 8 + warp;
-    if (t < a.T) route_token_warp(a, t, ev[warp]);
+    if (t < a.T) route_token_warp(a, t, scr[warp]);
 }
 
 // Counting-sort permutation of the routed pairs; one 1024-thread block.  Shared use:
@@ -277,18 +164,18 @@ __global__ void __launch_bounds__(1024) permute_kernel(RouteArgs a) {
 
 // Small batches: routing and permutation in one launch.
 __global__ void __launch_bounds__(1024) route_fused_kernel(RouteArgs a) {
-    extern __shared__ unsigned char dyn[];
-    float* ev = reinterpret_cast<float*>(dyn);  // [32][kMaxExperts]
-    unsigned char* idx8 = dyn + 32 * kMaxExperts * sizeof(float);
+    extern __shared__ __align__(16) unsigned char dyn[];
+    float* scr = reinterpret_cast<float*>(dyn);  // [32][2 * kMaxExperts]
+    unsigned char* idx8 = dyn + 32 * 2 * kMaxExperts * sizeof(float);
     const int warp = threadIdx.x >> 5;
-    for (int t = warp; t < a.T; t += 32) route_token_warp(a, t, ev + warp * kMaxExperts);
+    for (int t = warp; t < a.T; t += 32) route_token_warp(a, t, scr + warp * 2 * kMaxExperts);
     __syncthreads();
     permute_block(a, idx8);
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     if (a.T <= 64) {
-        size_t sm = 32 * kMaxExperts * sizeof(float) + (size_t)a.T * a.K;
+        size_t sm = 32 * 2 * kMaxExperts * sizeof(float) + (size_t)a.T * a.K;
         route_fused_kernel<<<1, 1024, sm, st>>>(a);
         if (launches) *launches += 1;
         return cudaGetLastError();
@@ -305,7 +192,7 @@ cudaError_t route_set_smem_limits() {
                                          kMaxTokens * kMaxTopK);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                32 * kMaxExperts * sizeof(float) + 64 * kMaxTopK);
+                                32 * 2 * kMaxExperts * sizeof(float) + 64 * kMaxTopK);
 }
 
 }  // namespace moe

@@ -256,6 +256,16 @@ class MoEDataPlane:
     def launch_count(self):
         return int(lib().moe_launch_count(self._h))
 
+    def set_option(self, option, value):
+        check(lib().moe_set_option(self._h, int(option), int(value)))
+
+    def timeline(self):
+        """Per-CTA phase stamps of the latest fused launch (MOE_OPT_TIMELINE on): [SMs, 16] ns."""
+        n = torch.cuda.get_device_properties(self.device).multi_processor_count * 16
+        buf = np.zeros(n, np.uint64)
+        check(lib().moe_timeline_read(self._h, buf.ctypes.data_as(ctypes.c_void_p), n))
+        return buf.reshape(-1, 16)
+
     def profile(self, enable=True):
         check(lib().moe_profile(self._h, int(bool(enable))))
 

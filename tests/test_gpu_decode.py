@@ -1,0 +1,107 @@
+"""The fused decode kernel (routing + expert GEMV + combine in one persistent launch) against the
+multi-kernel path and the oracle, its bounded-wait error path, and expert-parallel partial sums."""
+import numpy as np
+import pytest
+import torch
+
+from npu_offload_b200 import synth
+from tests.gpu_util import bf16_np, gpu_experts, oracle_layer
+from tests.parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+H, F, E, K = 4096, 1280, 128, 8
+
+
+@pytest.fixture(scope="module")
+def layer():
+    from npu_offload_b200.moe import MoEDataPlane
+    W = gpu_experts(33, E, H, F)
+    p = MoEDataPlane(H, F, E, K, n_layers=1, max_tokens=32)
+    for e, (g, u, d) in enumerate(W):
+        p.load_expert(0, e, g, u, d)
+    yield p, W
+    p.close()
+
+
+def _inputs(seed, T):
+    x = synth.hidden(seed, T, H)
+    lg = synth.logits(seed, T, E)
+    return x, lg, torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda(), torch.from_numpy(lg).cuda()
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 12, 16])
+def test_fused_matches_multikernel_path_and_oracle(layer, T):
+    from npu_offload_b200._lib import MOE_OPT_FUSED_DECODE
+    p, W = layer
+    x, lg, xd, lgd = _inputs(900 + T, T)
+    fused, fi, fw = p.forward(0, xd, lgd, return_topk=True, sync=True)
+    p.set_option(MOE_OPT_FUSED_DECODE, 0)
+    try:
+        multi, mi, mw = p.forward(0, xd, lgd, return_topk=True, sync=True)
+    finally:
+        p.set_option(MOE_OPT_FUSED_DECODE, 1)
+    np.testing.assert_array_equal(fi.cpu().numpy(), mi.cpu().numpy())
+    np.testing.assert_array_equal(fw.cpu().numpy(), mw.cpu().numpy())
+    assert_close(fused.cpu().numpy(), multi.cpu().numpy(), max_abs=1e-4, min_cos=0.9999999, what="fused vs multi")
+    ids = sorted(set(fi.cpu().numpy().ravel().tolist()))
+    ex = {e: ("bf16", np.concatenate([bf16_np(W[e][0]), bf16_np(W[e][1])], 0), bf16_np(W[e][2])) for e in ids}
+    ref, idx, _, _, kind = oracle_layer(x, lg, ex, K)
+    np.testing.assert_array_equal(fi.cpu().numpy(), idx)
+    assert_close(fused.cpu().numpy(), ref, what=f"fused T={T} vs {kind}")
+
+
+def test_fused_back_to_back_layers_are_independent(layer):
+    """Consecutive launches overlap through programmatic dependent launch; results must not mix."""
+    p, _ = layer
+    outs, refs = [], []
+    ins = [_inputs(1000 + i, 1 + (i % 4)) for i in range(12)]
+    for _, _, xd, lgd in ins:
+        outs.append(p.forward(0, xd, lgd))
+    torch.cuda.synchronize()
+    for _, _, xd, lgd in ins:
+        refs.append(p.forward(0, xd, lgd, sync=True))
+    for a, b in zip(outs, refs):
+        np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+
+
+def test_bounded_wait_reports_timeout_and_context_recovers(layer):
+    """A readiness count that is never published: the kernel gives up after the bound, reports
+    MOE_ETIMEOUT, and the next call on the same context is correct."""
+    from npu_offload_b200._lib import (MOE_ETIMEOUT, MOE_OPT_INJECT_WAIT_TIMEOUT, MOE_OPT_WAIT_TIMEOUT_US, MoEError)
+    p, _ = layer
+    x, lg, xd, lgd = _inputs(77, 2)
+    good = p.forward(0, xd, lgd, sync=True).cpu().numpy()
+    p.set_option(MOE_OPT_WAIT_TIMEOUT_US, 20000)
+    p.set_option(MOE_OPT_INJECT_WAIT_TIMEOUT, 1)
+    try:
+        with pytest.raises(MoEError) as ei:
+            p.forward(0, xd, lgd, sync=True)
+        assert ei.value.status == MOE_ETIMEOUT
+    finally:
+        p.set_option(MOE_OPT_INJECT_WAIT_TIMEOUT, 0)
+        p.set_option(MOE_OPT_WAIT_TIMEOUT_US, 1000000)
+    again = p.forward(0, xd, lgd, sync=True).cpu().numpy()
+    np.testing.assert_array_equal(again, good)
+
+
+def test_expert_parallel_partials_sum_to_the_full_layer(layer):
+    """Two expert-parallel rank contexts on one GPU: each computes its local experts only; the sum of
+    the partials equals the unsharded layer."""
+    from npu_offload_b200.moe import MoEDataPlane
+    from npu_offload_b200.parallel import shard_map
+    p, W = layer
+    smap = shard_map(np.exp(synth.zipf_bias(5, E))[None, :], 2)
+    ranks = [MoEDataPlane(H, F, E, K, n_layers=1, max_tokens=32, ep_rank=r, ep_world=2, shard_map=smap)
+             for r in range(2)]
+    try:
+        for e in range(E):
+            ranks[int(smap[0, e])].load_expert(0, e, *W[e])
+        for T in (1, 4, 16, 24):
+            x, lg, xd, lgd = _inputs(1200 + T, T)
+            full = p.forward(0, xd, lgd, sync=True).cpu().numpy()
+            parts = [r.forward(0, xd, lgd, sync=True).cpu().numpy() for r in ranks]
+            assert_close(parts[0] + parts[1], full, max_abs=1e-4, min_cos=0.9999999, what=f"ep2 T={T}")
+    finally:
+        for r in ranks:
+            r.close()
