@@ -172,20 +172,26 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               without faulting or hanging the GPU.
  *   MOE_OPT_RING_STAGES         tuning: cap on the fused kernel's shared-memory ring depth (4..16;
  *                               0 = as deep as shared memory allows, the default).
+ *   MOE_OPT_CONSUMER_WARPS      tuning: warps of the fused kernel that consume ring stages (1..8;
+ *                               0 = the default).
  *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
  *                               globaltimer stamps (0 start, 1 prologue done, 2 gate/up stages
  *                               issued, 3 all stages issued, 4 activations staged, 5 first warp done
- *                               with gate/up, 6 down consumed, 7 end, 8 routed, 9 grouped, 10 job
- *                               list, 11 partition, 12 all jobs published, 13 all warps done with
- *                               gate/up); read them with moe_timeline_read. */
+ *                               with gate/up, 6 down consumed, 7 end, 12 all jobs published, 13 all
+ *                               warps done with gate/up) and, for consumer warp 0, SM cycles spent
+ *                               (8) waiting for gate/up stages, (9) computing them, (10) waiting for
+ *                               down stages or activations, (11) computing down stages; read them
+ *                               with moe_timeline_read. */
 #define MOE_OPT_FUSED_DECODE 1
 #define MOE_OPT_WAIT_TIMEOUT_US 2
 #define MOE_OPT_INJECT_WAIT_TIMEOUT 3
 #define MOE_OPT_TIMELINE 4
 #define MOE_OPT_RING_STAGES 5
+#define MOE_OPT_CONSUMER_WARPS 6
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
-/* Copies up to cap stamps ([SM count][16], see MOE_OPT_TIMELINE) to host memory (synchronises). */
+/* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see
+ * MOE_OPT_TIMELINE) followed by CTA 0's per-stage issue / landed / released stamps ([3][1024]). */
 MOE_API int moe_timeline_read(moe_ctx* ctx, uint64_t* out, int cap);
 
 /* Stage timing of moe_forward with CUDA events on the caller's stream (instrumentation; off by

@@ -100,6 +100,45 @@ __device__ __forceinline__ float dot8_bf16(uint4 w, uint4 x, float acc) {
     return acc;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): low word = lower address element.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pack_f32x2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float sum_f32x2(f32x2 v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo + hi;
+}
+// two bf16 (one 32-bit word) widened to an fp32 pair
+__device__ __forceinline__ f32x2 bf16x2_to_f32x2(uint32_t w) { return pack_f32x2(bf_lo(w), bf_hi(w)); }
+// d = a * b + c per element, round to nearest (two fmaf in one instruction)
+__device__ __forceinline__ f32x2 ffma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// Sums 8 per-lane values across the warp with 9 shuffles: afterwards lane l holds the total of
+// value (l >> 2).
+__device__ __forceinline__ float warp_sum8(const float (&v)[8]) {
+    const int lane = threadIdx.x & 31;
+    float a[4], b[2];
+    const bool h16 = (lane >> 4) & 1, h8 = (lane >> 3) & 1, h4 = (lane >> 2) & 1;
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        a[k] = (h16 ? v[k + 4] : v[k]) + __shfl_xor_sync(0xffffffffu, h16 ? v[k] : v[k + 4], 16);
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+        b[k] = (h8 ? a[k + 2] : a[k]) + __shfl_xor_sync(0xffffffffu, h8 ? a[k] : a[k + 2], 8);
+    float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    return c;
+}
+
 // int8 value k (0..3) of a 32-bit word, exactly as float.
 __device__ __forceinline__ float i8f(uint32_t v, int k) { return (float)(int8_t)(v >> (8 * k)); }
 

@@ -54,6 +54,7 @@ struct __align__(16) Ctrl {
     int act_job[2];        // job whose activations occupy act slot b (-1: none)
     int act_done[2];       // phase-2 stages finished on act slot b
     int fill_seq[kMaxNS];  // fill number last issued into each ring slot (-1: none)
+    int ticket;            // next ring stage for a consumer warp
     PlanCta me;            // this CTA's share (copied from the plan; 16-byte aligned member)
     PlanShared sh;         // routing result and job list (copied from the plan; 16-byte aligned member)
 };
@@ -89,40 +90,73 @@ template <int NTB>
 __device__ __forceinline__ void p1_bf16(const uint16_t* gr, const uint16_t* ur, const uint16_t* const* xr, int H,
                                         float* g, float* u) {
     const int lane = threadIdx.x & 31;
-    float ag[NTB][2], au[NTB][2];  // two partial sums per row halve the dependent FMA chain
+    f32x2 ag[NTB][2], au[NTB][2];
 #pragma unroll
-    for (int i = 0; i < NTB; i++) ag[i][0] = ag[i][1] = au[i][0] = au[i][1] = 0.f;
+    for (int i = 0; i < NTB; i++) ag[i][0] = ag[i][1] = au[i][0] = au[i][1] = 0ull;
 #pragma unroll 4
     for (int c = lane * 8; c < H; c += 256) {
         const uint4 wg = *reinterpret_cast<const uint4*>(gr + c);
         const uint4 wu = *reinterpret_cast<const uint4*>(ur + c);
-        const uint32_t gw[4] = {wg.x, wg.y, wg.z, wg.w}, uw[4] = {wu.x, wu.y, wu.z, wu.w};
-        float gf[8], uf[8];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            gf[2 * k] = bf_lo(gw[k]);
-            gf[2 * k + 1] = bf_hi(gw[k]);
-            uf[2 * k] = bf_lo(uw[k]);
-            uf[2 * k + 1] = bf_hi(uw[k]);
-        }
+        const f32x2 g0 = bf16x2_to_f32x2(wg.x), g1 = bf16x2_to_f32x2(wg.y), g2 = bf16x2_to_f32x2(wg.z),
+                    g3 = bf16x2_to_f32x2(wg.w);
+        const f32x2 u0 = bf16x2_to_f32x2(wu.x), u1 = bf16x2_to_f32x2(wu.y), u2 = bf16x2_to_f32x2(wu.z),
+                    u3 = bf16x2_to_f32x2(wu.w);
 #pragma unroll
         for (int i = 0; i < NTB; i++) {
             const uint4 xv = *reinterpret_cast<const uint4*>(xr[i] + c);
-            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float x0 = bf_lo(xw[k]), x1 = bf_hi(xw[k]);
-                ag[i][0] = fmaf(gf[2 * k], x0, ag[i][0]);
-                ag[i][1] = fmaf(gf[2 * k + 1], x1, ag[i][1]);
-                au[i][0] = fmaf(uf[2 * k], x0, au[i][0]);
-                au[i][1] = fmaf(uf[2 * k + 1], x1, au[i][1]);
-            }
+            const f32x2 x0 = bf16x2_to_f32x2(xv.x), x1 = bf16x2_to_f32x2(xv.y), x2 = bf16x2_to_f32x2(xv.z),
+                        x3 = bf16x2_to_f32x2(xv.w);
+            ag[i][0] = ffma2(g0, x0, ag[i][0]);
+            ag[i][1] = ffma2(g1, x1, ag[i][1]);
+            ag[i][0] = ffma2(g2, x2, ag[i][0]);
+            ag[i][1] = ffma2(g3, x3, ag[i][1]);
+            au[i][0] = ffma2(u0, x0, au[i][0]);
+            au[i][1] = ffma2(u1, x1, au[i][1]);
+            au[i][0] = ffma2(u2, x2, au[i][0]);
+            au[i][1] = ffma2(u3, x3, au[i][1]);
         }
     }
 #pragma unroll
     for (int i = 0; i < NTB; i++) {
-        g[i] = warp_sum(ag[i][0] + ag[i][1]);
-        u[i] = warp_sum(au[i][0] + au[i][1]);
+        g[i] = warp_sum(sum_f32x2(ag[i][0]) + sum_f32x2(ag[i][1]));
+        u[i] = warp_sum(sum_f32x2(au[i][0]) + sum_f32x2(au[i][1]));
+    }
+}
+
+// Same with x already widened to fp32 in shared memory (small batches): no x conversion per use.
+template <int NTB>
+__device__ __forceinline__ void p1_bf16_xf(const uint16_t* gr, const uint16_t* ur, const float* const* xr, int H,
+                                           float* g, float* u) {
+    const int lane = threadIdx.x & 31;
+    f32x2 ag[NTB][2], au[NTB][2];
+#pragma unroll
+    for (int i = 0; i < NTB; i++) ag[i][0] = ag[i][1] = au[i][0] = au[i][1] = 0ull;
+#pragma unroll 4
+    for (int c = lane * 8; c < H; c += 256) {
+        const uint4 wg = *reinterpret_cast<const uint4*>(gr + c);
+        const uint4 wu = *reinterpret_cast<const uint4*>(ur + c);
+        const f32x2 g0 = bf16x2_to_f32x2(wg.x), g1 = bf16x2_to_f32x2(wg.y), g2 = bf16x2_to_f32x2(wg.z),
+                    g3 = bf16x2_to_f32x2(wg.w);
+        const f32x2 u0 = bf16x2_to_f32x2(wu.x), u1 = bf16x2_to_f32x2(wu.y), u2 = bf16x2_to_f32x2(wu.z),
+                    u3 = bf16x2_to_f32x2(wu.w);
+#pragma unroll
+        for (int i = 0; i < NTB; i++) {
+            const ulonglong2 xa = *reinterpret_cast<const ulonglong2*>(xr[i] + c);
+            const ulonglong2 xb = *reinterpret_cast<const ulonglong2*>(xr[i] + c + 4);
+            ag[i][0] = ffma2(g0, xa.x, ag[i][0]);
+            ag[i][1] = ffma2(g1, xa.y, ag[i][1]);
+            ag[i][0] = ffma2(g2, xb.x, ag[i][0]);
+            ag[i][1] = ffma2(g3, xb.y, ag[i][1]);
+            au[i][0] = ffma2(u0, xa.x, au[i][0]);
+            au[i][1] = ffma2(u1, xa.y, au[i][1]);
+            au[i][0] = ffma2(u2, xb.x, au[i][0]);
+            au[i][1] = ffma2(u3, xb.y, au[i][1]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NTB; i++) {
+        g[i] = warp_sum(sum_f32x2(ag[i][0]) + sum_f32x2(ag[i][1]));
+        u[i] = warp_sum(sum_f32x2(au[i][0]) + sum_f32x2(au[i][1]));
     }
 }
 
@@ -161,23 +195,61 @@ __device__ __forceinline__ void p1_q8(const int8_t* gr, const int8_t* ur, const 
     }
 }
 
+template <int NTB>
+__device__ __forceinline__ void p1_q8_xf(const int8_t* gr, const int8_t* ur, const float* const* xr, int H, float* g,
+                                         float* u) {
+    const int lane = threadIdx.x & 31;
+    float ag[NTB], au[NTB];
+#pragma unroll
+    for (int i = 0; i < NTB; i++) ag[i] = au[i] = 0.f;
+#pragma unroll 2
+    for (int c = lane * 16; c < H; c += 512) {
+        const uint4 wg = *reinterpret_cast<const uint4*>(gr + c);
+        const uint4 wu = *reinterpret_cast<const uint4*>(ur + c);
+        const uint32_t gw[4] = {wg.x, wg.y, wg.z, wg.w}, uw[4] = {wu.x, wu.y, wu.z, wu.w};
+#pragma unroll
+        for (int i = 0; i < NTB; i++) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 xv = *reinterpret_cast<const float4*>(xr[i] + c + 4 * q);
+                float a = ag[i], b = au[i];
+                a = fmaf(i8f(gw[q], 0), xv.x, a);
+                a = fmaf(i8f(gw[q], 1), xv.y, a);
+                a = fmaf(i8f(gw[q], 2), xv.z, a);
+                a = fmaf(i8f(gw[q], 3), xv.w, a);
+                b = fmaf(i8f(uw[q], 0), xv.x, b);
+                b = fmaf(i8f(uw[q], 1), xv.y, b);
+                b = fmaf(i8f(uw[q], 2), xv.z, b);
+                b = fmaf(i8f(uw[q], 3), xv.w, b);
+                ag[i] = a;
+                au[i] = b;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NTB; i++) {
+        g[i] = warp_sum(ag[i]);
+        u[i] = warp_sum(au[i]);
+    }
+}
+
 // ---- phase 2: nr down rows of one job, NTB tokens; results go straight to the ybuf rows ----
 // yb[i] = ybuf row of token slot i (nullptr for padded slots), wp[i] = routing weight,
 // sc = per-row int8 scales (nullptr for bf16).
 template <int NTB, int RSM>
 __device__ __forceinline__ void p2_store(float (&acc)[RSM][NTB], int nr, float* const* yb, const float* wp,
                                          const float* sc) {
+    static_assert(RSM == 8, "butterfly reduction of 8 rows");
     const int lane = threadIdx.x & 31;
+    const int r = lane >> 2;  // the row whose total this lane receives
+    const float s = (sc && r < nr) ? __ldg(sc + r) : 1.f;
 #pragma unroll
-    for (int r = 0; r < RSM; r++) {
-        if (r < nr) {
-            const float s = sc ? __ldg(sc + r) : 1.f;
+    for (int i = 0; i < NTB; i++) {
+        float v[8];
 #pragma unroll
-            for (int i = 0; i < NTB; i++) {
-                const float v = warp_sum(acc[r][i]);
-                if (lane == 0 && yb[i]) yb[i][r] = sc ? (wp[i] * v) * s : wp[i] * v;
-            }
-        }
+        for (int k = 0; k < 8; k++) v[k] = acc[k][i];
+        const float tot = warp_sum8(v);
+        if ((lane & 3) == 0 && r < nr && yb[i]) yb[i][r] = sc ? (wp[i] * tot) * s : wp[i] * tot;
     }
 }
 
@@ -185,24 +257,42 @@ template <int NTB, int RSM>
 __device__ __forceinline__ void p2_bf16(const uint16_t* S, int nr, const uint16_t* const* ar, int F, float* const* yb,
                                         const float* wp) {
     const int lane = threadIdx.x & 31;
-    float acc[RSM][NTB];
+    f32x2 acc2[RSM][NTB];
 #pragma unroll
     for (int r = 0; r < RSM; r++)
 #pragma unroll
-        for (int i = 0; i < NTB; i++) acc[r][i] = 0.f;
+        for (int i = 0; i < NTB; i++) acc2[r][i] = 0ull;
     for (int c = lane * 8; c < F; c += 256) {
-        uint4 av[NTB];
+        f32x2 av[NTB][4];
 #pragma unroll
-        for (int i = 0; i < NTB; i++) av[i] = *reinterpret_cast<const uint4*>(ar[i] + c);
+        for (int i = 0; i < NTB; i++) {
+            const uint4 a4 = *reinterpret_cast<const uint4*>(ar[i] + c);
+            av[i][0] = bf16x2_to_f32x2(a4.x);
+            av[i][1] = bf16x2_to_f32x2(a4.y);
+            av[i][2] = bf16x2_to_f32x2(a4.z);
+            av[i][3] = bf16x2_to_f32x2(a4.w);
+        }
 #pragma unroll
         for (int r = 0; r < RSM; r++) {
             if (r < nr) {
                 const uint4 wv = *reinterpret_cast<const uint4*>(S + (size_t)r * F + c);
+                const f32x2 w0 = bf16x2_to_f32x2(wv.x), w1 = bf16x2_to_f32x2(wv.y), w2 = bf16x2_to_f32x2(wv.z),
+                            w3 = bf16x2_to_f32x2(wv.w);
 #pragma unroll
-                for (int i = 0; i < NTB; i++) acc[r][i] = dot8_bf16(wv, av[i], acc[r][i]);
+                for (int i = 0; i < NTB; i++) {
+                    f32x2 t = ffma2(w0, av[i][0], acc2[r][i]);
+                    t = ffma2(w1, av[i][1], t);
+                    t = ffma2(w2, av[i][2], t);
+                    acc2[r][i] = ffma2(w3, av[i][3], t);
+                }
             }
         }
     }
+    float acc[RSM][NTB];
+#pragma unroll
+    for (int r = 0; r < RSM; r++)
+#pragma unroll
+        for (int i = 0; i < NTB; i++) acc[r][i] = r < nr ? sum_f32x2(acc2[r][i]) : 0.f;
     p2_store<NTB, RSM>(acc, nr, yb, wp, nullptr);
 }
 
@@ -250,23 +340,42 @@ __device__ void stage_p1(const DecodeArgs& a, Ctrl& c, const unsigned char* S, c
     const size_t rb = (size_t)H * esize(kind);
     for (int t0 = 0; t0 < n; t0 += 4) {
         const int nt = min(4, n - t0);
-        const uint16_t* xr[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            xr[i] = reinterpret_cast<const uint16_t*>(xreg) + (size_t)c.sh.ptok[p0 + t0 + min(i, nt - 1)] * H;
         float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-        if (kind == kKindBF16) {
-            const uint16_t* gr = reinterpret_cast<const uint16_t*>(S);
-            const uint16_t* ur = reinterpret_cast<const uint16_t*>(S + rb);
-            if (nt == 1) p1_bf16<1>(gr, ur, xr, H, g, u);
-            else if (nt == 2) p1_bf16<2>(gr, ur, xr, H, g, u);
-            else p1_bf16<4>(gr, ur, xr, H, g, u);
+        if (a.x_f32) {
+            const float* xr[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                xr[i] = reinterpret_cast<const float*>(xreg) + (size_t)c.sh.ptok[p0 + t0 + min(i, nt - 1)] * H;
+            if (kind == kKindBF16) {
+                const uint16_t* gr = reinterpret_cast<const uint16_t*>(S);
+                const uint16_t* ur = reinterpret_cast<const uint16_t*>(S + rb);
+                if (nt == 1) p1_bf16_xf<1>(gr, ur, xr, H, g, u);
+                else if (nt == 2) p1_bf16_xf<2>(gr, ur, xr, H, g, u);
+                else p1_bf16_xf<4>(gr, ur, xr, H, g, u);
+            } else {
+                const int8_t* gr = reinterpret_cast<const int8_t*>(S);
+                const int8_t* ur = reinterpret_cast<const int8_t*>(S + rb);
+                if (nt == 1) p1_q8_xf<1>(gr, ur, xr, H, g, u);
+                else p1_q8_xf<4>(gr, ur, xr, H, g, u);
+            }
         } else {
-            const int8_t* gr = reinterpret_cast<const int8_t*>(S);
-            const int8_t* ur = reinterpret_cast<const int8_t*>(S + rb);
-            if (nt == 1) p1_q8<1>(gr, ur, xr, H, g, u);
-            else if (nt == 2) p1_q8<2>(gr, ur, xr, H, g, u);
-            else p1_q8<4>(gr, ur, xr, H, g, u);
+            const uint16_t* xr[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                xr[i] = reinterpret_cast<const uint16_t*>(xreg) + (size_t)c.sh.ptok[p0 + t0 + min(i, nt - 1)] * H;
+            if (kind == kKindBF16) {
+                const uint16_t* gr = reinterpret_cast<const uint16_t*>(S);
+                const uint16_t* ur = reinterpret_cast<const uint16_t*>(S + rb);
+                if (nt == 1) p1_bf16<1>(gr, ur, xr, H, g, u);
+                else if (nt == 2) p1_bf16<2>(gr, ur, xr, H, g, u);
+                else p1_bf16<4>(gr, ur, xr, H, g, u);
+            } else {
+                const int8_t* gr = reinterpret_cast<const int8_t*>(S);
+                const int8_t* ur = reinterpret_cast<const int8_t*>(S + rb);
+                if (nt == 1) p1_q8<1>(gr, ur, xr, H, g, u);
+                else if (nt == 2) p1_q8<2>(gr, ur, xr, H, g, u);
+                else p1_q8<4>(gr, ur, xr, H, g, u);
+            }
         }
         float mg = 0.f, mu = 0.f;
 #pragma unroll
@@ -391,6 +500,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             c.act_done[b] = 0;
         }
         c.abort_flag = 0;
+        c.ticket = 0;
         fence_mbar_init();
         // The plan kernel published the plan before launching this grid; the acquire makes it visible
         // (bounded in case the launch order was violated).
@@ -426,9 +536,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         if (lane == 0) {
             const uint64_t deadline = globaltimer_ns() + 4 * a.timeout_ns;
             const uint64_t pol = l2_evict_first();
-            const uint32_t xb = (uint32_t)T * H * 2;
-            mbar_arrive_expect_tx(&c.x_full, xb);
-            bulk_g2s(xreg, a.x, xb, &c.x_full);  // read by every CTA: default L2 policy
+            if (!a.x_f32) {  // bf16 x via one bulk copy (read by every CTA: default L2 policy)
+                const uint32_t xb = (uint32_t)T * H * 2;
+                mbar_arrive_expect_tx(&c.x_full, xb);
+                bulk_g2s(xreg, a.x, xb, &c.x_full);
+            }
             P2Cursor cur;
             SegCursor seg;
             int i = 0;
@@ -462,11 +574,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
                     bulk_g2s(dst, c.sh.jw2[j] + (size_t)(c.me.h0 + row0) * rowb, nr * rowb, &c.full[slot], pol);
                 }
                 *(volatile int*)&c.fill_seq[slot] = i / NS;  // consumers may now wait on this fill's phase
+                if (a.stage_log && s == 0 && i < kStageLogMax) a.stage_log[i] = globaltimer_ns();
             }
             if (tl) tl[3] = globaltimer_ns();
             // every issued copy lands before this CTA may exit
             const uint64_t dd = globaltimer_ns() + a.timeout_ns;
-            drain_bar(&c.x_full, 0, dd);
+            if (!a.x_f32) drain_bar(&c.x_full, 0, dd);
             for (int k = i > NS ? i - NS : 0; k < i; k++) drain_bar(&c.full[k % NS], (k / NS) & 1, dd);
         }
         return;
@@ -563,12 +676,31 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     };
     P2Cursor cur;
     SegCursor seg;
-    const int nwc = a.nwc;  // consumer warps taking ring stages round-robin
-    bool ok = wait_bar(&c.x_full, 0, c, a.err, deadline);
-    int slot = warp % NS, fill = warp / NS;  // ring position of stage i, advanced incrementally
-    for (int i = warp; ok && warp < nwc && i < ntot; i += nwc) {
+    const int nwc = a.nwc;  // consumer warps taking ring stages
+    bool ok = true;
+    if (a.x_f32) {  // widen x to fp32 in shared memory once (all consumer warps), then meet
+        const uint4* xs = reinterpret_cast<const uint4*>(a.x);
+        float4* xd = reinterpret_cast<float4*>(xreg);
+        for (int q = tid; q < T * H / 8; q += kNWC * 32) {
+            const uint4 v = __ldg(xs + q);
+            xd[2 * q] = make_float4(bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y));
+            xd[2 * q + 1] = make_float4(bf_lo(v.z), bf_hi(v.z), bf_lo(v.w), bf_hi(v.w));
+        }
+        named_bar_sync(2, kNWC * 32);
+    } else {
+        ok = wait_bar(&c.x_full, 0, c, a.err, deadline);
+    }
+    long long cyc_wait[2] = {0, 0}, cyc_work[2] = {0, 0};  // timeline instrumentation (warp 0)
+    // Stages are taken in ticket order (a stage that has landed goes to the next free warp).
+    while (ok && warp < nwc) {
+        int i = 0;
+        if (lane == 0) i = atomicAdd(&c.ticket, 1);
+        i = __shfl_sync(0xffffffffu, i, 0);
+        if (i >= ntot) break;
+        const int slot = i % NS, fill = i / NS;
         // publish finished gate/up units before anything that may wait on other CTAs' publications
         if (i >= n1 && !p1_signalled) signal_p1();
+        const long long tw0 = tl ? clock64() : 0;
         // the slot's parity is only meaningful once this fill has been issued (fill_seq), so a warp
         // running ahead of the others never reads a phase from an older round of the ring
         int issued = 1;
@@ -580,6 +712,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         if (!__all_sync(0xffffffffu, issued)) break;
         if (!wait_bar(&c.full[slot], fill & 1, c, a.err, deadline)) break;
         const unsigned char* S = ring + (size_t)slot * SB;
+        const long long tw1 = tl ? clock64() : 0;
+        if (a.stage_log && s == 0 && lane == 0 && i < kStageLogMax) a.stage_log[kStageLogMax + i] = globaltimer_ns();
         if (i < n1) {
             int j, f, nu;
             seg.at(c, i, j, f, nu);
@@ -607,6 +741,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
                 }
             if (!__all_sync(0xffffffffu, ready)) break;
             __threadfence_block();
+            if (tl) cyc_wait[1] += clock64() - tw1;  // act hand-off wait counts as waiting
             const unsigned char* A = a.act_resident ? xreg + (size_t)c.sh.jp0[j] * F * 2 : xreg + (size_t)b * act_pitch;
             stage_p2(a, c, ybuf, S, reinterpret_cast<const uint16_t*>(A), j, row0, nr);
             __syncwarp();
@@ -614,13 +749,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&c.empty[slot]);
-        slot += nwc;
-        while (slot >= NS) {
-            slot -= NS;
-            fill++;
+        if (a.stage_log && s == 0 && lane == 0 && i < kStageLogMax) a.stage_log[2 * kStageLogMax + i] = globaltimer_ns();
+        if (tl) {
+            const int ph = i >= n1;
+            cyc_wait[ph] += tw1 - tw0;
+            cyc_work[ph] += clock64() - tw1;
         }
     }
     if (!p1_signalled) signal_p1();
+    if (tl && warp == 0 && lane == 0) {
+        tl[8] = (uint64_t)cyc_wait[0];
+        tl[9] = (uint64_t)cyc_work[0];
+        tl[10] = (uint64_t)cyc_wait[1];
+        tl[11] = (uint64_t)(cyc_work[1] - cyc_wait[1]);
+    }
     named_bar_sync(1, kNWC * 32);
     if (tl && tid == 0) tl[6] = globaltimer_ns();
 
@@ -651,7 +793,8 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     const size_t ctrl = up128(sizeof(Ctrl));
     const size_t ybuf = up128((size_t)a.T * a.K * a.hr_max * 4);
     const size_t act_pitch = up128((size_t)a.T * a.F * 2);
-    const size_t xrows = (size_t)a.T * a.H * 2;
+    a.x_f32 = a.T <= 4 ? 1 : 0;  // small batches keep x widened to fp32 in shared memory
+    const size_t xrows = (size_t)a.T * a.H * (a.x_f32 ? 4 : 2);
     // Resident mode keeps every pair's activations in shared memory (no slot reuse) when that still
     // leaves room for an 8-deep ring; otherwise two rolling per-job slots.
     const size_t act_all = up128((size_t)a.T * a.K * a.F * 2);
@@ -668,7 +811,7 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     int ns = (int)std::min<size_t>(kMaxNS, (kSmemCap - fixed) / slot);
     if (a.ns_cap > 0) ns = std::min(ns, a.ns_cap);
     if (ns < 2) return false;
-    a.nwc = kNWC;
+    a.nwc = a.nwc >= 1 && a.nwc <= kNWC ? a.nwc : kNWC;  // requested consumer warps (tuning), else all
     a.NS = ns;
     *smem_bytes = fixed + (size_t)a.NS * slot;
     return true;

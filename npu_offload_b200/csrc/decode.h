@@ -8,6 +8,7 @@ constexpr int kDecodeMaxT = 16;  // largest batch the fused decode kernel takes
 constexpr int kDecodeMaxPairs = kDecodeMaxT * kMaxTopK;
 constexpr int kDecodePlanJobs = 128;  // local jobs of one fused call (<= min(E, T*K))
 constexpr int kTimelineSlots = 16;  // per-CTA stamps recorded when DecodeArgs::timeline is set
+constexpr int kStageLogMax = 1024;  // stages of CTA 0 recorded in DecodeArgs::stage_log
 constexpr int kPlanMaxGrid = 256;   // decode CTAs a plan can describe
 constexpr int kSegPerCta = 16;      // gate/up segments (runs of one job's units) per decode CTA
 
@@ -76,12 +77,14 @@ struct DecodeArgs {
     uint32_t slot_bytes;   // bytes per ring stage
     int rs_bf16, rs_q8;    // down rows per phase-2 stage
     int act_resident;      // 1: all activations staged in shared memory at once; 0: two rolling slots
+    int x_f32;             // 1: x widened to fp32 in shared memory (small batches); 0: bf16 x
     uint32_t off_ring, off_x, off_ybuf;  // dynamic shared-memory offsets
     int hr_max;            // max output rows per CTA (ybuf row pitch)
     uint64_t timeout_ns;   // bound on every device-side wait
     int inject_timeout;    // test hook: wait for a readiness count that never arrives
     uint64_t* timeline;    // optional [grid][kTimelineSlots] per-CTA phase stamps (globaltimer ns), else null
     int ns_cap;            // tuning: cap on ring stages (0 = as many as shared memory allows)
+    uint64_t* stage_log;   // optional [3][kStageLogMax] issue / landed / released stamps of CTA 0's stages
 };
 
 // Host-side planning: shared-memory size and stage geometry for (T, H, F, K) on `grid` CTAs.

@@ -127,6 +127,7 @@ struct moe_ctx {
     int inject_timeout = 0;
     uint64_t* d_timeline = nullptr;  // [sm_count][kTimelineSlots] when MOE_OPT_TIMELINE is on
     int ns_cap = 0;
+    int nwc = 0;  // fused kernel consumer warps (0: all)
     // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_ev;  // kProfMarks events per profiled call
@@ -530,7 +531,9 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         da.timeout_ns = c->timeout_ns;
         da.inject_timeout = c->inject_timeout;
         da.timeline = c->d_timeline;
+        da.stage_log = c->d_timeline ? reinterpret_cast<uint64_t*>(c->d_timeline + (size_t)c->sm_count * kTimelineSlots) : nullptr;
         da.ns_cap = c->ns_cap;
+        da.nwc = c->nwc;
         use_fused = plan_decode(da, dgrid, &dsmem);
     }
     if (use_fused) {
@@ -884,12 +887,16 @@ int moe_set_option(moe_ctx* c, int option, int64_t value) {
             if (value < 0 || value > 16) return fail(MOE_EINVAL, "ring stages %lld not in [0,16]", (long long)value);
             c->ns_cap = (int)value;
             return MOE_OK;
+        case MOE_OPT_CONSUMER_WARPS:
+            if (value < 0 || value > 8) return fail(MOE_EINVAL, "consumer warps %lld not in [0,8]", (long long)value);
+            c->nwc = (int)value;
+            return MOE_OK;
         case MOE_OPT_TIMELINE: {
             DeviceGuard dg(c->dev);
             if (value && !c->d_timeline) {
-                int st = dalloc(&c->d_timeline, (size_t)c->sm_count * kTimelineSlots);
+                int st = dalloc(&c->d_timeline, (size_t)c->sm_count * kTimelineSlots + 3 * kStageLogMax);
                 if (st) return st;
-                CUDA_TRY(cudaMemset(c->d_timeline, 0, sizeof(uint64_t) * c->sm_count * kTimelineSlots));
+                CUDA_TRY(cudaMemset(c->d_timeline, 0, sizeof(uint64_t) * ((size_t)c->sm_count * kTimelineSlots + 3 * kStageLogMax)));
             } else if (!value && c->d_timeline) {
                 cudaDeviceSynchronize();
                 cudaFree(c->d_timeline);
@@ -906,7 +913,7 @@ int moe_timeline_read(moe_ctx* c, uint64_t* out, int cap) {
     if (!c || !out) return fail(MOE_EINVAL, "bad argument");
     if (!c->d_timeline) return fail(MOE_ESTATE, "timeline recording is off (MOE_OPT_TIMELINE)");
     DeviceGuard dg(c->dev);
-    const int n = std::min(cap, c->sm_count * kTimelineSlots);
+    const int n = std::min(cap, c->sm_count * kTimelineSlots + 3 * kStageLogMax);
     CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaMemcpy(out, c->d_timeline, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
     return MOE_OK;

@@ -261,10 +261,12 @@ class MoEDataPlane:
 
     def timeline(self):
         """Per-CTA phase stamps of the latest fused launch (MOE_OPT_TIMELINE on): [SMs, 16] ns."""
-        n = torch.cuda.get_device_properties(self.device).multi_processor_count * 16
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        n = sms * 16 + 3 * 1024
         buf = np.zeros(n, np.uint64)
         check(lib().moe_timeline_read(self._h, buf.ctypes.data_as(ctypes.c_void_p), n))
-        return buf.reshape(-1, 16)
+        self.stage_log = buf[sms * 16:].reshape(3, 1024)
+        return buf[:sms * 16].reshape(-1, 16)
 
     def profile(self, enable=True):
         check(lib().moe_profile(self._h, int(bool(enable))))
