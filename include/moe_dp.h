@@ -167,27 +167,25 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               (routing + expert GEMV + combine); 0: the multi-kernel path.
  *   MOE_OPT_WAIT_TIMEOUT_US     bound on every device-side wait of the fused kernel (default 1 s);
  *                               a wait that runs out makes the call report MOE_ETIMEOUT.
- *   MOE_OPT_INJECT_WAIT_TIMEOUT test hook: 1 makes the fused kernel wait for a readiness count that
- *                               is never published, so the bounded-wait error path can be tested
- *                               without faulting or hanging the GPU.
- *   MOE_OPT_RING_STAGES         tuning: cap on the fused kernel's shared-memory ring depth (4..16;
+ *   MOE_OPT_INJECT_WAIT_TIMEOUT test hook: 1 makes the fused kernel's grid-wide arrival wait for one
+ *                               CTA more than the grid has, so the bounded-wait error path can be
+ *                               tested without faulting or hanging the GPU.
+ *   MOE_OPT_RING_STAGES         tuning: cap on the fused kernel's shared-memory ring depth (2..16;
  *                               0 = as deep as shared memory allows, the default).
- *   MOE_OPT_CONSUMER_WARPS      tuning: warps of the fused kernel that consume ring stages (1..8;
- *                               0 = the default).
+ *   MOE_OPT_STAGE_BYTES         tuning: target bytes per ring stage of the fused kernel (a stage holds
+ *                               max(1, target / unit bytes) units; 0 = the default, 32 KiB).
  *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
- *                               globaltimer stamps (0 start, 1 prologue done, 2 gate/up stages
- *                               issued, 3 all stages issued, 4 activations staged, 5 first warp done
- *                               with gate/up, 6 down consumed, 7 end, 12 all jobs published, 13 all
- *                               warps done with gate/up) and, for consumer warp 0, SM cycles spent
- *                               (8) waiting for gate/up stages, (9) computing them, (10) waiting for
- *                               down stages or activations, (11) computing down stages; read them
- *                               with moe_timeline_read. */
+ *                               globaltimer / cycle slots (0 start, 1 plan share loaded, 2 all stages
+ *                               issued, 3 all segments done, 4 grid-wide arrival seen, 5 reduction
+ *                               done; for consumer warp 0, SM cycles (8) waiting for ring stages,
+ *                               (9) working on them, (10) of which in the cross-warp exchange) and
+ *                               CTA 0's per-stage stamps; read them with moe_timeline_read. */
 #define MOE_OPT_FUSED_DECODE 1
 #define MOE_OPT_WAIT_TIMEOUT_US 2
 #define MOE_OPT_INJECT_WAIT_TIMEOUT 3
 #define MOE_OPT_TIMELINE 4
 #define MOE_OPT_RING_STAGES 5
-#define MOE_OPT_CONSUMER_WARPS 6
+#define MOE_OPT_STAGE_BYTES 6
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
 /* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see

@@ -21,17 +21,20 @@ constexpr int kKindBF16 = 1;
 constexpr int kKindQ8 = 2;
 constexpr int kKindRemote = 3;
 
-// Gate/up row layouts of ExpDesc::w1.
-//   kLayoutSplit:       [F gate rows][F up rows] (the reference's [Wg; Wu], cpu_moe.cpp:4)
-//   kLayoutInterleaved: [F][gate row | up row]   (expert tables held by a context: one
-//                       contiguous 2-row unit per f, streamed with a single bulk copy)
+// Weight layouts of ExpDesc.
+//   kLayoutSplit: w1 = [F gate rows][F up rows] of H (the reference's [Wg; Wu], cpu_moe.cpp:4),
+//                 w2 = [H, F] down rows; int8 scales sc = [2F + H] (gate f, up F+f, down 2F+h).
+//   kLayoutUnit:  expert tables held by a context.  One unit per intermediate index f, stored
+//                 contiguously so that a CTA owning units [f0, f1) streams them as one run:
+//                   bf16: [gate row f | up row f | down column f] = 3H elements
+//                   int8: [gate row f | up row f | down column f | sc_gate f, sc_up f, 0, 0 (fp32)]
+//                         = 3H + 16 bytes
+//                 (down column f = W2[:, f]).  w1 = unit 0, w2 = w1 + 2H elements (down column 0),
+//                 sc = the separate [2F + H] scale array (also used for the down scales).
 constexpr int kLayoutSplit = 0;
-constexpr int kLayoutInterleaved = 1;
+constexpr int kLayoutUnit = 2;
 
 // Per (layer, expert) storage descriptor, resident in HBM.
-//   kind 1 (bf16): w1 = 2F rows of H (layout above), w2 = [H,F] down, sc = null
-//   kind 2 (int8): w1 = 2F rows of H int8, w2 = [H,F] int8, sc = [2F+H] fp32 row scales
-//                  (scale f: gate row f, F+f: up row f, 2F+h: down row h)
 struct ExpDesc {
     const void* w1;
     const void* w2;
@@ -40,12 +43,21 @@ struct ExpDesc {
     int32_t layout;
 };
 
+// Elements (bf16) or bytes (int8) between consecutive units of a kLayoutUnit table.
+__host__ __device__ __forceinline__ size_t unit_pitch(int kind, int H) {
+    return kind == kKindQ8 ? (size_t)3 * H + 16 : (size_t)3 * H;
+}
+// Bytes of one unit.
+__host__ __device__ __forceinline__ size_t unit_bytes(int kind, int H) {
+    return kind == kKindQ8 ? (size_t)3 * H + 16 : (size_t)6 * H;
+}
+
 // Element offsets of gate row f and up row f inside w1.
 __host__ __device__ __forceinline__ size_t gate_row(const ExpDesc& d, int f, int H, int F) {
-    return d.layout == kLayoutInterleaved ? (size_t)f * 2 * H : (size_t)f * H;
+    return d.layout == kLayoutUnit ? (size_t)f * unit_pitch(d.kind, H) : (size_t)f * H;
 }
 __host__ __device__ __forceinline__ size_t up_row(const ExpDesc& d, int f, int H, int F) {
-    return d.layout == kLayoutInterleaved ? (size_t)f * 2 * H + H : (size_t)(F + f) * H;
+    return d.layout == kLayoutUnit ? (size_t)f * unit_pitch(d.kind, H) + H : (size_t)(F + f) * H;
 }
 
 // One expert job of a forward call: which weights, which pairs.
@@ -121,6 +133,29 @@ __device__ __forceinline__ f32x2 ffma2(f32x2 a, f32x2 b, f32x2 c) {
     return d;
 }
 
+// Mixed-precision FMA (sm_100): bf16 x bf16 products accumulated in fp32 with one rounding -- the
+// same bits as fmaf on the widened operands (a bf16 product is exact in fp32), without widening.
+// lo += w.lo * x.lo, hi += w.hi * x.hi for two packed bf16 pairs.
+__device__ __forceinline__ void fma_bf16x2(uint32_t w, uint32_t x, float& lo, float& hi) {
+    asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+        "mov.b32 {wl, wh}, %2;\n\t"
+        "mov.b32 {xl, xh}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, wl, xl, %0;\n\t"
+        "fma.rn.f32.bf16 %1, wh, xh, %1;\n\t}"
+        : "+f"(lo), "+f"(hi)
+        : "r"(w), "r"(x));
+}
+// lo += w.lo * s, hi += w.hi * s with s the bf16 in the low half of a (a scalar times a pair).
+__device__ __forceinline__ void fma_bf16x2_s(uint32_t w, uint32_t a, float& lo, float& hi) {
+    asm("{\n\t.reg .b16 wl, wh, al, ah;\n\t"
+        "mov.b32 {wl, wh}, %2;\n\t"
+        "mov.b32 {al, ah}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, wl, al, %0;\n\t"
+        "fma.rn.f32.bf16 %1, wh, al, %1;\n\t}"
+        : "+f"(lo), "+f"(hi)
+        : "r"(w), "r"(a));
+}
+
 // Sums 8 per-lane values across the warp with 9 shuffles: afterwards lane l holds the total of
 // value (l >> 2).
 __device__ __forceinline__ float warp_sum8(const float (&v)[8]) {
@@ -137,6 +172,35 @@ __device__ __forceinline__ float warp_sum8(const float (&v)[8]) {
     c += __shfl_xor_sync(0xffffffffu, c, 2);
     c += __shfl_xor_sync(0xffffffffu, c, 1);
     return c;
+}
+
+// Sums V per-lane values (V a power of two, <= 32) across the warp with V - 1 + 5 - log2(V)
+// shuffles (recursive halving).  Afterwards every lane of the group of 32/V consecutive lanes
+// l with l / (32 / V) == i holds the total of value i; the additions follow a fixed tree, so
+// every warp computing the same inputs gets the same bits.
+template <int V>
+__device__ __forceinline__ float warp_sum_multi(float (&v)[V]) {
+    static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
+    const int lane = threadIdx.x & 31;
+    int n = V;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (n > 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int k = 0; k < V / 2; k++) {
+                if (k < n / 2) {
+                    const float keep = up ? v[k + n / 2] : v[k];
+                    const float give = up ? v[k] : v[k + n / 2];
+                    v[k] = keep + __shfl_xor_sync(0xffffffffu, give, o);
+                }
+            }
+            n >>= 1;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
+    return v[0];
 }
 
 // int8 value k (0..3) of a 32-bit word, exactly as float.

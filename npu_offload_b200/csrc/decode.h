@@ -1,46 +1,53 @@
-// Fused persistent decode kernel: launch interface.
+// Fused decode path: plan kernel + persistent decode kernel, launch interface.
 #pragma once
 #include "common.cuh"
 
 namespace moe {
 
-constexpr int kDecodeMaxT = 16;  // largest batch the fused decode kernel takes
+constexpr int kDecodeMaxT = 16;  // largest batch the fused decode path takes
 constexpr int kDecodeMaxPairs = kDecodeMaxT * kMaxTopK;
-constexpr int kDecodePlanJobs = 128;  // local jobs of one fused call (<= min(E, T*K))
+constexpr int kGroupMax = 4;     // tokens of one token group (their x / y slices live in registers)
+constexpr int kMaxGroups = kDecodeMaxPairs;
+constexpr int kPlanMaxGrid = 256;  // decode CTAs a plan can describe
+constexpr int kSegPerCta = 8;      // segments (runs of one token group's units) per decode CTA
+constexpr int kMaxSegTotal = kPlanMaxGrid + kMaxGroups;  // segments of one call: <= grid + groups
 constexpr int kTimelineSlots = 16;  // per-CTA stamps recorded when DecodeArgs::timeline is set
 constexpr int kStageLogMax = 1024;  // stages of CTA 0 recorded in DecodeArgs::stage_log
-constexpr int kPlanMaxGrid = 256;   // decode CTAs a plan can describe
-constexpr int kSegPerCta = 16;      // gate/up segments (runs of one job's units) per decode CTA
 
-// Routing result and job list of one fused call, identical for every decode CTA.  The plan structs
-// are copied with 16-byte vector loads, hence the 16-byte alignment (sizes are multiples of 16).
-struct __align__(16) PlanShared {
-    int nj, np, T, pad;
-    int jexp[kDecodePlanJobs];
-    int jkind[kDecodePlanJobs];
-    int jlayout[kDecodePlanJobs];
-    const unsigned char* jw1[kDecodePlanJobs];  // job's gate/up rows
-    const unsigned char* jw2[kDecodePlanJobs];  // job's down rows
-    const float* jsc[kDecodePlanJobs];          // job's int8 row scales
-    int jp0[kDecodePlanJobs + 1];               // pair offsets (job-major)
-    int ptok[kDecodeMaxPairs];                  // token of each pair
-    float pw[kDecodeMaxPairs];                  // routing weight of each pair
-    int tpn[kDecodeMaxT];                       // local pairs per token
-    int tpair[kDecodeMaxT][kMaxTopK];           // a token's pairs in job order
+// One segment: units [f0, f0 + nu) of one token group's expert, a contiguous run of the unit table.
+struct __align__(16) Seg {
+    const unsigned char* src;  // unit f0
+    const float* sc;           // int8 scales [2F + H] of the expert (down scales at 2F), null for bf16
+    int kind, f0, nu, nt;      // expert kind, first unit, units, tokens of the group (1..kGroupMax)
+    int gidx, grp, pad0, pad1; // call-wide segment index (its partial-sum slot), token group
+    int tok[kGroupMax];        // the group's token rows of x
 };
 
-// One decode CTA's static share: gate/up units [u_first, u_end) as segments, down rows [h0, h1).
+// One decode CTA's static share: its segments (in stream order) and the output quads it reduces.
 struct __align__(16) PlanCta {
-    int u_first, u_end, n1, n2, h0, h1, nseg, pad;
-    int seg_j[kSegPerCta], seg_f0[kSegPerCta], seg_fend[kSegPerCta], seg_ups[kSegPerCta];
-    int seg_stage[kSegPerCta + 1];
-    int pad2[3];
+    int nseg, nstage, q0, q1;          // segments, ring stages, output quads [q0, q1) of H/4
+    int seg_stage[kSegPerCta + 1];     // first ring stage of each segment
+    int pad[3];
+    Seg seg[kSegPerCta];
+};
+
+// Routing result and reduction tables of one call, read by every CTA after its segments.
+struct __align__(16) PlanShared {
+    int T, np, ngrp, nsegtot;
+    int gvs0[kMaxGroups], gvs1[kMaxGroups];  // segment range [gvs0, gvs1) of each token group
+    int pgrp[kDecodeMaxPairs];               // token group of pair p (pairs job-major)
+    int prow[kDecodeMaxPairs];               // row of pair p inside its group
+    float pw[kDecodeMaxPairs];               // routing weight of pair p
+    int tpn[kDecodeMaxT];                    // local pairs of token t
+    int tpair[kDecodeMaxT][kMaxTopK];        // token t's pairs in job order
+    int segrows[kMaxSegTotal];               // rows (tokens) of each segment's partial sums
 };
 
 struct __align__(16) DecodePlan {
     PlanShared sh;
     PlanCta cta[kPlanMaxGrid];
 };
+static_assert(sizeof(Seg) == 64, "Seg layout");
 static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0 && sizeof(DecodePlan) % 16 == 0,
               "plan structs are copied as int4");
 static_assert(alignof(PlanShared) == 16 && alignof(PlanCta) == 16, "plan structs are copied as int4");
@@ -57,8 +64,8 @@ struct PlanArgs {
     uint32_t* err;
     int T, E, K, H, F, scoring;
     int G;                 // decode grid size
-    uint32_t slot_bytes;
-    int rs_bf16, rs_q8;
+    int gmax;              // tokens per token group (<= kGroupMax)
+    int ups_bf16, ups_q8;  // units per ring stage of each kind
 };
 
 struct DecodeArgs {
@@ -67,28 +74,27 @@ struct DecodeArgs {
     uint32_t stamp;
     const uint16_t* x;     // [T, H] bf16
     float* out;            // [T, H] fp32
-    uint16_t* act;         // [kDecodeMaxPairs, F] bf16 scratch
-    uint32_t* ctr;         // [2, kDecodeMaxPairs] readiness counters (parity double-buffered)
+    float* part;           // [kMaxSegTotal, kGroupMax, H] fp32 partial sums, one block per segment
+    uint32_t* ctr;         // [2] grid-barrier counters (parity double-buffered)
     uint32_t* err;
     int T, E, K, H, F, scoring, accumulate;
     uint32_t epoch;        // call counter: selects the counter parity
     int NS;                // ring stages
-    int nwc;               // consumer warps that take ring stages round-robin
+    int ch;                // 256-element chunks per lane and row (H <= 2048 * ch)
+    int gmax;              // tokens per token group
+    int ups_bf16, ups_q8;  // units per ring stage of each kind
     uint32_t slot_bytes;   // bytes per ring stage
-    int rs_bf16, rs_q8;    // down rows per phase-2 stage
-    int act_resident;      // 1: all activations staged in shared memory at once; 0: two rolling slots
-    int x_f32;             // 1: x widened to fp32 in shared memory (small batches); 0: bf16 x
-    uint32_t off_ring, off_x, off_ybuf;  // dynamic shared-memory offsets
-    int hr_max;            // max output rows per CTA (ybuf row pitch)
+    uint32_t off_ring;     // dynamic shared-memory offset of the ring
     uint64_t timeout_ns;   // bound on every device-side wait
-    int inject_timeout;    // test hook: wait for a readiness count that never arrives
-    uint64_t* timeline;    // optional [grid][kTimelineSlots] per-CTA phase stamps (globaltimer ns), else null
-    int ns_cap;            // tuning: cap on ring stages (0 = as many as shared memory allows)
+    int inject_timeout;    // test hook: the grid barrier waits for one CTA more than the grid
+    uint64_t* timeline;    // optional [grid][kTimelineSlots] per-CTA stamps, else null
     uint64_t* stage_log;   // optional [3][kStageLogMax] issue / landed / released stamps of CTA 0's stages
+    int ns_cap;            // tuning: cap on ring stages (0 = as many as shared memory allows)
+    uint32_t stage_target; // tuning: target bytes per ring stage (0 = default)
 };
 
-// Host-side planning: shared-memory size and stage geometry for (T, H, F, K) on `grid` CTAs.
-// Returns false when the shape does not fit the fused kernel.
+// Host-side planning: shared-memory size and stage geometry for (T, H, F) on `grid` CTAs.
+// Returns false when the shape does not fit the fused path.
 bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes);
 
 // Both launches use programmatic dependent launch: the plan kernel (one CTA) runs beside the
@@ -97,6 +103,12 @@ cudaError_t launch_plan(const PlanArgs& p, cudaStream_t st);
 cudaError_t launch_decode(const DecodeArgs& a, int grid, size_t smem, cudaStream_t st);
 
 cudaError_t decode_set_smem_limit();
+// True when every decode kernel instantiation is launched with enough registers per thread for its
+// producer / consumer register split (otherwise the fused path must not be used).
+bool decode_register_split_fits();
 cudaError_t plan_set_smem_limit();
+
+// Partial-sum floats the decode path needs for hidden size H.
+inline size_t decode_part_floats(int H) { return (size_t)kMaxSegTotal * kGroupMax * H; }
 
 }  // namespace moe

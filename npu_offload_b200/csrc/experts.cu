@@ -11,7 +11,9 @@
 //   gateup_kernel   one warp per (job, f): streams gate row f and up row f once (128-bit no-allocate
 //                   loads), dots them with the job's tokens, writes act[pair, f] in bf16.
 //   down_kernel     one warp per (job, h): streams down row h once, dots with the job's activations,
-//                   writes y[pair, h] = w_pair * dot (fp32).
+//                   writes y[pair, h] = w_pair * dot (fp32).  For unit-layout tables (down columns
+//                   stored per f) down_unit_kernel computes the same y as a sum of columns scaled
+//                   by the activations, with each warp owning 256 consecutive h.
 //   combine_kernel  out[t, h] = sum of y over the token's pairs in job order.
 #include <algorithm>
 
@@ -200,6 +202,86 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(ExpertArgs a) {
     }
 }
 
+// y[p, h] = w_p * sum_f act[p, f] * down[h, f] for unit-layout tables: CTA = (job, block of 4
+// tokens, 2048 h); warp w owns h0 + 256w + 8*lane .. +8 and walks f in order, so every y is a
+// sequential fp32 sum over f.  The block's activation rows are staged in shared memory.
+constexpr int kDUTok = 4;
+constexpr int kDUH = kWarps * 256;
+__global__ void __launch_bounds__(kWarps * 32) down_unit_kernel(ExpertArgs a) {
+    extern __shared__ __align__(16) unsigned char dsm[];
+    uint16_t* sact = reinterpret_cast<uint16_t*>(dsm);  // [kDUTok][F]
+    const int nj = njobs_of(a);
+    const int H = a.H, F = a.F;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntb = (a.max_pairs + kDUTok - 1) / kDUTok, nhb = (H + kDUH - 1) / kDUH;
+    const long total = (long)nj * ntb * nhb;
+    for (long it = blockIdx.x; it < total; it += gridDim.x) {
+        const int j = (int)(it / ((long)ntb * nhb));
+        const int tb = (int)(it / nhb % ntb), hb = (int)(it % nhb);
+        const Job jb = a.jobs[j];
+        const int t0 = tb * kDUTok;
+        if (t0 >= jb.n) continue;  // uniform across the CTA
+        const int nt = min(kDUTok, jb.n - t0);
+        __syncthreads();  // previous item's readers are done with sact
+        for (int q = threadIdx.x; q < nt * F / 8; q += kWarps * 32) {
+            const int i = q / (F / 8), c = q % (F / 8);
+            reinterpret_cast<uint4*>(sact + (size_t)i * F)[c] =
+                __ldg(reinterpret_cast<const uint4*>(a.act + (size_t)(jb.p0 + t0 + i) * F) + c);
+        }
+        __syncthreads();
+        const int h = hb * kDUH + warp * 256 + lane * 8;
+        if (h >= H) continue;
+        const bool q8 = jb.ex.kind == kKindQ8;
+        const size_t pitch = unit_pitch(jb.ex.kind, H);
+        float acc[kDUTok][8];
+#pragma unroll
+        for (int i = 0; i < kDUTok; i++)
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[i][e] = 0.f;
+        if (!q8) {
+            const uint16_t* col = (const uint16_t*)jb.ex.w2 + h;
+#pragma unroll 4
+            for (int f = 0; f < F; f++) {
+                const uint4 d = ldg_stream(col + (size_t)f * pitch);
+                const float dv[8] = {bf_lo(d.x), bf_hi(d.x), bf_lo(d.y), bf_hi(d.y),
+                                     bf_lo(d.z), bf_hi(d.z), bf_lo(d.w), bf_hi(d.w)};
+#pragma unroll
+                for (int i = 0; i < kDUTok; i++) {
+                    const float av = bf2f(sact[(size_t)min(i, nt - 1) * F + f]);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) acc[i][e] = fmaf(av, dv[e], acc[i][e]);
+                }
+            }
+        } else {
+            const int8_t* col = (const int8_t*)jb.ex.w2 + h;
+#pragma unroll 4
+            for (int f = 0; f < F; f++) {
+                const uint2 d = __ldg(reinterpret_cast<const uint2*>(col + (size_t)f * pitch));
+                const float dv[8] = {i8f(d.x, 0), i8f(d.x, 1), i8f(d.x, 2), i8f(d.x, 3),
+                                     i8f(d.y, 0), i8f(d.y, 1), i8f(d.y, 2), i8f(d.y, 3)};
+#pragma unroll
+                for (int i = 0; i < kDUTok; i++) {
+                    const float av = bf2f(sact[(size_t)min(i, nt - 1) * F + f]);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) acc[i][e] = fmaf(av, dv[e], acc[i][e]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kDUTok; i++) {
+            if (i < nt) {
+                const int p = jb.p0 + t0 + i;
+                float o[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = q8 ? (a.pw[p] * acc[i][e]) * jb.ex.sc[2 * F + h + e] : a.pw[p] * acc[i][e];
+                float4* dst = reinterpret_cast<float4*>(a.y + (size_t)p * H + h);
+                dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+                dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) combine_kernel(ExpertArgs a) {
     const int t = blockIdx.y;
     const int h = (blockIdx.x * 256 + threadIdx.x) * 4;
@@ -228,7 +310,11 @@ cudaError_t launch_experts(const ExpertArgs& a, int sm_count, cudaStream_t st, i
         *launches += 1;
     }
     if (marks) cudaEventRecord(marks[0], st);
-    if (nj > 0) {
+    if (nj > 0 && a.unit_layout) {
+        const long items = (long)nj * ((a.max_pairs + kDUTok - 1) / kDUTok) * ((a.H + kDUH - 1) / kDUH);
+        down_unit_kernel<<<(int)std::min<long>(items, cap), kWarps * 32, (size_t)kDUTok * a.F * 2, st>>>(a);
+        *launches += 1;
+    } else if (nj > 0) {
         const long dn_units = (long)nj * (a.H / kWarps);
         down_kernel<<<(int)std::min<long>(dn_units, cap), kWarps * 32, 0, st>>>(a);
         *launches += 1;
@@ -241,38 +327,43 @@ cudaError_t launch_experts(const ExpertArgs& a, int sm_count, cudaStream_t st, i
     return cudaGetLastError();
 }
 
-// quant_row (cpu_kern.c:218-224) per row: one warp per row.  Input gate row f at g + f*gu_pitch,
-// up row f at u + f*gu_pitch, down row h at d + h*F; output gate row f at q + f*q_pitch, up row f at
-// q + f*q_pitch + q_up_off, down row h at q + q_down_off + h*F; scales / row sums in the reference's
-// row order (gate rows, up rows, down rows).
-__global__ void __launch_bounds__(256) quantize_q8_kernel(const uint16_t* g, const uint16_t* u, size_t gu_pitch,
-                                                          const uint16_t* d, int H, int F, int8_t* q, size_t q_pitch,
-                                                          size_t q_up_off, size_t q_down_off, float* sc, int32_t* rs) {
+// quant_row (cpu_kern.c:218-224) per row, one warp per row, in the reference's row order (F gate
+// rows, F up rows, H down rows).  Element i of row r is read at src(r) + i * in_step and written at
+// dst(r) + i * out_step, with the per-row bases and steps given by QuantGeom; scales / row sums go
+// to sc[r] / rs[r], and (unit layout) the gate/up scales of unit f also to the unit's trailer.
+__global__ void __launch_bounds__(256) quantize_q8_kernel(QuantGeom q, int H, int F, float* sc, int32_t* rs) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int rows = 2 * F + H;
     if (warp >= rows) return;
     const uint16_t* src;
     int8_t* dst;
+    size_t si, di;
     int n;
-    if (warp < F) {
-        src = g + (size_t)warp * gu_pitch; dst = q + (size_t)warp * q_pitch; n = H;
-    } else if (warp < 2 * F) {
-        src = u + (size_t)(warp - F) * gu_pitch; dst = q + (size_t)(warp - F) * q_pitch + q_up_off; n = H;
+    if (warp < 2 * F) {
+        const int f = warp < F ? warp : warp - F;
+        src = (warp < F ? q.g : q.u) + (size_t)f * q.gu_pitch;
+        dst = q.q + (size_t)f * q.q_pitch + (warp < F ? 0 : q.q_up_off);
+        si = di = 1;
+        n = H;
     } else {
         const int h = warp - 2 * F;
-        src = d + (size_t)h * F; dst = q + q_down_off + (size_t)h * F; n = F;
+        src = q.d + (size_t)h * q.d_row_step;
+        dst = q.q + q.q_down_off + (size_t)h * q.q_down_row_step;
+        si = q.d_elem_step;
+        di = q.q_down_elem_step;
+        n = F;
     }
     float m = 0.f;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, fabsf(bf2f(src[i])));
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, fabsf(bf2f(src[(size_t)i * si])));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float s = m > 0.f ? __fdiv_rn(m, 127.f) : 1.f;
     const float inv = __fdiv_rn(1.f, s);
     int sum = 0;
     for (int i = lane; i < n; i += 32) {
-        int v = __float2int_rn(__fmul_rn(bf2f(src[i]), inv));
+        int v = __float2int_rn(__fmul_rn(bf2f(src[(size_t)i * si]), inv));
         v = v > 127 ? 127 : (v < -127 ? -127 : v);
-        dst[i] = (int8_t)v;
+        dst[(size_t)i * di] = (int8_t)v;
         sum += v;
     }
 #pragma unroll
@@ -280,19 +371,82 @@ __global__ void __launch_bounds__(256) quantize_q8_kernel(const uint16_t* g, con
     if (lane == 0) {
         sc[warp] = s;
         if (rs) rs[warp] = sum;
+        if (q.trailer && warp < 2 * F) {  // unit trailer: sc_gate f, sc_up f, 0, 0
+            const int f = warp < F ? warp : warp - F;
+            float* t = reinterpret_cast<float*>(q.q + (size_t)f * q.q_pitch + 3 * (size_t)H);
+            t[warp < F ? 0 : 1] = s;
+            t[warp < F ? 2 : 3] = 0.f;
+        }
     }
 }
 
-cudaError_t launch_quantize_q8(const uint16_t* g, const uint16_t* u, const uint16_t* d, int H, int F, int8_t* q,
-                               float* sc, int32_t* rs, cudaStream_t st, int* launches, int interleaved) {
+cudaError_t launch_quantize_q8(const QuantGeom& q, int H, int F, float* sc, int32_t* rs, cudaStream_t st,
+                               int* launches) {
     const int rows = 2 * F + H;
+    quantize_q8_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(q, H, F, sc, rs);
+    *launches += 1;
+    return cudaGetLastError();
+}
+
+QuantGeom quant_geom_split(const uint16_t* g, const uint16_t* u, const uint16_t* d, int H, int F, int8_t* q) {
     const size_t FH = (size_t)F * H;
-    if (interleaved)
-        quantize_q8_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(g, u, 2 * (size_t)H, d, H, F, q, 2 * (size_t)H,
-                                                                    (size_t)H, 2 * FH, sc, rs);
+    QuantGeom r{};
+    r.g = g;
+    r.u = u;
+    r.d = d;
+    r.gu_pitch = H;
+    r.d_row_step = F;
+    r.d_elem_step = 1;
+    r.q = q;
+    r.q_pitch = H;
+    r.q_up_off = FH;
+    r.q_down_off = 2 * FH;
+    r.q_down_row_step = F;
+    r.q_down_elem_step = 1;
+    r.trailer = 0;
+    return r;
+}
+
+QuantGeom quant_geom_unit(const uint16_t* unit_bf16, int H, int F, int8_t* q_unit) {
+    const size_t pb = unit_pitch(kKindBF16, H), pq = unit_pitch(kKindQ8, H);
+    QuantGeom r{};
+    r.g = unit_bf16;
+    r.u = unit_bf16 + H;
+    r.d = unit_bf16 + 2 * (size_t)H;  // down row h = column h of the stored down columns
+    r.gu_pitch = pb;
+    r.d_row_step = 1;
+    r.d_elem_step = pb;
+    r.q = q_unit;
+    r.q_pitch = pq;
+    r.q_up_off = H;
+    r.q_down_off = 2 * (size_t)H;
+    r.q_down_row_step = 1;
+    r.q_down_elem_step = pq;
+    r.trailer = 1;
+    return r;
+}
+
+// dst[f * pitch + h] = src[h * F + f]: an [H, F] row-major down matrix into the down columns of a
+// unit table (32 x 32 tiles through shared memory, coalesced on both sides).
+template <class T>
+__global__ void __launch_bounds__(256) scatter_down_kernel(const T* src, T* dst, size_t pitch, int H, int F) {
+    __shared__ T tile[32][33];
+    const int f0 = blockIdx.x * 32, h0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int r = ty; r < 32; r += 8)
+        if (h0 + r < H && f0 + tx < F) tile[r][tx] = src[(size_t)(h0 + r) * F + f0 + tx];
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8)
+        if (f0 + r < F && h0 + tx < H) dst[(size_t)(f0 + r) * pitch + h0 + tx] = tile[tx][r];
+}
+
+cudaError_t launch_scatter_down(const void* src, void* dst, size_t pitch, int H, int F, int esize, cudaStream_t st,
+                                int* launches) {
+    const dim3 grid((F + 31) / 32, (H + 31) / 32);
+    if (esize == 2)
+        scatter_down_kernel<uint16_t><<<grid, 256, 0, st>>>((const uint16_t*)src, (uint16_t*)dst, pitch, H, F);
     else
-        quantize_q8_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(g, u, (size_t)H, d, H, F, q, (size_t)H, FH, 2 * FH,
-                                                                    sc, rs);
+        scatter_down_kernel<int8_t><<<grid, 256, 0, st>>>((const int8_t*)src, (int8_t*)dst, pitch, H, F);
     *launches += 1;
     return cudaGetLastError();
 }

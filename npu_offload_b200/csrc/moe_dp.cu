@@ -118,7 +118,8 @@ struct moe_ctx {
     int64_t launches = 0;
     uint32_t latched = 0;
     // fused decode kernel state
-    uint32_t* d_ctr = nullptr;  // [2 * kDecodeMaxPairs] readiness counters
+    uint32_t* d_ctr = nullptr;  // [2] grid-barrier counters of the fused decode kernel
+    float* d_part = nullptr;    // fused decode partial sums
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
     uint32_t epoch = 0;
@@ -127,7 +128,7 @@ struct moe_ctx {
     int inject_timeout = 0;
     uint64_t* d_timeline = nullptr;  // [sm_count][kTimelineSlots] when MOE_OPT_TIMELINE is on
     int ns_cap = 0;
-    int nwc = 0;  // fused kernel consumer warps (0: all)
+    uint32_t stage_target = 0;  // fused kernel bytes per ring stage (0: default)
     // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_ev;  // kProfMarks events per profiled call
@@ -164,6 +165,8 @@ int finish_sync(moe_ctx* c, cudaStream_t st) {
     CUDA_TRY(cudaStreamSynchronize(st));
     uint32_t bits = *c->h_err | c->latched;
     c->latched = 0;
+    // a fused call that gave up may leave its grid-arrival counter short of the grid: clear both
+    if ((bits & kErrTimeout) && c->d_ctr) CUDA_TRY(cudaMemset(c->d_ctr, 0, 2 * sizeof(uint32_t)));
     return map_err(bits);
 }
 
@@ -208,8 +211,36 @@ int upload_desc(moe_ctx* c, int layer, int expert, const ExpDesc& d) {
     return MOE_OK;
 }
 
+// int8 unit tables: F units of 3H + 16 bytes, then the [2F + H] fp32 scales.
 size_t q8_scale_off(const moe_ctx* c) {
-    return align_up((size_t)3 * c->cfg.inter * c->cfg.hidden, 256);
+    return align_up((size_t)c->cfg.inter * unit_pitch(kKindQ8, c->cfg.hidden), 256);
+}
+
+// Scatters a row-major [H, F] down matrix (device or host memory) into the down columns of the
+// unit table at dst (pitch in elements of esize bytes).  Host sources go through a temporary
+// device buffer.
+int load_down_columns(moe_ctx* c, void* dst, const void* src, size_t pitch, int esize, bool host) {
+    const size_t H = c->cfg.hidden, F = c->cfg.inter, bytes = F * H * esize;
+    void* tmp = nullptr;
+    if (host) {
+        if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MOE_ENOMEM, "down-matrix staging (%zu bytes)", bytes);
+        }
+        cudaError_t e = cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, 0);
+        if (e != cudaSuccess) {
+            cudaFree(tmp);
+            return fail(MOE_ECUDA, "down-matrix copy: %s", cudaGetErrorString(e));
+        }
+        src = tmp;
+    }
+    int n = 0;
+    cudaError_t e = launch_scatter_down(src, dst, pitch, (int)H, (int)F, esize, 0, &n);
+    c->launches += n;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+    if (tmp) cudaFree(tmp);
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "down-matrix scatter: %s", cudaGetErrorString(e));
+    return MOE_OK;
 }
 
 // Copies n bytes into device memory dst from src (host when host != 0).
@@ -297,11 +328,12 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
-    if (!st) st = dalloc(&c->d_ctr, 2 * (size_t)kDecodeMaxPairs);
+    if (!st) st = dalloc(&c->d_ctr, 2);
+    if (!st) st = dalloc(&c->d_part, decode_part_floats(k.hidden));
     if (!st) st = dalloc(&c->d_plan, 2);
     if (!st) st = dalloc(&c->d_plan_flag, 2);
     if (!st && cudaMemset(c->d_plan_flag, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
-    if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 2 * kDecodeMaxPairs) != cudaSuccess)
+    if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 2) != cudaSuccess)
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && (cudaEventCreateWithFlags(&c->in_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
@@ -320,6 +352,7 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
         cudaError_t e = decode_set_smem_limit();
         if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
     }
+    if (!st && !decode_register_split_fits()) c->fused = false;  // this build cannot run the fused kernel
     if (!st) {
         cudaError_t e = route_set_smem_limits();
         if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
@@ -341,7 +374,7 @@ int moe_destroy(moe_ctx* c) {
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
                   c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
                   c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
-                  c->d_plan_flag};
+                  c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
     if (c->h_err) cudaFreeHost(c->h_err);
     for (cudaEvent_t ev : c->prof_ev) cudaEventDestroy(ev);
@@ -360,15 +393,15 @@ int moe_load_expert_bf16(moe_ctx* c, int layer, int expert, const uint16_t* gate
     if (!gate || !up || !down) return fail(MOE_EINVAL, "null weight pointer");
     DeviceGuard dg(c->dev);
     if ((st = ensure_arena(c, layer))) return st;
-    const size_t H = c->cfg.hidden, F = c->cfg.inter, FH = F * H;
+    const size_t H = c->cfg.hidden, F = c->cfg.inter, P = unit_pitch(kKindBF16, (int)H);
     char* base = slot_ptr(c, layer, expert);
-    const cudaMemcpyKind kind = (flags & MOE_F_HOST) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
-    // stored interleaved: gate row f and up row f adjacent ([F][gate|up]), then the down rows
-    CUDA_TRY(cudaMemcpy2DAsync(base, 4 * H, gate, 2 * H, 2 * H, F, kind, 0));
-    CUDA_TRY(cudaMemcpy2DAsync(base + 2 * H, 4 * H, up, 2 * H, 2 * H, F, kind, 0));
-    if ((st = copy_in(base + FH * 4, down, FH * 2, (flags & MOE_F_HOST) != 0, 0))) return st;
-    CUDA_TRY(cudaStreamSynchronize(0));
-    return upload_desc(c, layer, expert, ExpDesc{base, base + FH * 4, nullptr, kKindBF16, kLayoutInterleaved});
+    const bool host = flags & MOE_F_HOST;
+    const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    // unit table: [gate row f | up row f | down column f] per f
+    CUDA_TRY(cudaMemcpy2DAsync(base, 2 * P, gate, 2 * H, 2 * H, F, kind, 0));
+    CUDA_TRY(cudaMemcpy2DAsync(base + 2 * H, 2 * P, up, 2 * H, 2 * H, F, kind, 0));
+    if ((st = load_down_columns(c, base + 4 * H, down, P, 2, host))) return st;
+    return upload_desc(c, layer, expert, ExpDesc{base, base + 4 * H, nullptr, kKindBF16, kLayoutUnit});
 }
 
 int moe_load_expert_q8(moe_ctx* c, int layer, int expert, const int8_t* q, const float* scales, int flags) {
@@ -377,18 +410,20 @@ int moe_load_expert_q8(moe_ctx* c, int layer, int expert, const int8_t* q, const
     if (!q || !scales) return fail(MOE_EINVAL, "null weight pointer");
     DeviceGuard dg(c->dev);
     if ((st = ensure_arena(c, layer))) return st;
-    const size_t H = c->cfg.hidden, F = c->cfg.inter;
+    const size_t H = c->cfg.hidden, F = c->cfg.inter, P = unit_pitch(kKindQ8, (int)H);
     char* base = slot_ptr(c, layer, expert);
     const bool host = flags & MOE_F_HOST;
     const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
-    // reference layout [F gate][F up][H down] rows -> interleaved [F][gate|up], then down rows
-    CUDA_TRY(cudaMemcpy2DAsync(base, 2 * H, q, H, H, F, kind, 0));
-    CUDA_TRY(cudaMemcpy2DAsync(base + H, 2 * H, q + F * H, H, H, F, kind, 0));
-    if ((st = copy_in(base + 2 * F * H, q + 2 * F * H, F * H, host, 0))) return st;
+    // reference layout [F gate][F up][H down] rows -> unit table [gate | up | down column | sc_g, sc_u, 0, 0]
+    CUDA_TRY(cudaMemcpy2DAsync(base, P, q, H, H, F, kind, 0));
+    CUDA_TRY(cudaMemcpy2DAsync(base + H, P, q + F * H, H, H, F, kind, 0));
+    CUDA_TRY(cudaMemcpy2DAsync(base + 3 * H, P, scales, 4, 4, F, kind, 0));
+    CUDA_TRY(cudaMemcpy2DAsync(base + 3 * H + 4, P, scales + F, 4, 4, F, kind, 0));
+    CUDA_TRY(cudaMemset2DAsync(base + 3 * H + 8, P, 0, 8, F, 0));
     if ((st = copy_in(base + q8_scale_off(c), scales, (2 * F + H) * 4, host, 0))) return st;
-    CUDA_TRY(cudaStreamSynchronize(0));
+    if ((st = load_down_columns(c, base + 2 * H, q + 2 * F * H, P, 1, host))) return st;
     return upload_desc(c, layer, expert,
-                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutInterleaved});
+                       ExpDesc{base, base + 2 * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutUnit});
 }
 
 int moe_quantize_expert_q8(moe_ctx* c, int layer, int expert) {
@@ -406,16 +441,16 @@ int moe_quantize_expert_q8(moe_ctx* c, int layer, int expert) {
         return fail(MOE_ENOMEM, "quantisation scratch");
     }
     int n = 0;
-    // the bf16 table is interleaved; quantise into the same interleaved int8 layout
-    cudaError_t e = launch_quantize_q8((const uint16_t*)base, (const uint16_t*)base + H, (const uint16_t*)(base + F * H * 4),
-                                       (int)H, (int)F, (int8_t*)tmp, (float*)(tmp + q8_scale_off(c)), nullptr, 0, &n, 1);
+    // bf16 unit table in, int8 unit table (with per-unit scale trailers) out
+    cudaError_t e = launch_quantize_q8(quant_geom_unit((const uint16_t*)base, (int)H, (int)F, (int8_t*)tmp), (int)H,
+                                       (int)F, (float*)(tmp + q8_scale_off(c)), nullptr, 0, &n);
     c->launches += n;
     if (e == cudaSuccess) e = cudaMemcpyAsync(base, tmp, bytes, cudaMemcpyDeviceToDevice, 0);
     if (e == cudaSuccess) e = cudaStreamSynchronize(0);
     cudaFree(tmp);
     if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise: %s", cudaGetErrorString(e));
     return upload_desc(c, layer, expert,
-                       ExpDesc{base, base + 2 * F * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutInterleaved});
+                       ExpDesc{base, base + 2 * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutUnit});
 }
 
 int moe_expert_kind(moe_ctx* c, int layer, int expert) {
@@ -518,7 +553,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
     if (T > 0 && c->fused && dgrid >= 1) {
         da.x = x;
         da.out = o;
-        da.act = c->d_act;
+        da.part = c->d_part;
         da.ctr = c->d_ctr;
         da.err = c->d_err;
         da.T = T;
@@ -533,7 +568,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         da.timeline = c->d_timeline;
         da.stage_log = c->d_timeline ? reinterpret_cast<uint64_t*>(c->d_timeline + (size_t)c->sm_count * kTimelineSlots) : nullptr;
         da.ns_cap = c->ns_cap;
-        da.nwc = c->nwc;
+        da.stage_target = c->stage_target;
         use_fused = plan_decode(da, dgrid, &dsmem);
     }
     if (use_fused) {
@@ -555,9 +590,9 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         pa.F = c->cfg.inter;
         pa.scoring = c->cfg.scoring;
         pa.G = dgrid;
-        pa.slot_bytes = da.slot_bytes;
-        pa.rs_bf16 = da.rs_bf16;
-        pa.rs_q8 = da.rs_q8;
+        pa.gmax = da.gmax;
+        pa.ups_bf16 = da.ups_bf16;
+        pa.ups_q8 = da.ups_q8;
         cudaError_t e = launch_plan(pa, st);
         if (e != cudaSuccess) return fail(MOE_ECUDA, "plan launch: %s", cudaGetErrorString(e));
         if (marks) cudaEventRecord(marks[1], st);
@@ -596,6 +631,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         ea.out = o;
         ea.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
         ea.err = c->d_err;
+        ea.unit_layout = 1;  // context tables
         e = launch_experts(ea, c->sm_count, st, &n, marks ? marks + 2 : nullptr);
         c->launches += n;
         if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
@@ -832,7 +868,7 @@ int moe_place_expert_q8(moe_ctx* c, const uint16_t* g, const uint16_t* u, const 
     const size_t H = c->cfg.hidden, F = c->cfg.inter, FH = F * H, R = 2 * F + H;
     int n = 0;
     if (!(flags & MOE_F_HOST)) {
-        cudaError_t e = launch_quantize_q8(g, u, d, (int)H, (int)F, q, sc, rs, st, &n, 0);
+        cudaError_t e = launch_quantize_q8(quant_geom_split(g, u, d, (int)H, (int)F, q), (int)H, (int)F, sc, rs, st, &n);
         c->launches += n;
         if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise launch: %s", cudaGetErrorString(e));
         if (flags & MOE_F_SYNC) return finish_sync(c, st);
@@ -851,7 +887,9 @@ int moe_place_expert_q8(moe_ctx* c, const uint16_t* g, const uint16_t* u, const 
     cudaError_t e = cudaMemcpyAsync(dg_, g, FH * 2, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(dg_ + FH, u, FH * 2, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(dg_ + 2 * FH, d, FH * 2, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = launch_quantize_q8(dg_, dg_ + FH, dg_ + 2 * FH, (int)H, (int)F, dq, dsc, drs, st, &n, 0);
+    if (e == cudaSuccess)
+        e = launch_quantize_q8(quant_geom_split(dg_, dg_ + FH, dg_ + 2 * FH, (int)H, (int)F, dq), (int)H, (int)F, dsc,
+                               drs, st, &n);
     c->launches += n;
     if (e == cudaSuccess) e = cudaMemcpyAsync(q, dq, 3 * FH, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(sc, dsc, R * 4, cudaMemcpyDeviceToHost, st);
@@ -887,9 +925,9 @@ int moe_set_option(moe_ctx* c, int option, int64_t value) {
             if (value < 0 || value > 16) return fail(MOE_EINVAL, "ring stages %lld not in [0,16]", (long long)value);
             c->ns_cap = (int)value;
             return MOE_OK;
-        case MOE_OPT_CONSUMER_WARPS:
-            if (value < 0 || value > 8) return fail(MOE_EINVAL, "consumer warps %lld not in [0,8]", (long long)value);
-            c->nwc = (int)value;
+        case MOE_OPT_STAGE_BYTES:
+            if (value < 0 || value > 196608) return fail(MOE_EINVAL, "stage bytes %lld not in [0,196608]", (long long)value);
+            c->stage_target = (uint32_t)value;
             return MOE_OK;
         case MOE_OPT_TIMELINE: {
             DeviceGuard dg(c->dev);

@@ -1,11 +1,20 @@
 // Plan kernel of the fused decode path: one CTA computes everything the decode grid needs before it
-// can stream weights -- routing (route_core.cuh), the token->expert grouping in first-appearance
-// order (solar_hybrid/runtime.py:343-354), the local job list, and every decode CTA's byte-balanced
-// share -- into a global plan, then publishes it with a release flag.
+// can stream weights, and publishes it with a release flag:
+//   routing      route_core.cuh, one warp per token
+//   grouping     local expert jobs in first-appearance order of the flattened top-k list
+//                (solar_hybrid/runtime.py:343-354), each job's pairs in token order
+//   token groups each job's pairs split into groups of at most gmax tokens; a group is one pass
+//                over the job's unit table (F units: gate row f, up row f, down column f)
+//   partition    the unit stream (all groups' units, in group order) cut into G byte-balanced
+//                contiguous shares at unit boundaries; a share is a list of segments (runs of one
+//                group's units), numbered call-wide in stream order -- the numbering fixes where
+//                each segment's partial sums go and the order in which they are added up
+//   reduction    per pair: its group and row; per group: its segment range; per token: its pairs
+//                in job order
 //
-// It is launched with programmatic dependent launch right after the previous decode grid triggers,
-// and runs on the one SM that decode grid leaves free, so for back-to-back layers the plan of layer
-// l+1 is ready while layer l still streams.  Before exiting it waits for its predecessor grid, which
+// It is launched with programmatic dependent launch right after the previous decode grid triggers
+// and runs on the one SM that grid leaves free, so for back-to-back layers the plan of layer l+1
+// is ready while layer l still streams.  Before exiting it waits for its predecessor grid, which
 // makes "plan(l) complete" imply "decode(l-1) complete" for the decode grid that depends on it.
 #include <climits>
 #include <cstddef>
@@ -18,6 +27,7 @@
 namespace moe {
 
 constexpr int kPlanThreads = kDecodeMaxT * 32;  // one warp per token
+constexpr int kPlanJobs = kDecodeMaxPairs;      // local jobs <= pairs
 
 struct PlanSmem {
     int idx[kDecodeMaxT][kMaxTopK];
@@ -27,9 +37,17 @@ struct PlanSmem {
     uint32_t tokmask[kMaxExperts];
     int jmap[kMaxExperts];
     int pos2e[kDecodeMaxPairs];
-    long long cum1[kDecodePlanJobs + 1];  // gate/up bytes of jobs < j
-    long long P1, R;
-    int nbf, nq8;
+    int ptok[kDecodeMaxPairs];            // token of pair p (job-major)
+    int jkind[kPlanJobs];
+    int jp0[kPlanJobs + 1];               // pair offsets
+    int jg0[kPlanJobs + 1];               // group offsets
+    const unsigned char* jw1[kPlanJobs];  // unit 0 of the job's table
+    const float* jsc[kPlanJobs];
+    int gjob[kMaxGroups];
+    long long gcum[kMaxGroups + 1];       // unit-stream bytes of groups < g
+    int cta_nseg[kPlanMaxGrid];
+    int cta_seg0[kPlanMaxGrid + 1];
+    int nj, np, ngrp, pad;
     PlanShared sh;
 };
 static_assert(offsetof(PlanSmem, sh) % 16 == 0, "int4 copies from PlanSmem::sh");
@@ -39,10 +57,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     PlanSmem& m = *reinterpret_cast<PlanSmem*>(dyn);
     float* scr = reinterpret_cast<float*>(dyn + ((sizeof(PlanSmem) + 15) / 16) * 16);  // [warps][2*kMaxExperts]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int T = a.T, E = a.E, K = a.K, H = a.H, F = a.F, G = a.G;
+    const int T = a.T, E = a.E, K = a.K, H = a.H, F = a.F, G = a.G, GM = a.gmax;
     const int NP = T * K;
 
-    // routing: one warp per token
+    // ---- routing: one warp per token ----
     if (warp < T) {
         const bool bad = route_token(a.logits + (size_t)warp * E, a.bias, E, K, a.scoring, m.idx[warp], m.w[warp],
                                      scr + warp * 2 * kMaxExperts);
@@ -55,6 +73,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
         m.jmap[e] = -1;
     }
     for (int q = tid; q < NP; q += kPlanThreads) m.pos2e[q] = -1;
+    for (int g = tid; g < kMaxGroups; g += kPlanThreads) m.sh.gvs0[g] = m.sh.gvs1[g] = 0;
+    for (int k = tid; k < kMaxSegTotal; k += kPlanThreads) m.sh.segrows[k] = 0;
     __syncthreads();
     for (int q = tid; q < NP; q += kPlanThreads) {
         const int t = q / K, k = q % K, e = m.idx[t][k];
@@ -68,9 +88,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     for (int e = tid; e < E; e += kPlanThreads)
         if (m.counts[e] > 0) m.pos2e[m.firstpos[e]] = e;
     __syncthreads();
-    if (warp == 0) {  // local jobs in first-appearance order, pair offsets, gate/up byte prefix
-        int nj = 0, np = 0, nbf = 0, nq8 = 0;
-        long long cum = 0, R = 0;
+
+    // ---- local jobs in first-appearance order: pair and group offsets ----
+    if (warp == 0) {
+        int nj = 0, np = 0, ng = 0;
         for (int q0 = 0; q0 < NP; q0 += 32) {
             const int q = q0 + lane;
             const int e = q < NP ? m.pos2e[q] : -1;
@@ -79,62 +100,51 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
             if (e >= 0 && kind == kKindNone) atomicOr(a.err, kErrBadExpert);
             const unsigned msk = __ballot_sync(0xffffffffu, local);
             const int n = local ? m.counts[e] : 0;
-            const long long ub = local ? 2LL * H * (kind == kKindBF16 ? 2 : 1) * F : 0;
-            int incl = n;
-            long long cincl = ub;
+            const int ngj = (n + GM - 1) / GM;
+            int incl = n, gincl = ngj;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                const long long cy = __shfl_up_sync(0xffffffffu, cincl, o);
+                const int gy = __shfl_up_sync(0xffffffffu, gincl, o);
                 if (lane >= o) {
                     incl += y;
-                    cincl += cy;
+                    gincl += gy;
                 }
             }
             if (local) {
                 const int j = nj + __popc(msk & ((1u << lane) - 1u));
-                if (j < kDecodePlanJobs) {
-                    const ExpDesc d = a.desc[e];
-                    m.sh.jexp[j] = e;
-                    m.sh.jkind[j] = kind;
-                    m.sh.jlayout[j] = d.layout;
-                    m.sh.jw1[j] = static_cast<const unsigned char*>(d.w1);
-                    m.sh.jw2[j] = static_cast<const unsigned char*>(d.w2);
-                    m.sh.jsc[j] = d.sc;
-                    m.sh.jp0[j] = np + incl - n;
-                    m.cum1[j] = cum + cincl - ub;
-                    m.jmap[e] = j;
-                }
+                const ExpDesc d = a.desc[e];
+                m.jkind[j] = kind;
+                m.jw1[j] = static_cast<const unsigned char*>(d.w1);
+                m.jsc[j] = d.sc;
+                m.jp0[j] = np + incl - n;
+                m.jg0[j] = ng + gincl - ngj;
+                m.jmap[e] = j;
             }
-            nbf += __popc(__ballot_sync(0xffffffffu, local && kind == kKindBF16));
-            nq8 += __popc(__ballot_sync(0xffffffffu, local && kind == kKindQ8));
-            R += __shfl_sync(0xffffffffu, cincl, 31) / (2LL * H);
             nj += __popc(msk);
             np += __shfl_sync(0xffffffffu, incl, 31);
-            cum += __shfl_sync(0xffffffffu, cincl, 31);
+            ng += __shfl_sync(0xffffffffu, gincl, 31);
         }
         if (lane == 0) {
-            if (nj > kDecodePlanJobs) {  // the host checks min(E, T*K) <= kDecodePlanJobs; never expected
-                atomicOr(a.err, kErrBadIndex);
-                nj = kDecodePlanJobs;
-            }
-            m.sh.nj = nj;
-            m.sh.np = np;
-            m.sh.T = T;
-            m.sh.jp0[nj] = np;
-            m.cum1[nj] = cum;
-            m.P1 = cum;
-            m.R = R;
-            m.nbf = nbf;
-            m.nq8 = nq8;
+            m.nj = nj;
+            m.np = np;
+            m.ngrp = ng;
+            m.jp0[nj] = np;
+            m.jg0[nj] = ng;
         }
     }
     __syncthreads();
+    const int nj = m.nj, np = m.np, ngrp = m.ngrp;
+
+    // ---- pairs (job-major, tokens in order inside a job), token -> pairs, group -> job ----
     for (int q = tid; q < NP; q += kPlanThreads) {
         const int t = q / K, k = q % K, e = m.idx[t][k], j = m.jmap[e];
         if (j >= 0) {
-            const int p = m.sh.jp0[j] + __popc(m.tokmask[e] & ((1u << t) - 1u));
-            m.sh.ptok[p] = t;
+            const int r = __popc(m.tokmask[e] & ((1u << t) - 1u));  // rank of t among the job's tokens
+            const int p = m.jp0[j] + r;
+            m.ptok[p] = t;
+            m.sh.pgrp[p] = m.jg0[j] + r / GM;
+            m.sh.prow[p] = r % GM;
             m.sh.pw[p] = m.w[t][k];
             int slot = 0;
             for (int k2 = 0; k2 < K; k2++) {
@@ -149,70 +159,122 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
         for (int k = 0; k < K; k++) n += m.jmap[m.idx[t][k]] >= 0;
         m.sh.tpn[t] = n;
     }
+    for (int j = tid; j < nj; j += kPlanThreads)
+        for (int g = m.jg0[j]; g < m.jg0[j + 1]; g++) m.gjob[g] = j;
     __syncthreads();
-    // publish the shared part
+
+    // ---- unit-stream byte prefix over groups (warp 0) ----
+    if (warp == 0) {
+        long long run = 0;
+        for (int g0 = 0; g0 < ngrp; g0 += 32) {
+            const int g = g0 + lane;
+            const long long b = g < ngrp ? (long long)F * (long long)unit_bytes(m.jkind[m.gjob[g]], H) : 0;
+            long long incl = b;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (g < ngrp) m.gcum[g] = run + incl - b;
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) m.gcum[ngrp] = run;
+    }
+    __syncthreads();
+
+    // ---- partition: CTA ss owns units [U(ss), U(ss+1)) of the stream ----
+    const long long total = m.gcum[ngrp];
+    const double per = (double)total / G;
+    auto unit_at = [&](int ss) -> int {  // first unit starting at or after byte ss * total / G
+        if (ss >= G) return ngrp * F;
+        const long long B = (long long)(ss * per);
+        if (B >= total) return ngrp * F;
+        int lo = 0, hi = ngrp - 1;  // group g with gcum[g] <= B < gcum[g+1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (m.gcum[mid] <= B) lo = mid;
+            else hi = mid - 1;
+        }
+        const long long ub = (m.gcum[lo + 1] - m.gcum[lo]) / F;
+        return lo * F + (int)((B - m.gcum[lo] + ub - 1) / ub);
+    };
+    for (int ss = tid; ss < G; ss += kPlanThreads) {
+        const int uf = unit_at(ss), ue = unit_at(ss + 1);
+        m.cta_nseg[ss] = ue > uf ? (ue - 1) / F - uf / F + 1 : 0;
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of segment counts -> call-wide segment numbers
+        int run = 0;
+        for (int s0 = 0; s0 < G; s0 += 32) {
+            const int ss = s0 + lane;
+            const int v = ss < G ? m.cta_nseg[ss] : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (ss < G) m.cta_seg0[ss] = run + incl - v;
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) m.cta_seg0[G] = run;
+    }
+    __syncthreads();
+    const int H4 = H / 4;
+    for (int ss = tid; ss < G; ss += kPlanThreads) {
+        PlanCta* pc = &a.plan->cta[ss];
+        const int uf = unit_at(ss), ue = unit_at(ss + 1);
+        int nseg = m.cta_nseg[ss];
+        if (nseg > kSegPerCta) {  // never expected: a share spans at most groups/G + 2 groups
+            atomicOr(a.err, kErrBadIndex);
+            nseg = kSegPerCta;
+        }
+        int stage = 0;
+        for (int k = 0; k < nseg; k++) {
+            const int g = uf / F + k, j = m.gjob[g], kind = m.jkind[j];
+            const int f0 = k == 0 ? uf % F : 0;
+            const int fend = g == (ue - 1) / F ? (ue - 1) % F + 1 : F;
+            const int r0 = (g - m.jg0[j]) * GM;  // first pair rank of the group
+            const int nt = min(GM, m.jp0[j + 1] - m.jp0[j] - r0);
+            const int gidx = m.cta_seg0[ss] + k;
+            Seg sg;
+            sg.src = m.jw1[j] + (size_t)f0 * unit_bytes(kind, H);
+            sg.sc = kind == kKindQ8 ? m.jsc[j] : nullptr;
+            sg.kind = kind;
+            sg.f0 = f0;
+            sg.nu = fend - f0;
+            sg.nt = nt;
+            sg.gidx = gidx;
+            sg.grp = g;
+            sg.pad0 = sg.pad1 = 0;
+#pragma unroll
+            for (int i = 0; i < kGroupMax; i++) sg.tok[i] = m.ptok[m.jp0[j] + r0 + min(i, nt - 1)];
+            pc->seg[k] = sg;
+            pc->seg_stage[k] = stage;
+            const int ups = kind == kKindQ8 ? a.ups_q8 : a.ups_bf16;
+            stage += (sg.nu + ups - 1) / ups;
+            if (gidx < kMaxSegTotal) m.sh.segrows[gidx] = nt;
+            if (f0 == 0) m.sh.gvs0[g] = gidx;
+            if (fend == F) m.sh.gvs1[g] = gidx + 1;
+        }
+        pc->seg_stage[nseg] = stage;
+        pc->nseg = nseg;
+        pc->nstage = stage;
+        pc->q0 = (int)((long long)ss * H4 / G);
+        pc->q1 = (int)((long long)(ss + 1) * H4 / G);
+    }
+    if (tid == 0) {
+        m.sh.T = T;
+        m.sh.np = np;
+        m.sh.ngrp = ngrp;
+        m.sh.nsegtot = m.cta_seg0[G];
+        if (m.cta_seg0[G] > kMaxSegTotal) atomicOr(a.err, kErrBadIndex);  // the host bounds it; never expected
+    }
+    __syncthreads();
     {
         const int4* src = reinterpret_cast<const int4*>(&m.sh);
         int4* dst = reinterpret_cast<int4*>(&a.plan->sh);
         for (int q = tid; q < (int)(sizeof(PlanShared) / 16); q += kPlanThreads) dst[q] = src[q];
-    }
-    // every decode CTA's share: CTA ss starts at byte ss*total/G of the weight stream minus the down
-    // rows of CTAs < ss (down rows split evenly by h); one thread per CTA, all evaluating the same
-    // expressions, so neighbouring CTAs agree on their shared boundary
-    const int nj = m.sh.nj;
-    const long long P1 = m.P1, R = m.R, total = P1 + (long long)H * R;
-    const double per = (double)total / G;
-    auto bound = [&](int ss) -> long long {
-        if (ss >= G) return P1;
-        const long long hh = (long long)ss * H / G;
-        const long long b = (long long)(ss * per) - hh * R;
-        return b < 0 ? 0 : (b > P1 ? P1 : b);
-    };
-    auto unit_at = [&](long long B) -> int {  // first unit starting at or after byte B of the gate/up stream
-        if (B >= P1) return nj * F;
-        int lo = 0, hi = nj - 1;  // job j with cum1[j] <= B < cum1[j+1]
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (m.cum1[mid] <= B) lo = mid;
-            else hi = mid - 1;
-        }
-        const long long ub = 2LL * H * (m.sh.jkind[lo] == kKindBF16 ? 2 : 1);
-        return lo * F + (int)((double)(B - m.cum1[lo] + ub - 1) / (double)ub);
-    };
-    for (int ss = tid; ss < G; ss += kPlanThreads) {
-        PlanCta pc;
-        const int uf = unit_at(bound(ss)), ue0 = unit_at(bound(ss + 1));
-        const int ue = ue0 > uf ? ue0 : uf;
-        pc.u_first = uf;
-        pc.u_end = ue;
-        int n1 = 0, ns = 0;
-        for (int u = uf; u < ue;) {
-            const int j = u / F, seg_end = min(ue, (j + 1) * F);
-            int ups = 1;
-            if (m.sh.jlayout[j] == kLayoutInterleaved)
-                ups = max(1, (int)(a.slot_bytes / (2u * H * (m.sh.jkind[j] == kKindBF16 ? 2u : 1u))));
-            if (ns == kSegPerCta) {  // never expected: nj / G + 2 segments per CTA at most
-                atomicOr(a.err, kErrBadIndex);
-                break;
-            }
-            pc.seg_j[ns] = j;
-            pc.seg_f0[ns] = u - j * F;
-            pc.seg_fend[ns] = seg_end - j * F;
-            pc.seg_ups[ns] = ups;
-            pc.seg_stage[ns] = n1;
-            n1 += (seg_end - u + ups - 1) / ups;
-            ns++;
-            u = seg_end;
-        }
-        pc.seg_stage[ns] = n1;
-        pc.nseg = ns;
-        pc.n1 = n1;
-        pc.h0 = (int)((long long)ss * H / G);
-        pc.h1 = (int)((long long)(ss + 1) * H / G);
-        const int hr = pc.h1 - pc.h0;
-        pc.n2 = hr > 0 ? m.nbf * ((hr + a.rs_bf16 - 1) / a.rs_bf16) + m.nq8 * ((hr + a.rs_q8 - 1) / a.rs_q8) : 0;
-        pc.pad = 0;
-        a.plan->cta[ss] = pc;
     }
     __syncthreads();
     if (tid == 0) {
