@@ -36,13 +36,13 @@ sys.path.insert(0, ROOT)
 
 H, F, E, K = 4096, 1280, 128, 8
 EXPERT_BYTES = 3 * H * F * 2          # 31,457,280 B per bf16 expert
-GATEUP_BYTES = 2 * H * F * 2          # gate + up rows, read by the gate/up kernel
 DOWN_BYTES = H * F * 2
 METRIC = "MoE-layer decode tokens/s and achieved HBM GB/s vs peak"
 UNIT = "MoE-layer tokens/s"
-# DRAM bytes per algorithmic byte of the gate/up kernel from the committed ncu capture
-# (profiles/gateup_kernel_decode.md); None until a capture exists.
-TRAFFIC_RATIO = None
+# DRAM bytes (read + write) per algorithmic byte of decode_kernel, from the committed ncu capture of
+# one T=1 layer (profiles/decode_kernel_T1.md); None until a capture exists.
+TRAFFIC_RATIO = 255.278 / 251.658
+TRAFFIC_SOURCE = "profiles/decode_kernel_T1.md"
 
 
 def parse():
@@ -429,30 +429,26 @@ def our_arm(args):
     with ClockSampler(device.index) as clk:
         ms, launches, _ = timed(stack, args.steps, args.warmup, ws, profile=False)
     ms_max = max_over_ranks(ms, ws)
-    # the same K steps again with per-stage CUDA events on the launching stream (roofline)
-    ms_prof, _, stage = timed(stack, args.steps, args.warmup, ws, profile=True)
     step_ms = ms_max / args.steps
     value = T * L * args.steps / (ms_max / 1e3)
 
-    # roofline of the dominant kernel (gate/up+SwiGLU): algorithmic bytes / its event-timed duration
+    # Roofline of the dominant kernel (decode_kernel, one launch per layer): algorithmic bytes per
+    # launch = this rank's distinct routed experts x their gate/up/down bytes; launch duration = the
+    # timed region / decode launches (the plan kernel of the next layer runs on the SM the decode
+    # grid leaves free, overlapped; no events between launches, which would break that overlap).
     R = stack.R
     reps = [(args.warmup + s) % R for s in range(args.steps)]
-    u_tot = sum(stack.ucount[r].sum() for r in reps)
-    gu_bytes = u_tot * GATEUP_BYTES
-    all_bytes = u_tot * EXPERT_BYTES
-    n_launch_gu = args.steps * L
-    route_ms, gu_ms, dn_ms, cb_ms = stage
-    achieved = gu_bytes / (gu_ms / 1e3) / 1e9 if gu_ms > 0 else 0.0
-    roof = {"bound": "hbm", "kernel": "gateup_kernel", "achieved": achieved, "peak": peak, "unit": "GB/s",
+    n_dec = args.steps * L
+    all_bytes = sum(stack.ucount[r].sum() for r in reps) * EXPERT_BYTES
+    bpl = all_bytes / n_dec
+    dur_s = ms / 1e3 / n_dec
+    achieved = bpl / dur_s / 1e9
+    roof = {"bound": "hbm", "kernel": "decode_kernel", "achieved": achieved, "peak": peak, "unit": "GB/s",
             "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-            "traffic": (TRAFFIC_RATIO * gu_bytes / n_launch_gu) if TRAFFIC_RATIO else None,
-            "algorithmic_bytes_per_launch": gu_bytes / n_launch_gu,
-            "layer": {"achieved": all_bytes / (ms / 1e3) / 1e9, "frac": all_bytes / (ms / 1e3) / 1e9 / peak,
-                      "bytes_per_layer": all_bytes / n_launch_gu},
-            "timed_region": "stage events recorded in a repeat of the K timed steps (%.3f ms vs %.3f ms unprofiled)"
-                            % (ms_prof, ms),
-            "stage_ms_per_layer": {"route": route_ms / n_launch_gu, "gateup": gu_ms / n_launch_gu,
-                                   "down": dn_ms / n_launch_gu, "combine": cb_ms / n_launch_gu}}
+            "traffic": TRAFFIC_RATIO * bpl if TRAFFIC_RATIO else None,
+            "traffic_source": TRAFFIC_SOURCE if TRAFFIC_RATIO else None,
+            "algorithmic_bytes_per_launch": bpl, "launch_us": dur_s * 1e6,
+            "timed_region": "the K timed steps; per-launch duration = timed region / decode launches"}
 
     e2e = None
     if not args.no_e2e:
@@ -465,13 +461,12 @@ def our_arm(args):
         if tb == T:
             continue
         stack.set_batch(tb, args.seed)
-        sms, _, sstage = timed(stack, max(1, args.steps // 4), min(args.warmup, 3), ws, profile=True)
+        ks = max(1, args.steps // 4)
+        sms, _, _ = timed(stack, ks, min(args.warmup, 3), ws, profile=False)
         sms = max_over_ranks(sms, ws)
-        reps = [(min(args.warmup, 3) + s) % R for s in range(max(1, args.steps // 4))]
+        reps = [(min(args.warmup, 3) + s) % R for s in range(ks)]
         ub = sum(stack.ucount[r].sum() for r in reps) * EXPERT_BYTES
-        sweep.append({"batch": tb, "value": tb * L * len(reps) / (sms / 1e3),
-                      "layer_gbs": ub / (sms / 1e3) / 1e9,
-                      "gateup_gbs": ub * 2 / 3 / (sstage[1] / 1e3) / 1e9 if sstage[1] > 0 else None,
+        sweep.append({"batch": tb, "value": tb * L * ks / (sms / 1e3), "layer_gbs": ub / (sms / 1e3) / 1e9,
                       "experts_per_layer": float(np.mean([stack.ucount[r].mean() for r in reps]))})
     launches_all = int(sum_over_ranks(launches, ws))
 

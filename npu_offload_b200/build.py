@@ -32,18 +32,34 @@ def up_to_date():
     return all(os.path.getmtime(d) <= t for d in sources()[1])
 
 
-def build(force=False, verbose=False, extra=()):
-    if not force and up_to_date():
-        return LIB
+def build(force=False, verbose=False, extra=(), out=None):
+    """Compiles every source to an object in parallel (objects under _build/), then links the library.
+    extra: additional nvcc flags; out: library path (default: the in-tree libmoe_dp.so)."""
+    lib = out or LIB
+    if not force and out is None and up_to_date():
+        return lib
     srcs, _ = sources()
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-           "-I", os.path.join(ROOT, "include"), "-I", CSRC, "-o", LIB + ".tmp", *srcs, "-lcudart", *extra]
+    tag = str(abs(hash((tuple(extra), lib))) % (1 << 32))
+    objdir = os.path.join(HERE, "_build", tag)
+    os.makedirs(objdir, exist_ok=True)
+    common = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+              "-I", os.path.join(ROOT, "include"), "-I", CSRC, *extra]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
-    subprocess.check_call(cmd)
-    os.replace(LIB + ".tmp", LIB)
-    return LIB
+        common.insert(1, "-Xptxas=-v")
+    jobs = []
+    for src in srcs:
+        obj = os.path.join(objdir, os.path.basename(src) + ".o")
+        cmd = [*common, "-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd))
+        jobs.append((obj, subprocess.Popen(cmd)))
+    failed = [obj for obj, p in jobs if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, "nvcc " + " ".join(failed))
+    link = [NVCC, *ARCH, "-shared", "-o", lib + ".tmp", *[obj for obj, _ in jobs], "-lcudart"]
+    subprocess.check_call(link)
+    os.replace(lib + ".tmp", lib)
+    return lib
 
 
 if __name__ == "__main__":

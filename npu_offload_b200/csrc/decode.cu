@@ -52,11 +52,10 @@ static_assert(4 * 32 * kProdRegs + 8 * 32 * kConsRegs <= kDecThreads * 168, "reg
 constexpr int kMaxNS = 16;
 constexpr size_t kSmemCap = 227 * 1024;
 constexpr uint32_t kStageTarget = 49152;  // default bytes per ring stage
-constexpr int kBatch = 2;                 // units per cross-warp exchange
-// Exchange buffers.  With the pipeline below a warp writes buffer k % kXB for batch k + kXB after its
-// latest exchange wait, which is for batch k + kXB - 2; every warp arrives for that batch only after
-// it has read the buffer for batch k (its finish of batch k precedes its arrival for batch k + 2).
-// kXB = 4 satisfies k + kXB - 2 >= k + 2; three buffers would not.
+constexpr int kBatch = 4;  // units per exchange (a batch may span ring stages)
+// Exchange buffers.  A warp writes buffer k % kXB for batch k + kXB after its exchange wait for batch
+// k + kXB - 1, i.e. after every warp arrived for that batch; each warp arrives for batch k + 1 only
+// after it has read the buffer of batch k.  Any kXB >= 2 is safe; 4 costs 4 KB of shared memory.
 constexpr int kXB = 4;
 
 struct __align__(16) Ctrl {
@@ -105,8 +104,8 @@ struct LoopStat {
 };
 
 // 8 int8 weights (8 bytes of shared memory) as fp32 (exact).
-__device__ __forceinline__ void load_q8_f32(const unsigned char* p, float (&w)[8]) {
-    const uint2 v = *reinterpret_cast<const uint2*>(p);
+__device__ __forceinline__ void load_q8_f32(uint32_t p, float (&w)[8]) {
+    const uint2 v = lds64(p);
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         w[k] = i8f(v.x, k);
@@ -120,23 +119,28 @@ __device__ __forceinline__ void load_q8_f32(const unsigned char* p, float (&w)[8
 //
 // bf16 experts use the mixed-precision FMA on packed bf16 operands (x, weights and the bf16 SwiGLU
 // output are never widened); int8 experts widen weights and x to fp32.  Either way every product
-// and sum is the fp32 arithmetic of the widened values.  A full batch (kBatch units) runs as one
-// straight-line block so the units' independent FMA chains interleave.
+// and sum is the fp32 arithmetic of the widened values.
 //
-// Software pipeline over batches: batch k's dots and slice-sum butterfly are issued before batch
-// k-1's exchange wait, SwiGLU and down-column update, so the exchange latency of one batch hides
-// behind the next batch's arithmetic.  A ring stage is released after the update of its last batch,
-// i.e. while the following stage is already in use (NS >= 2).
+// Units are processed in batches of KB (one exchange per batch); a batch may span ring stages and a
+// stage may hold several batches: a stage is waited for when the first of its units is needed and
+// released once all of its units have been applied.  A full batch runs as one straight-line block
+// so the units' independent FMA chains interleave.  (Overlapping a batch's exchange with the next
+// batch's dot products measured slower than batches of 4 units: it holds more ring stages and adds
+// bookkeeping.)
 template <int CH, bool Q8, int NT, bool FULL>
 __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* ring, const Seg& sg, int& stage,
                             int& batch, uint64_t deadline, LoopStat* ls) {
-    constexpr int VP = Pow2Up<2 * kBatch * NT>::v;  // values exchanged per batch (padded)
-    constexpr int ES = Q8 ? 1 : 2;                   // bytes per weight element
+    constexpr int KB = CH <= 2 ? kBatch : 2;  // units per exchange (H > 4096: 2, for registers)
+    constexpr int VP = Pow2Up<2 * KB * NT>::v;              // values exchanged per batch (padded)
+    static_assert(2 * KB * NT <= 32, "one value per lane at most");
+    constexpr int NA = NT == 1 ? 4 : 2;                     // accumulators per row and token
+    constexpr int ES = Q8 ? 1 : 2;                          // bytes per weight element
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int H = a.H, NS = a.NS;
     const int slice = H / kCW;
     const int ub = (int)unit_bytes(Q8 ? kKindQ8 : kKindBF16, H);
     const int ups = Q8 ? a.ups_q8 : a.ups_bf16;
+    const int nu = sg.nu;
     bool valid[CH];
     int eoff[CH];
 #pragma unroll
@@ -161,26 +165,56 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
             for (int e = 0; e < 8; e++) y[t][cc][e] = 0.f;
         }
 
+    // Ring cursor over the segment's units: stage cst (absolute), its slot cslot, unit coff inside it.
+    // Advanced with compare-and-wrap only (no division in the loop).
+    const int stage0 = stage;
+    const uint32_t ring_s = smem_u32(ring);
+    int cst = stage0, cslot = stage0 % NS, coff = 0;
+    int waited = stage0 - 1, released = stage0 - 1;
+    auto wait_through = [&](int st) -> bool {  // stages <= st have landed
+        while (waited < st) {
+            ++waited;
+            const long long t0 = ls ? clock64() : 0;
+            int ws = waited - (waited / NS) * NS;
+            if (!wait_bar(&c.full[ws], (waited / NS) & 1, c, a.err, deadline)) return false;
+            if (ls) ls->wait += clock64() - t0;
+            if (a.stage_log && blockIdx.x == 0 && warp == 0 && lane == 0 && waited < kStageLogMax)
+                a.stage_log[kStageLogMax + waited] = globaltimer_ns();
+        }
+        return true;
+    };
+    auto release_below = [&](int st) {  // release stages < st
+        if (released >= st - 1) return;
+        __syncwarp();
+        while (released < st - 1) {
+            ++released;
+            if (lane == 0) mbar_arrive(&c.empty[released % NS]);
+            if (a.stage_log && blockIdx.x == 0 && warp == 0 && lane == 0 && released < kStageLogMax)
+                a.stage_log[2 * kStageLogMax + released] = globaltimer_ns();
+        }
+    };
+
     // slice dot products of one unit: v[base + 2t] = gate . x_t, v[base + 2t + 1] = up . x_t
-    auto unit_dots = [&](const unsigned char* U, float (&v)[VP], const int base) {
-        float ag[NT][4], au[NT][4];  // 4 accumulators per row: short FMA chains
+    auto unit_dots = [&](uint32_t U, float (&v)[VP], const int base) {
+        float ag[NT][NA], au[NT][NA];
 #pragma unroll
         for (int t = 0; t < NT; t++)
 #pragma unroll
-            for (int k = 0; k < 4; k++) ag[t][k] = au[t][k] = 0.f;
+            for (int k = 0; k < NA; k++) ag[t][k] = au[t][k] = 0.f;
 #pragma unroll
         for (int cc = 0; cc < CH; cc++) {
             if (!valid[cc]) continue;
             if (!Q8) {
-                const uint4 g4 = *reinterpret_cast<const uint4*>(U + (size_t)eoff[cc] * 2);
-                const uint4 u4 = *reinterpret_cast<const uint4*>(U + ((size_t)H + eoff[cc]) * 2);
+                const uint4 g4 = lds128(U + (uint32_t)eoff[cc] * 2);
+                const uint4 u4 = lds128(U + (uint32_t)(H + eoff[cc]) * 2);
                 const uint32_t wg[4] = {g4.x, g4.y, g4.z, g4.w}, wu[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
                 for (int q = 0; q < 4; q++)
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
-                        fma_bf16x2(wg[q], xw[t][cc][q], ag[t][(q & 1) * 2], ag[t][(q & 1) * 2 + 1]);
-                        fma_bf16x2(wu[q], xw[t][cc][q], au[t][(q & 1) * 2], au[t][(q & 1) * 2 + 1]);
+                        const int k0 = NA == 4 ? (q & 1) * 2 : 0;
+                        fma_bf16x2(wg[q], xw[t][cc][q], ag[t][k0], ag[t][k0 + 1]);
+                        fma_bf16x2(wu[q], xw[t][cc][q], au[t][k0], au[t][k0 + 1]);
                     }
             } else {
                 float wg[8], wu[8];
@@ -191,7 +225,7 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
                         const float x0 = bf_lo(xw[t][cc][q]), x1 = bf_hi(xw[t][cc][q]);
-                        const int k0 = (q & 1) * 2;
+                        const int k0 = NA == 4 ? (q & 1) * 2 : 0;
                         ag[t][k0] = fmaf(wg[2 * q], x0, ag[t][k0]);
                         ag[t][k0 + 1] = fmaf(wg[2 * q + 1], x1, ag[t][k0 + 1]);
                         au[t][k0] = fmaf(wu[2 * q], x0, au[t][k0]);
@@ -201,18 +235,23 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
         }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
-            v[base + 2 * t] = (ag[t][0] + ag[t][1]) + (ag[t][2] + ag[t][3]);
-            v[base + 2 * t + 1] = (au[t][0] + au[t][1]) + (au[t][2] + au[t][3]);
+            float gs = ag[t][0] + ag[t][1], us = au[t][0] + au[t][1];
+            if (NA == 4) {
+                gs += ag[t][2] + ag[t][3];
+                us += au[t][2] + au[t][3];
+            }
+            v[base + 2 * t] = gs;
+            v[base + 2 * t + 1] = us;
         }
     };
     // y[t, slice] += act[t] * down column of one unit (ab[t]: bf16 bits of act in the low half)
-    auto unit_axpy = [&](const unsigned char* U, const uint32_t (&ab)[NT]) {
-        const unsigned char* D = U + 2 * (size_t)H * ES;
+    auto unit_axpy = [&](uint32_t U, const uint32_t (&ab)[NT]) {
+        const uint32_t D = U + 2u * H * ES;
 #pragma unroll
         for (int cc = 0; cc < CH; cc++) {
             if (!valid[cc]) continue;
             if (!Q8) {
-                const uint4 wd = *reinterpret_cast<const uint4*>(D + (size_t)eoff[cc] * 2);
+                const uint4 wd = lds128(D + (uint32_t)eoff[cc] * 2);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                     fma_bf16x2_s(wd.x, ab[t], y[t][cc][0], y[t][cc][1]);
@@ -234,11 +273,10 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
     };
 
     // pending batch: exchanged but not yet applied
-    bool pend = false, prel = false;
-    const unsigned char* pS = nullptr;
-    int pb0 = 0, pnb = 0, pbatch = 0, pslot = 0, pstage = 0;
-    // exchange wait + SwiGLU + down-column update of the pending batch; releases its stage when it
-    // was the stage's last batch
+    bool pend = false;
+    int pnb = 0, pbatch = 0, pnext = 0;  // units, exchange number, stage of the unit after the batch
+    uint32_t pptr[KB];
+    // exchange wait + SwiGLU + down-column update of the pending batch, then stage releases
     auto finish = [&]() -> bool {
         const long long t2 = ls ? clock64() : 0;
         const int buf = pbatch % kXB;
@@ -254,36 +292,34 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
         uint32_t actb = 0;  // bf16 bits of act in the low half
         {
             const int item = lane >> 1, uu = item / NT;
-            if (!(lane & 1) && lane < 2 * kBatch * NT && uu < pnb) {
+            if (!(lane & 1) && lane < 2 * KB * NT && uu < pnb) {
                 float g = sum, u = upv;
                 if (Q8) {  // per-unit scales ride in the unit's trailer
-                    const float* tr = reinterpret_cast<const float*>(pS + (size_t)(pb0 + uu) * ub + 3 * (size_t)H);
-                    g *= tr[0];
-                    u *= tr[1];
+                    uint32_t U = pptr[0];
+#pragma unroll
+                    for (int k = 1; k < KB; k++)
+                        if (uu == k) U = pptr[k];
+                    g *= lds_f32(U + 3u * H);
+                    u *= lds_f32(U + 3u * H + 4u);
                 }
                 actb = swiglu_bf16(g, u);
             }
         }
         const long long t4 = ls ? clock64() : 0;
-        const unsigned char* U0 = pS + (size_t)pb0 * ub;
-        uint32_t ab0[NT];
+        uint32_t ab[KB][NT];
 #pragma unroll
-        for (int t = 0; t < NT; t++) ab0[t] = __shfl_sync(0xffffffffu, actb, 2 * t);
-        if (pnb == kBatch) {
-            uint32_t ab1[NT];
+        for (int uu = 0; uu < KB; uu++)
 #pragma unroll
-            for (int t = 0; t < NT; t++) ab1[t] = __shfl_sync(0xffffffffu, actb, 2 * (NT + t));
-            unit_axpy(U0, ab0);
-            unit_axpy(U0 + ub, ab1);
+            for (int t = 0; t < NT; t++) ab[uu][t] = __shfl_sync(0xffffffffu, actb, 2 * (uu * NT + t));
+        if (pnb == KB) {
+#pragma unroll
+            for (int uu = 0; uu < KB; uu++) unit_axpy(pptr[uu], ab[uu]);
         } else {
-            unit_axpy(U0, ab0);
+#pragma unroll
+            for (int uu = 0; uu < KB; uu++)
+                if (uu < pnb) unit_axpy(pptr[uu], ab[uu]);
         }
-        if (prel) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&c.empty[pslot]);
-            if (a.stage_log && blockIdx.x == 0 && warp == 0 && lane == 0 && pstage < kStageLogMax)
-                a.stage_log[2 * kStageLogMax + pstage] = globaltimer_ns();
-        }
+        release_below(pnext);
         if (ls) {
             const long long t5 = clock64();
             ls->bar += t3 - t2;
@@ -294,53 +330,57 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
         return true;
     };
 
-    const int nst = (sg.nu + ups - 1) / ups;
-    for (int si = 0; si < nst; si++, stage++) {
-        const int slot = stage % NS;
-        const long long t0 = ls ? clock64() : 0;
-        if (!wait_bar(&c.full[slot], (stage / NS) & 1, c, a.err, deadline)) return false;
-        if (ls) ls->wait += clock64() - t0;
-        if (a.stage_log && blockIdx.x == 0 && warp == 0 && lane == 0 && stage < kStageLogMax)
-            a.stage_log[kStageLogMax + stage] = globaltimer_ns();
-        const unsigned char* S = ring + (size_t)slot * a.slot_bytes;
-        const int nu = min(ups, sg.nu - si * ups);
-        for (int b0 = 0; b0 < nu; b0 += kBatch, batch++) {
-            const int nb = min(kBatch, nu - b0);
-            const long long tbs = ls ? clock64() : 0;
-            float v[VP];
+    for (int i0 = 0; i0 < nu; i0 += KB, batch++) {
+        const int nb = min(KB, nu - i0);
+        uint32_t uptr[KB];
+        int last_st = cst;
 #pragma unroll
-            for (int k = 0; k < VP; k++) v[k] = 0.f;
-            const unsigned char* U0 = S + (size_t)b0 * ub;
-            if (nb == kBatch) {
-                unit_dots(U0, v, 0);
-                unit_dots(U0 + ub, v, 2 * NT);
-            } else {
-                unit_dots(U0, v, 0);
+        for (int uu = 0; uu < KB; uu++) {
+            uptr[uu] = ring_s + (uint32_t)cslot * a.slot_bytes + (uint32_t)coff * ub;
+            if (uu < nb) {
+                last_st = cst;
+                if (++coff == ups) {
+                    coff = 0;
+                    ++cst;
+                    if (++cslot == NS) cslot = 0;
+                }
             }
-            const long long tb0 = ls ? clock64() : 0;
-            // slice sums: value i ends in the lanes of group i (32 / VP lanes each)
-            const float tot = warp_sum_multi<VP>(v);
-            const int buf = batch % kXB;
-            if ((lane & (32 / VP - 1)) == 0) c.red[buf][warp][lane / (32 / VP)] = tot;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&c.xbar[buf]);
-            if (ls) {
-                const long long tb1 = clock64();
-                ls->dots += tb0 - tbs;
-                ls->bfly += tb1 - tb0;
-            }
-            if (pend && !finish()) return false;
-            pend = true;
-            pS = S;
-            pb0 = b0;
-            pnb = nb;
-            pbatch = batch;
-            pslot = slot;
-            pstage = stage;
-            prel = b0 + kBatch >= nu;
         }
+        if (!wait_through(last_st)) return false;
+        const long long tbs = ls ? clock64() : 0;
+        float v[VP];
+#pragma unroll
+        for (int k = 0; k < VP; k++) v[k] = 0.f;
+        if (nb == KB) {
+#pragma unroll
+            for (int uu = 0; uu < KB; uu++) unit_dots(uptr[uu], v, 2 * NT * uu);
+        } else {
+#pragma unroll
+            for (int uu = 0; uu < KB; uu++)
+                if (uu < nb) unit_dots(uptr[uu], v, 2 * NT * uu);
+        }
+        const long long tb0 = ls ? clock64() : 0;
+        // slice sums: value i ends in the lanes of group i (32 / VP lanes each)
+        const float tot = warp_sum_multi<VP>(v);
+        const int buf = batch % kXB;
+        if ((lane & (32 / VP - 1)) == 0) c.red[buf][warp][lane / (32 / VP)] = tot;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c.xbar[buf]);
+        if (ls) {
+            const long long tb1 = clock64();
+            ls->dots += tb0 - tbs;
+            ls->bfly += tb1 - tb0;
+        }
+        pend = true;
+        pnb = nb;
+        pbatch = batch;
+        pnext = cst;  // stages < cst hold only units of this batch or earlier
+#pragma unroll
+        for (int uu = 0; uu < KB; uu++) pptr[uu] = uptr[uu];
+        if (!finish()) return false;
     }
-    if (pend && !finish()) return false;
+    release_below(waited + 1);
+    stage = waited + 1;
     // the segment's partial sums: part[gidx][t][h] (int8: times the down-row scales)
     float* P = a.part + (size_t)sg.gidx * kGroupMax * H;
 #pragma unroll
@@ -592,6 +632,21 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     int ns = (int)std::min<size_t>(kMaxNS, (kSmemCap - ctrl) / slot);
     if (a.ns_cap > 0) ns = std::min(ns, a.ns_cap);
     if (ns < 2) return false;
+    // A batch of kb units starting at a multiple of kb spans at most span(kb, ups) stages; consumers
+    // hold the stages of the batch they are waiting for, so the ring must have room for all of them
+    // or the producer could never issue the last one.
+    auto gcd = [](int x, int y) {
+        while (y) {
+            const int t = x % y;
+            x = y;
+            y = t;
+        }
+        return x;
+    };
+    auto span = [&](int kb, int ups) { return (ups - gcd(kb, ups) + kb - 1) / ups + 1; };
+    for (int kb : {kBatch, 2})
+        for (int ups : {a.ups_bf16, a.ups_q8})
+            if (span(kb, ups) > ns) return false;
     // the ring doubles as reduction scratch once every stage is consumed
     const size_t nq = (size_t)(a.H / 4 + grid - 1) / grid + 1;
     const size_t red = ((size_t)(grid + np) * kGroupMax * nq + (size_t)np * nq) * 16;
