@@ -459,8 +459,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
                 break;
             }
     }
+    // CTA 0 leaves the call's error bits in host memory when asked to (host callers read it after
+    // their stream synchronisation instead of copying the device word back)
+    auto snapshot_err = [&]() {
+        if (a.err_host && s == 0 && tid == 0) *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+    };
     __syncthreads();
-    if (c.abort_flag) return;  // no plan: write nothing, the call reports MOE_ETIMEOUT
+    if (c.abort_flag) {  // no plan: write nothing, the call reports MOE_ETIMEOUT
+        snapshot_err();
+        return;
+    }
     {
         const int4* src = reinterpret_cast<const int4*>(&a.plan->cta[s]);
         int4* dst = reinterpret_cast<int4*>(&c.me);
@@ -541,7 +549,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         }
     }
     named_bar_sync(1, kCThreads);
-    if (*(volatile int*)&c.abort_flag) return;
+    if (*(volatile int*)&c.abort_flag) {
+        snapshot_err();
+        return;
+    }
     if (tl && tid == 0) tl[4] = globaltimer_ns();
 
     // ---------------- reduction of output quads [q0, q1) ----------------
@@ -609,6 +620,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         *o = acc;
     }
     if (tl && tid == 0) tl[5] = globaltimer_ns();
+    snapshot_err();  // after the grid-wide arrival no CTA raises an error any more
 }
 
 static size_t up128(size_t v) { return (v + 127) / 128 * 128; }
@@ -616,7 +628,7 @@ static size_t up128(size_t v) { return (v + 127) / 128 * 128; }
 bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     if (a.T < 1 || a.T > kDecodeMaxT || a.H % 64 || a.H > 8192 || a.F % 64 || a.E > kMaxExperts || a.K > kMaxTopK)
         return false;
-    if (grid < 1 || grid > kPlanMaxGrid) return false;
+    if (grid < 1 || grid > plan_max_grid()) return false;
     a.ch = a.H <= 2048 ? 1 : (a.H <= 4096 ? 2 : 4);
     a.gmax = a.ch == 4 ? 2 : 4;
     const int np = a.T * a.K;

@@ -53,7 +53,7 @@ static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0 && sizeo
 static_assert(alignof(PlanShared) == 16 && alignof(PlanCta) == 16, "plan structs are copied as int4");
 
 struct PlanArgs {
-    const float* logits;   // [T, E]
+    const float* logits;   // [T, E] (device memory or device-accessible pinned host memory)
     const float* bias;     // [E] or null
     const ExpDesc* desc;   // [E] expert table of the layer
     DecodePlan* plan;      // this call's plan (parity buffer)
@@ -66,6 +66,7 @@ struct PlanArgs {
     int G;                 // decode grid size
     int gmax;              // tokens per token group (<= kGroupMax)
     int ups_bf16, ups_q8;  // units per ring stage of each kind
+    uint64_t* timeline;    // optional kTimelineSlots phase stamps of the plan kernel, else null
 };
 
 struct DecodeArgs {
@@ -73,10 +74,11 @@ struct DecodeArgs {
     const uint32_t* flag;      // plan flag; the plan is valid once *flag == stamp
     uint32_t stamp;
     const uint16_t* x;     // [T, H] bf16
-    float* out;            // [T, H] fp32
+    float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
     float* part;           // [kMaxSegTotal, kGroupMax, H] fp32 partial sums, one block per segment
     uint32_t* ctr;         // [2] grid-barrier counters (parity double-buffered)
     uint32_t* err;
+    uint32_t* err_host;    // optional host-mapped word: CTA 0 stores the error bits there when it exits
     int T, E, K, H, F, scoring, accumulate;
     uint32_t epoch;        // call counter: selects the counter parity
     int NS;                // ring stages
@@ -107,6 +109,8 @@ cudaError_t decode_set_smem_limit();
 // producer / consumer register split (otherwise the fused path must not be used).
 bool decode_register_split_fits();
 cudaError_t plan_set_smem_limit();
+// Largest decode grid the plan kernel can describe (its shared memory stages one share per CTA).
+int plan_max_grid();
 
 // Partial-sum floats the decode path needs for hidden size H.
 inline size_t decode_part_floats(int H) { return (size_t)kMaxSegTotal * kGroupMax * H; }

@@ -110,6 +110,7 @@ struct moe_ctx {
     float* d_y = nullptr;
     uint32_t* d_err = nullptr;
     uint32_t* h_err = nullptr;  // pinned
+    uint32_t* h_errsnap = nullptr;  // pinned, written by the decode kernel on host-buffer calls
     // MOE_F_HOST staging
     uint16_t* d_hidden = nullptr;
     float* d_logits = nullptr;
@@ -144,6 +145,17 @@ bool is_pinned_host(const void* p) {
         return false;
     }
     return at.type == cudaMemoryTypeHost;
+}
+
+// True when p is page-locked host memory that device code can address through p itself (unified
+// addressing maps cudaMallocHost / cudaHostAlloc memory at the same address).
+bool device_mapped(const void* p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost && at.devicePointer == p;
 }
 
 int map_err(uint32_t bits) {
@@ -249,6 +261,119 @@ int copy_in(void* dst, const void* src, size_t n, bool host, cudaStream_t st) {
     return MOE_OK;
 }
 
+// Fills the fused-path arguments that do not depend on the call's buffers; false when the call does
+// not fit the fused path (then the multi-kernel path runs).
+bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) {
+    const int dgrid = c->sm_count - 1;  // one SM stays free for the next call's plan kernel
+    if (T <= 0 || !c->fused || dgrid < 1) return false;
+    da = DecodeArgs{};
+    da.part = c->d_part;
+    da.ctr = c->d_ctr;
+    da.err = c->d_err;
+    da.T = T;
+    da.E = c->cfg.n_experts;
+    da.K = c->cfg.top_k;
+    da.H = c->cfg.hidden;
+    da.F = c->cfg.inter;
+    da.scoring = c->cfg.scoring;
+    da.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
+    da.timeout_ns = c->timeout_ns;
+    da.inject_timeout = c->inject_timeout;
+    da.timeline = c->d_timeline;
+    da.stage_log = c->d_timeline ? reinterpret_cast<uint64_t*>(c->d_timeline + (size_t)c->sm_count * kTimelineSlots) : nullptr;
+    da.ns_cap = c->ns_cap;
+    da.stage_target = c->stage_target;
+    return plan_decode(da, dgrid, dsmem);
+}
+
+// Launches plan_kernel + decode_kernel for one layer (da prepared by prepare_fused, x / out set).
+int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t dsmem, cudaStream_t st,
+                 cudaEvent_t* marks) {
+    const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
+    const uint32_t epoch = c->epoch++;
+    PlanArgs pa{};
+    pa.logits = lg;
+    pa.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
+    pa.desc = c->d_desc + (size_t)layer * E;
+    pa.plan = c->d_plan + (epoch & 1);
+    pa.flag = c->d_plan_flag + (epoch & 1);
+    pa.stamp = epoch + 1;
+    pa.idx_out = c->d_idx;
+    pa.w_out = c->d_w;
+    pa.err = c->d_err;
+    pa.T = da.T;
+    pa.E = E;
+    pa.K = da.K;
+    pa.H = da.H;
+    pa.F = da.F;
+    pa.scoring = da.scoring;
+    pa.G = dgrid;
+    pa.gmax = da.gmax;
+    pa.ups_bf16 = da.ups_bf16;
+    pa.ups_q8 = da.ups_q8;
+    pa.timeline = c->d_timeline ? c->d_timeline + (size_t)(c->sm_count - 1) * kTimelineSlots : nullptr;
+    cudaError_t e = launch_plan(pa, st);
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "plan launch: %s", cudaGetErrorString(e));
+    if (marks) cudaEventRecord(marks[1], st);
+    da.plan = pa.plan;
+    da.flag = pa.flag;
+    da.stamp = pa.stamp;
+    da.epoch = epoch;
+    e = launch_decode(da, dgrid, dsmem, st);
+    c->launches += 2;
+    if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
+    if (marks)
+        for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
+    return MOE_OK;
+}
+
+// Host buffers on the fused path.  Pinned host memory is device-accessible under unified addressing,
+// so the kernels use it in place: the plan kernel reads the logits, the decode kernel writes the
+// output and leaves its error bits in a pinned word; only the hidden states are copied to the device
+// (every decode CTA reads them).  Unpinned (or, for the output, unaligned) buffers go through the
+// context's pinned staging.  One stream synchronisation ends the call.
+int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, const float* logits, float* out,
+                       int32_t* topk_idx, float* topk_w, int flags, cudaStream_t st, DecodeArgs& da, size_t dsmem) {
+    const int H = c->cfg.hidden, E = c->cfg.n_experts, K = c->cfg.top_k;
+    const size_t hb = (size_t)T * H * 2, lb = (size_t)T * E * 4, ob = (size_t)T * H * 4;
+    const bool pin_x = is_pinned_host(hidden), pin_l = device_mapped(logits);
+    const bool pin_o = device_mapped(out) && ((uintptr_t)out & 15u) == 0;
+    int s;
+    const float* lg = logits;
+    if (!pin_x || !pin_l) {
+        if ((s = c->in_stage.reserve(align_up(hb, 256) + lb))) return s;
+        if (!pin_l) {
+            memcpy((char*)c->in_stage.host + align_up(hb, 256), logits, lb);
+            lg = reinterpret_cast<const float*>((char*)c->in_stage.host + align_up(hb, 256));
+        }
+        if (!pin_x) memcpy(c->in_stage.host, hidden, hb);
+    }
+    CUDA_TRY(cudaMemcpyAsync(c->d_hidden, pin_x ? (const void*)hidden : c->in_stage.host, hb, cudaMemcpyHostToDevice, st));
+    float* o = out;
+    if (!pin_o) {
+        if ((s = c->out_stage.reserve(ob))) return s;
+        o = static_cast<float*>(c->out_stage.host);
+        if (flags & MOE_F_ACCUMULATE) memcpy(o, out, ob);
+    }
+    *c->h_errsnap = 0;
+    da.x = c->d_hidden;
+    da.out = o;
+    da.err_host = c->h_errsnap;
+    if ((s = launch_fused(c, layer, lg, da, dsmem, st, nullptr))) return s;
+    if (!pin_x || !pin_l) c->in_stage.mark(st);
+    if (topk_idx) CUDA_TRY(cudaMemcpyAsync(topk_idx, c->d_idx, sizeof(int32_t) * T * K, cudaMemcpyDeviceToHost, st));
+    if (topk_w) CUDA_TRY(cudaMemcpyAsync(topk_w, c->d_w, sizeof(float) * T * K, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    uint32_t bits = *(volatile uint32_t*)c->h_errsnap | c->latched;
+    c->latched = 0;
+    if (bits) {  // clear the sticky device word (and, after a timeout, the grid counters)
+        CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(uint32_t)));
+        if (bits & kErrTimeout) CUDA_TRY(cudaMemset(c->d_ctr, 0, 2 * sizeof(uint32_t)));
+    }
+    if (!pin_o) memcpy(out, o, ob);
+    return map_err(bits);
+}
+
 }  // namespace
 
 extern "C" {
@@ -336,6 +461,7 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 2) != cudaSuccess)
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
+    if (!st && cudaMallocHost((void**)&c->h_errsnap, 16) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && (cudaEventCreateWithFlags(&c->in_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&c->out_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&c->job_stage.ev, cudaEventDisableTiming) != cudaSuccess))
@@ -377,6 +503,7 @@ int moe_destroy(moe_ctx* c) {
                   c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
     if (c->h_err) cudaFreeHost(c->h_err);
+    if (c->h_errsnap) cudaFreeHost(c->h_errsnap);
     for (cudaEvent_t ev : c->prof_ev) cudaEventDestroy(ev);
     for (Staging* s : {&c->in_stage, &c->out_stage, &c->job_stage}) {
         if (s->host) cudaFreeHost(s->host);
@@ -515,6 +642,11 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
     const float* lg = logits;
     float* o = out;
     int s;
+    DecodeArgs da{};
+    size_t dsmem = 0;
+    const bool use_fused = prepare_fused(c, T, flags, da, &dsmem);
+    if (host && use_fused && !c->prof_on)
+        return forward_host_fused(c, layer, T, hidden, logits, out, topk_idx, topk_w, flags, st, da, dsmem);
     if (host && T > 0) {
         const size_t hb = (size_t)T * H * 2, lb = (size_t)T * E * 4;
         if (is_pinned_host(hidden) && is_pinned_host(logits)) {
@@ -546,65 +678,10 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         c->prof_calls++;
         CUDA_TRY(cudaEventRecord(marks[0], st));
     }
-    DecodeArgs da{};
-    size_t dsmem = 0;
-    bool use_fused = false;
-    const int dgrid = c->sm_count - 1;  // one SM stays free for the next call's plan kernel
-    if (T > 0 && c->fused && dgrid >= 1) {
+    if (use_fused) {
         da.x = x;
         da.out = o;
-        da.part = c->d_part;
-        da.ctr = c->d_ctr;
-        da.err = c->d_err;
-        da.T = T;
-        da.E = E;
-        da.K = K;
-        da.H = H;
-        da.F = c->cfg.inter;
-        da.scoring = c->cfg.scoring;
-        da.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
-        da.timeout_ns = c->timeout_ns;
-        da.inject_timeout = c->inject_timeout;
-        da.timeline = c->d_timeline;
-        da.stage_log = c->d_timeline ? reinterpret_cast<uint64_t*>(c->d_timeline + (size_t)c->sm_count * kTimelineSlots) : nullptr;
-        da.ns_cap = c->ns_cap;
-        da.stage_target = c->stage_target;
-        use_fused = plan_decode(da, dgrid, &dsmem);
-    }
-    if (use_fused) {
-        const uint32_t epoch = c->epoch++;
-        PlanArgs pa{};
-        pa.logits = lg;
-        pa.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
-        pa.desc = c->d_desc + (size_t)layer * E;
-        pa.plan = c->d_plan + (epoch & 1);
-        pa.flag = c->d_plan_flag + (epoch & 1);
-        pa.stamp = epoch + 1;
-        pa.idx_out = c->d_idx;
-        pa.w_out = c->d_w;
-        pa.err = c->d_err;
-        pa.T = T;
-        pa.E = E;
-        pa.K = K;
-        pa.H = H;
-        pa.F = c->cfg.inter;
-        pa.scoring = c->cfg.scoring;
-        pa.G = dgrid;
-        pa.gmax = da.gmax;
-        pa.ups_bf16 = da.ups_bf16;
-        pa.ups_q8 = da.ups_q8;
-        cudaError_t e = launch_plan(pa, st);
-        if (e != cudaSuccess) return fail(MOE_ECUDA, "plan launch: %s", cudaGetErrorString(e));
-        if (marks) cudaEventRecord(marks[1], st);
-        da.plan = pa.plan;
-        da.flag = pa.flag;
-        da.stamp = pa.stamp;
-        da.epoch = epoch;
-        e = launch_decode(da, dgrid, dsmem, st);
-        c->launches += 2;
-        if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
-        if (marks)
-            for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
+        if ((s = launch_fused(c, layer, lg, da, dsmem, st, marks))) return s;
     }
     if (T > 0 && !use_fused) {
         RouteArgs ra = route_args(c, T, lg, c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr);

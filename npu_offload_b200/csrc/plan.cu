@@ -14,8 +14,10 @@
 //
 // It is launched with programmatic dependent launch right after the previous decode grid triggers
 // and runs on the one SM that grid leaves free, so for back-to-back layers the plan of layer l+1
-// is ready while layer l still streams.  Before exiting it waits for its predecessor grid, which
-// makes "plan(l) complete" imply "decode(l-1) complete" for the decode grid that depends on it.
+// is ready while layer l still streams.  It lets its own decode grid launch at once (the decode
+// CTAs set up and wait on the plan flag), and before exiting it waits for its predecessor grid,
+// which makes "plan(l) complete" imply "decode(l-1) complete" for the decode grid that depends on it.
+#include <algorithm>
 #include <climits>
 #include <cstddef>
 
@@ -47,25 +49,86 @@ struct PlanSmem {
     long long gcum[kMaxGroups + 1];       // unit-stream bytes of groups < g
     int cta_nseg[kPlanMaxGrid];
     int cta_seg0[kPlanMaxGrid + 1];
+    int cta_uf[kPlanMaxGrid + 1];         // first unit of each CTA's share (cta_uf[G] = all units)
     int nj, np, ngrp, pad;
+    alignas(16) float rscr[kDecodeMaxT][kMaxExperts];              // routing: exp values (read as float4)
+    alignas(16) unsigned long long rck[kDecodeMaxT][kMaxExperts];  // routing: composite keys of each token
+    alignas(16) int rrank[kDecodeMaxT][kMaxExperts];               // routing: ranks (partial counts summed)
     PlanShared sh;
 };
 static_assert(offsetof(PlanSmem, sh) % 16 == 0, "int4 copies from PlanSmem::sh");
+static_assert(offsetof(PlanSmem, rscr) % 16 == 0 && (kMaxExperts * sizeof(float)) % 16 == 0,
+              "route_keys_s reads its scratch as float4");
+static_assert(offsetof(PlanCta, seg) == 64, "PlanCta header is 64 bytes");
+static_assert(sizeof(Seg) % 16 == 0, "segments are copied as int4");
+
+// Routing of T <= 16 tokens with all 16 warps: the first warp of each token's group computes its
+// scores and keys (route_core.cuh), the group's warps count the keys ordered before each key over a
+// slice of the experts each (shared-memory atomics sum the partial counts), and the first warp
+// selects the top-k.  Same bits as route_token (the rank is an exact count).
+template <int S>
+__device__ void plan_route(const PlanArgs& a, PlanSmem& m) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = a.T, E = a.E, K = a.K;
+    const int wpt = T == 1 ? 16 : T == 2 ? 8 : T <= 4 ? 4 : T <= 8 ? 2 : 1;  // warps per token
+    const int t = warp / wpt, g = warp % wpt;
+    unsigned long long mine[S];
+    float val[S];
+    bool bad = false;
+    if (t < T && g == 0)
+        bad = route_keys_s<S>(a.logits + (size_t)t * E, a.bias, E, a.scoring, m.rscr[t], m.rck[t], mine, val);
+    for (int q = tid; q < T * kMaxExperts; q += kPlanThreads) m.rrank[q / kMaxExperts][q % kMaxExperts] = 0;
+    __syncthreads();
+    if (t < T) {
+        unsigned long long km[S];
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            const int i = lane + 32 * s;
+            km[s] = i < E ? m.rck[t][i] : 0ull;
+        }
+        const int per = (E + wpt - 1) / wpt, j0 = g * per, j1 = min(E, j0 + per);
+        int r[S];
+        route_rank_s<S>(m.rck[t], j0, j1, km, r);
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            const int i = lane + 32 * s;
+            if (i < E && r[s]) atomicAdd(&m.rrank[t][i], r[s]);
+        }
+    }
+    __syncthreads();
+    if (t < T && g == 0) {
+        int r[S];
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            const int i = lane + 32 * s;
+            r[s] = i < E ? m.rrank[t][i] : INT_MAX;
+        }
+        route_select_s<S>(E, K, a.scoring, r, val, m.idx[t], m.w[t], m.rscr[t]);
+        if (bad && lane == 0) atomicOr(a.err, kErrNonFinite);
+    }
+}
 
 __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a) {
     extern __shared__ __align__(16) unsigned char dyn[];
     PlanSmem& m = *reinterpret_cast<PlanSmem*>(dyn);
-    float* scr = reinterpret_cast<float*>(dyn + ((sizeof(PlanSmem) + 15) / 16) * 16);  // [warps][2*kMaxExperts]
+    PlanCta* cs = reinterpret_cast<PlanCta*>(dyn + ((sizeof(PlanSmem) + 15) / 16) * 16);  // [G] staged shares
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, E = a.E, K = a.K, H = a.H, F = a.F, G = a.G, GM = a.gmax;
     const int NP = T * K;
+    uint64_t* tl = a.timeline;
+    auto stamp = [&](int i) {
+        if (tl && tid == 0) tl[i] = globaltimer_ns();
+    };
+    stamp(0);
+    // The decode grid may be scheduled at once: it acquires this call's flag (bounded) before it
+    // reads the plan, and its griddepcontrol.wait still waits for this grid to complete.
+    if (tid == 0) griddep_launch_dependents();
 
-    // ---- routing: one warp per token ----
-    if (warp < T) {
-        const bool bad = route_token(a.logits + (size_t)warp * E, a.bias, E, K, a.scoring, m.idx[warp], m.w[warp],
-                                     scr + warp * 2 * kMaxExperts);
-        if (bad && lane == 0) atomicOr(a.err, kErrNonFinite);
-    }
+    // ---- routing ----
+    if (E <= 32) plan_route<1>(a, m);
+    else if (E <= 64) plan_route<2>(a, m);
+    else if (E <= 128) plan_route<4>(a, m);
+    else plan_route<8>(a, m);
     for (int e = tid; e < E; e += kPlanThreads) {
         m.counts[e] = 0;
         m.firstpos[e] = INT_MAX;
@@ -88,6 +151,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     for (int e = tid; e < E; e += kPlanThreads)
         if (m.counts[e] > 0) m.pos2e[m.firstpos[e]] = e;
     __syncthreads();
+    stamp(1);
 
     // ---- local jobs in first-appearance order: pair and group offsets ----
     if (warp == 0) {
@@ -134,6 +198,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
         }
     }
     __syncthreads();
+    stamp(2);
     const int nj = m.nj, np = m.np, ngrp = m.ngrp;
 
     // ---- pairs (job-major, tokens in order inside a job), token -> pairs, group -> job ----
@@ -182,6 +247,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     }
     __syncthreads();
 
+    stamp(3);
     // ---- partition: CTA ss owns units [U(ss), U(ss+1)) of the stream ----
     const long long total = m.gcum[ngrp];
     const double per = (double)total / G;
@@ -195,11 +261,14 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
             if (m.gcum[mid] <= B) lo = mid;
             else hi = mid - 1;
         }
-        const long long ub = (m.gcum[lo + 1] - m.gcum[lo]) / F;
-        return lo * F + (int)((B - m.gcum[lo] + ub - 1) / ub);
+        const uint32_t ub = (uint32_t)((m.gcum[lo + 1] - m.gcum[lo]) / F);
+        const uint32_t off = (uint32_t)(B - m.gcum[lo]);  // < F * ub < 2^31
+        return lo * F + (int)((off + ub - 1) / ub);
     };
+    for (int ss = tid; ss <= G; ss += kPlanThreads) m.cta_uf[ss] = unit_at(ss);
+    __syncthreads();
     for (int ss = tid; ss < G; ss += kPlanThreads) {
-        const int uf = unit_at(ss), ue = unit_at(ss + 1);
+        const int uf = m.cta_uf[ss], ue = m.cta_uf[ss + 1];
         m.cta_nseg[ss] = ue > uf ? (ue - 1) / F - uf / F + 1 : 0;
     }
     __syncthreads();
@@ -221,9 +290,9 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     }
     __syncthreads();
     const int H4 = H / 4;
-    for (int ss = tid; ss < G; ss += kPlanThreads) {
-        PlanCta* pc = &a.plan->cta[ss];
-        const int uf = unit_at(ss), ue = unit_at(ss + 1);
+    for (int ss = tid; ss < G; ss += kPlanThreads) {  // shares staged in shared memory
+        PlanCta* pc = &cs[ss];
+        const int uf = m.cta_uf[ss], ue = m.cta_uf[ss + 1];
         int nseg = m.cta_nseg[ss];
         if (nseg > kSegPerCta) {  // never expected: a share spans at most groups/G + 2 groups
             atomicOr(a.err, kErrBadIndex);
@@ -237,7 +306,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
             const int r0 = (g - m.jg0[j]) * GM;  // first pair rank of the group
             const int nt = min(GM, m.jp0[j + 1] - m.jp0[j] - r0);
             const int gidx = m.cta_seg0[ss] + k;
-            Seg sg;
+            Seg& sg = pc->seg[k];
             sg.src = m.jw1[j] + (size_t)f0 * unit_bytes(kind, H);
             sg.sc = kind == kKindQ8 ? m.jsc[j] : nullptr;
             sg.kind = kind;
@@ -249,7 +318,6 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
             sg.pad0 = sg.pad1 = 0;
 #pragma unroll
             for (int i = 0; i < kGroupMax; i++) sg.tok[i] = m.ptok[m.jp0[j] + r0 + min(i, nt - 1)];
-            pc->seg[k] = sg;
             pc->seg_stage[k] = stage;
             const int ups = kind == kKindQ8 ? a.ups_q8 : a.ups_bf16;
             stage += (sg.nu + ups - 1) / ups;
@@ -263,6 +331,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
         pc->q0 = (int)((long long)ss * H4 / G);
         pc->q1 = (int)((long long)(ss + 1) * H4 / G);
     }
+    stamp(4);
     if (tid == 0) {
         m.sh.T = T;
         m.sh.np = np;
@@ -271,33 +340,47 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
         if (m.cta_seg0[G] > kMaxSegTotal) atomicOr(a.err, kErrBadIndex);  // the host bounds it; never expected
     }
     __syncthreads();
+    // publish: each share's header and used segments, a warp per share (coalesced 16-byte stores)
+    for (int ss = warp; ss < G; ss += kPlanThreads / 32) {
+        const int4* src = reinterpret_cast<const int4*>(&cs[ss]);
+        int4* dst = reinterpret_cast<int4*>(&a.plan->cta[ss]);
+        const int n16 = (int)((offsetof(PlanCta, seg) + (size_t)cs[ss].nseg * sizeof(Seg)) / 16);
+        for (int q = lane; q < n16; q += 32) dst[q] = src[q];
+    }
     {
         const int4* src = reinterpret_cast<const int4*>(&m.sh);
         int4* dst = reinterpret_cast<int4*>(&a.plan->sh);
         for (int q = tid; q < (int)(sizeof(PlanShared) / 16); q += kPlanThreads) dst[q] = src[q];
     }
     __syncthreads();
+    stamp(5);
     if (tid == 0) {
         __threadfence();
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.flag), "r"(a.stamp) : "memory");
-        griddep_launch_dependents();
+        stamp(6);
         griddep_wait();  // complete only after the preceding grid: orders this call after the previous one
+        stamp(7);
     }
 }
 
-static size_t plan_smem_bytes() {
-    return ((sizeof(PlanSmem) + 15) / 16) * 16 + (size_t)kDecodeMaxT * 2 * kMaxExperts * sizeof(float);
+constexpr size_t kPlanSmemCap = 227 * 1024;
+
+static size_t plan_smem_bytes(int G) { return ((sizeof(PlanSmem) + 15) / 16) * 16 + (size_t)G * sizeof(PlanCta); }
+
+int plan_max_grid() {
+    const size_t fixed = ((sizeof(PlanSmem) + 15) / 16) * 16;
+    return (int)std::min<size_t>(kPlanMaxGrid, (kPlanSmemCap - fixed) / sizeof(PlanCta));
 }
 
 cudaError_t plan_set_smem_limit() {
-    return cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem_bytes());
+    return cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlanSmemCap);
 }
 
 cudaError_t launch_plan(const PlanArgs& p, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(kPlanThreads);
-    cfg.dynamicSmemBytes = plan_smem_bytes();
+    cfg.dynamicSmemBytes = plan_smem_bytes(p.G);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

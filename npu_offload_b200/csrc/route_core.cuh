@@ -23,16 +23,16 @@ __device__ __forceinline__ uint32_t ordered_bits(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// One warp routes one token; S = number of 32-expert slices (E <= 32 * S).  scr: this warp's shared
-// scratch of at least 2 * kMaxExperts floats (16-byte aligned).  Lanes 0..K-1 write idx[0..K) and
-// w[0..K) (generic pointers: global or shared).  Returns true on every lane when some
-// probability/key was NaN (an error the caller reports); NaN keys then order as -inf so the K
-// selected indices are always distinct and in range.
+// Scores of one token, one warp; S = number of 32-expert slices (E <= 32 * S).  scr: this warp's
+// shared scratch of at least kMaxExperts floats (16-byte aligned); ck: shared [E] composite keys
+// (written; may alias scr).  Lane l keeps element i = l + 32 s in key[s] / val[s] (its composite key and its
+// probability or sigmoid value).  Returns true on every lane when some probability/key was NaN (an
+// error the caller reports); NaN keys then order as -inf so the selected indices stay distinct.
 template <int S>
-__device__ __forceinline__ bool route_token_s(const float* v, const float* bias, int E, int K, int scoring, int* idx,
-                                              float* w, float* scr) {
+__device__ __forceinline__ bool route_keys_s(const float* v, const float* bias, int E, int scoring, float* scr,
+                                             unsigned long long* ck, unsigned long long (&mine)[S], float (&val)[S]) {
     const int lane = threadIdx.x & 31;
-    float key[S], val[S];
+    float key[S];
     bool bad = false;
     const int nq = E >> 2;  // whole float4 groups of the scratch
     if (scoring == 0) {
@@ -90,10 +90,8 @@ __device__ __forceinline__ bool route_token_s(const float* v, const float* bias,
         }
     }
     bad = __any_sync(0xffffffffu, bad);
-    __syncwarp();
+    __syncwarp();  // every lane's z-sum reads of scr precede key writes (ck may alias scr)
     // composite keys: ordered key bits, then the complemented index -> strictly ordered, larger first
-    unsigned long long* ck = reinterpret_cast<unsigned long long*>(scr);
-    unsigned long long mine[S];
 #pragma unroll
     for (int s = 0; s < S; s++) {
         const int i = lane + 32 * s;
@@ -101,20 +99,32 @@ __device__ __forceinline__ bool route_token_s(const float* v, const float* bias,
         mine[s] = ((unsigned long long)ordered_bits(k) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)i);
         if (i < E) ck[i] = mine[s];
     }
-    __syncwarp();
-    // rank = number of elements ordered before this one; the K elements of rank < K are the top-k
-    int rank[S];
+    return bad;
+}
+
+// Number of keys ck[j], j in [j0, j1), ordered before each of this lane's keys.
+template <int S>
+__device__ __forceinline__ void route_rank_s(const unsigned long long* ck, int j0, int j1,
+                                             const unsigned long long (&mine)[S], int (&rank)[S]) {
 #pragma unroll
     for (int s = 0; s < S; s++) rank[s] = 0;
 #pragma unroll 4
-    for (int jj = 0; jj < E; jj++) {
+    for (int jj = j0; jj < j1; jj++) {
         const unsigned long long kj = ck[jj];
 #pragma unroll
         for (int s = 0; s < S; s++) rank[s] += kj > mine[s] ? 1 : 0;
     }
-    __syncwarp();
+}
+
+// The K elements of rank < K are the top-k; weights renormalised in k order (softmax: no epsilon;
+// sigmoid: + 1e-20).  scr: the warp's scratch (>= 2 * kMaxTopK floats).  Lanes 0..K-1 write idx/w.
+template <int S>
+__device__ __forceinline__ void route_select_s(int E, int K, int scoring, const int (&rank)[S], const float (&val)[S],
+                                               int* idx, float* w, float* scr) {
+    const int lane = threadIdx.x & 31;
     int* sel_i = reinterpret_cast<int*>(scr);
     float* sel_v = scr + kMaxTopK;
+    __syncwarp();
 #pragma unroll
     for (int s = 0; s < S; s++) {
         const int i = lane + 32 * s;
@@ -132,6 +142,23 @@ __device__ __forceinline__ bool route_token_s(const float* v, const float* bias,
         w[lane] = __fdiv_rn(sel_v[lane], tot);
     }
     __syncwarp();
+}
+
+// One warp routes one token.  scr: this warp's shared scratch of at least 2 * kMaxExperts floats
+// (16-byte aligned).  Lanes 0..K-1 write idx[0..K) and w[0..K) (generic pointers: global or shared).
+// Returns true on every lane when some probability/key was NaN.
+template <int S>
+__device__ __forceinline__ bool route_token_s(const float* v, const float* bias, int E, int K, int scoring, int* idx,
+                                              float* w, float* scr) {
+    unsigned long long mine[S];
+    float val[S];
+    // exp values, then (aliasing them) the composite keys: E <= 256 keys fill the 2 KB scratch
+    unsigned long long* ck = reinterpret_cast<unsigned long long*>(scr);
+    const bool bad = route_keys_s<S>(v, bias, E, scoring, scr, ck, mine, val);
+    __syncwarp();
+    int rank[S];
+    route_rank_s<S>(ck, 0, E, mine, rank);
+    route_select_s<S>(E, K, scoring, rank, val, idx, w, scr);
     return bad;
 }
 

@@ -160,8 +160,9 @@ class MoEDataPlane:
                                 _stream_ptr(stream, x.device)))
         return (out, idx, w) if return_topk else out
 
-    def forward_host(self, layer, hidden, logits, out=None, return_topk=False):
-        """Host buffers in and out (numpy or CPU tensors; pinned ones are copied directly)."""
+    def forward_host(self, layer, hidden, logits, out=None, return_topk=False, accumulate=False):
+        """Host buffers in and out (numpy or CPU tensors).  On the fused path pinned logits and
+        16-byte-aligned pinned outputs are used in place by the kernels; others are staged."""
         x = as_bf16(hidden)
         lg = _as(logits, torch.float32)
         T = x.shape[0]
@@ -171,7 +172,8 @@ class MoEDataPlane:
         if return_topk:
             idx = torch.empty(T, self.K, dtype=torch.int32)
             w = torch.empty(T, self.K, dtype=torch.float32)
-        check(lib().moe_forward(self._h, layer, T, _vp(x), _vp(lg), _vp(out), _vp(idx), _vp(w), MOE_F_HOST,
+        flags = MOE_F_HOST | (MOE_F_ACCUMULATE if accumulate else 0)
+        check(lib().moe_forward(self._h, layer, T, _vp(x), _vp(lg), _vp(out), _vp(idx), _vp(w), flags,
                                 _stream_ptr(None, self.device)))
         return (out, idx, w) if return_topk else out
 

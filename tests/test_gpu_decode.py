@@ -85,6 +85,45 @@ def test_bounded_wait_reports_timeout_and_context_recovers(layer):
     np.testing.assert_array_equal(again, good)
 
 
+def test_host_buffers_errors_timeout_and_accumulate(layer):
+    """Host-buffer calls on the fused path: the kernels read the pinned logits and write the pinned
+    output in place and leave their error bits in a pinned word.  A NaN logit is reported and does not
+    leak into the next call; an injected timeout is reported and the context recovers; accumulate adds
+    to the caller's output."""
+    from npu_offload_b200._lib import (MOE_ENONFINITE, MOE_ETIMEOUT, MOE_OPT_INJECT_WAIT_TIMEOUT,
+                                       MOE_OPT_WAIT_TIMEOUT_US, MoEError)
+    p, _ = layer
+    T = 3
+    x, lg, xd, lgd = _inputs(55, T)
+    ref = p.forward(0, xd, lgd, sync=True).cpu().numpy()
+    px = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory()
+    pl = torch.from_numpy(lg).pin_memory()
+    po = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    p.forward_host(0, px, pl, out=po)
+    np.testing.assert_array_equal(po.numpy(), ref)
+    bad = pl.clone().pin_memory()
+    bad[1, 5] = float("nan")
+    with pytest.raises(MoEError) as ei:
+        p.forward_host(0, px, bad, out=po)
+    assert ei.value.status == MOE_ENONFINITE
+    p.forward_host(0, px, pl, out=po)  # no error carried over
+    np.testing.assert_array_equal(po.numpy(), ref)
+    p.set_option(MOE_OPT_WAIT_TIMEOUT_US, 20000)
+    p.set_option(MOE_OPT_INJECT_WAIT_TIMEOUT, 1)
+    try:
+        with pytest.raises(MoEError) as ei:
+            p.forward_host(0, px, pl, out=po)
+        assert ei.value.status == MOE_ETIMEOUT
+    finally:
+        p.set_option(MOE_OPT_INJECT_WAIT_TIMEOUT, 0)
+        p.set_option(MOE_OPT_WAIT_TIMEOUT_US, 1000000)
+    p.forward_host(0, px, pl, out=po)
+    np.testing.assert_array_equal(po.numpy(), ref)
+    base = torch.full((T, H), 0.5, dtype=torch.float32).pin_memory()
+    p.forward_host(0, px, pl, out=base, accumulate=True)
+    np.testing.assert_allclose(base.numpy(), ref + 0.5, atol=1e-6)
+
+
 def test_expert_parallel_partials_sum_to_the_full_layer(layer):
     """Two expert-parallel rank contexts on one GPU: each computes its local experts only; the sum of
     the partials equals the unsharded layer."""
