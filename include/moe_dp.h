@@ -18,8 +18,10 @@
  *    calling thread's message for its last failing call.  Unlike the reference's void C kernels,
  *    nothing aborts the process.
  *  - Pointers are device pointers unless the call takes MOE_F_HOST, in which case hidden / logits /
- *    x / out / topk / w pointers are host memory: the library copies them through its own pinned
- *    staging buffers and the call returns after the result has been copied back.
+ *    x / out / topk / w pointers are host memory and the call returns with the result in place.
+ *    Pinned (cudaMallocHost / cudaHostAlloc) buffers are used directly: on the fused decode path the
+ *    kernels read pinned logits and write a 16-byte-aligned pinned output over the bus; any other
+ *    host buffer goes through the library's own pinned staging.
  *  - Device-pointer calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy default
  *    stream).  Device-side errors (non-finite router input, a bounded wait that gave up) are
  *    latched in the context and returned by the next MOE_F_SYNC call or by moe_status().
@@ -71,7 +73,7 @@ extern "C" {
 #define MOE_KIND_Q8 2
 
 typedef struct moe_config {
-    int32_t hidden;           /* H (multiple of 256) */
+    int32_t hidden;           /* H (multiple of 64, <= 16384; the fused decode path takes H <= 8192) */
     int32_t inter;            /* F (multiple of 64) */
     int32_t n_experts;        /* E, 1..256 */
     int32_t top_k;            /* K, 1..16, <= E */
@@ -97,7 +99,8 @@ MOE_API int moe_destroy(moe_ctx* ctx);
 
 /* Load one bf16 expert: gate [F,H], up [F,H], down [H,F] -- the tensors of
  * Weights::expert (track2_opt/solar_engine/src/host.rs:112-116).  The library stores them in its
- * own HBM table; the caller keeps ownership of its buffers.  flags: MOE_F_HOST if host pointers. */
+ * own HBM table (one contiguous unit per intermediate index f: gate row f, up row f, down column f);
+ * the caller keeps ownership of its buffers.  flags: MOE_F_HOST if host pointers. */
 MOE_API int moe_load_expert_bf16(moe_ctx* ctx, int layer, int expert, const uint16_t* gate, const uint16_t* up,
                          const uint16_t* down, int flags);
 
