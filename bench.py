@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1 combine: in-kernel NVLink peer exchange (p2p) or an NCCL all-reduce per layer")
     return ap.parse_args()
 
 
@@ -184,6 +186,9 @@ class Stack:
         self.plane = MoEDataPlane(H, F, E, K, n_layers=L, max_tokens=max(T, 16), device=device.index,
                                   ep_rank=rank, ep_world=ws, shard_map=self.owner if ws > 1 else None)
         load_weights(self.plane, L, self.owner, rank, args.seed, device)
+        if ws > 1 and getattr(args, "ep", "p2p") == "p2p":
+            from npu_offload_b200.parallel import attach_peers
+            attach_peers(self.plane)  # the decode kernel combines over NVLink peer memory
         self.R = args.rotate
         self.set_batch(T, args.seed)
 
@@ -211,7 +216,7 @@ class Stack:
         r = s % self.R
         for l in range(self.L):
             self.plane.forward(l, self.x[r, l], self.lg[r, l], out=self.out[l])
-            if self.ws > 1:
+            if self.ws > 1 and not self.plane.ep_attached:
                 from npu_offload_b200.parallel import allreduce_partial
                 allreduce_partial(self.out[l])
 
@@ -294,8 +299,9 @@ def e2e_run(stack, steps, warmup, ws):
                 stack.x[r, l].copy_(xh[r, l], non_blocking=True)
                 stack.lg[r, l].copy_(lh[r, l], non_blocking=True)
                 stack.plane.forward(l, stack.x[r, l], stack.lg[r, l], out=stack.out[l])
-                from npu_offload_b200.parallel import allreduce_partial
-                allreduce_partial(stack.out[l])
+                if not stack.plane.ep_attached:
+                    from npu_offload_b200.parallel import allreduce_partial
+                    allreduce_partial(stack.out[l])
                 oh[l].copy_(stack.out[l], non_blocking=True)
         if ws > 1:
             torch.cuda.current_stream(stack.device).synchronize()
@@ -497,12 +503,16 @@ def our_arm(args):
                            "layers": L, "batch": T, "hidden": H, "experts": E, "inter": F, "top_k": K,
                            "weights_gb": round(L * E * EXPERT_BYTES / 1e9, 1),
                            "parallelism": f"ep{ws}" if ws > 1 else "single",
+                           "combine": ("in-kernel NVLink peer exchange" if args.ep == "p2p" else "NCCL all-reduce")
+                                      if ws > 1 else None,
                            "l2": "no flush: each step streams its routed experts (~%.1f GB/step/GPU) >> 126 MB L2"
                                  % (ubytes_main.mean() * L / 1e9),
                            "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
                 "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep}
         print(json.dumps(line), flush=True)
+    if ws > 1:
+        barrier(ws)  # no rank frees its exchange buffer while a peer may still use it
     stack.plane.close()
     if ws > 1:
         import torch.distributed as dist

@@ -159,6 +159,18 @@ MOE_API int moe_ck_moe_q8w(moe_ctx* ctx, int E, const int8_t* const* q, const fl
 MOE_API int moe_place_expert_q8(moe_ctx* ctx, const uint16_t* g, const uint16_t* u, const uint16_t* d, int8_t* q, float* sc,
                         int32_t* rs, int flags, void* stream);
 
+/* Expert-parallel combine over NVLink peer memory (no counterpart in the reference, whose chips
+ * return partial sums to one host).  Collective set-up, once per context, every rank of the box:
+ *   moe_ep_export(ctx, buf, cap)      writes this rank's MOE_EP_RECORD_BYTES handle record into buf;
+ *   (the caller all-gathers the records in rank order, e.g. torch.distributed.all_gather_object)
+ *   moe_ep_import(ctx, records, world) maps every other rank's exchange buffer.
+ * Afterwards moe_forward on every rank returns the full combined output (all ranks' experts),
+ * identical on all ranks; every rank must make the same sequence of moe_forward calls.  A rank that
+ * stops calling makes the others' calls fail with MOE_ETIMEOUT after the wait bound. */
+#define MOE_EP_RECORD_BYTES 256
+MOE_API int moe_ep_export(moe_ctx* ctx, void* buf, int cap);
+MOE_API int moe_ep_import(moe_ctx* ctx, const void* records, int world);
+
 /* Synchronise `stream`, then return (and clear) the latched device-side status. */
 MOE_API int moe_status(moe_ctx* ctx, void* stream);
 

@@ -427,6 +427,50 @@ __device__ bool run_segment_any(const DecodeArgs& a, Ctrl& c, const unsigned cha
     return run_segment_nt<CH, false>(a, c, ring, sg, stage, batch, deadline, ls);
 }
 
+// Cross-rank combine of output quads [q0, q0 + nq) of tokens [0, T) (see EpExchange): mine[t * nq + q]
+// holds this rank's sums in shared memory; out receives (accumulate ? out : 0) + the partials of
+// ranks 0..world-1 added in that order.  The nthr threads of named barrier 1 take part.  Returns
+// false when a rank's slice did not arrive in time (kErrTimeout raised, *abort set).
+__device__ bool ep_combine(const EpExchange& ep, const float4* mine, float* out, int T, int H, int q0, int nq, int s,
+                           int accumulate, uint32_t* err, uint64_t deadline, int nthr, int* abort) {
+    const int tid = threadIdx.x, W = ep.world, H4 = H / 4, par = ep.epoch & 1;
+    for (int f = tid; f < W * T * nq; f += nthr) {  // this rank's partial into every rank's buffer
+        const int q = f % nq, t = (f / nq) % T, r = f / (nq * T);
+        float4* dst = reinterpret_cast<float4*>(ep.peer_x[r]) + ((size_t)(par * W + ep.rank) * kEpMaxT + t) * H4 + q0 + q;
+        *dst = mine[t * nq + q];
+    }
+    __threadfence_system();
+    named_bar_sync(1, nthr);
+    if (tid < W) st_release_sys(ep.peer_flag[tid] + ep.rank * kPlanMaxGrid + s, ep.epoch);
+    if (tid < W) {
+        const uint32_t* f = ep.flag_local + tid * kPlanMaxGrid + s;
+        while (ld_acquire_sys(f) < ep.epoch) {
+            if (*(volatile int*)abort || globaltimer_ns() > deadline) {
+                atomicOr(err, kErrTimeout);
+                *(volatile int*)abort = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    named_bar_sync(1, nthr);
+    if (*(volatile int*)abort) return false;
+    for (int f = tid; f < T * nq; f += nthr) {  // every rank adds the same partials in rank order
+        const int q = f % nq, t = f / nq;
+        float4* o = reinterpret_cast<float4*>(out + (size_t)t * H) + q0 + q;
+        float4 acc = accumulate ? *o : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < W; r++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(ep.x_local) + ((size_t)(par * W + r) * kEpMaxT + t) * H4 + q0 + q);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *o = acc;
+    }
+    return true;
+}
+
 template <int CH>
 __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -603,6 +647,32 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         R[(size_t)p * nq + q] = acc;
     }
     named_bar_sync(1, kCThreads);
+    if (a.ep.world > 1) {  // expert parallel: this rank's slice sums, then the cross-rank combine
+        float4* mine = R + (size_t)np * nq;  // [T][nq]
+        for (int f = tid; f < a.T * nq; f += kCThreads) {
+            const int t = f / nq, q = f % nq;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            const int npt = min(c.sh.tpn[t], kMaxTopK);
+            for (int m = 0; m < npt; m++) {
+                const int p = min(max(c.sh.tpair[t][m], 0), np - 1);
+                const float w = c.sh.pw[p];
+                const float4 v = R[(size_t)p * nq + q];
+                acc.x = fmaf(w, v.x, acc.x);
+                acc.y = fmaf(w, v.y, acc.y);
+                acc.z = fmaf(w, v.z, acc.z);
+                acc.w = fmaf(w, v.w, acc.w);
+            }
+            mine[f] = acc;
+        }
+        named_bar_sync(1, kCThreads);
+        if (!ep_combine(a.ep, mine, a.out, a.T, H, q0, nq, s, a.accumulate, a.err, deadline, kCThreads, &c.abort_flag)) {
+            snapshot_err();
+            return;
+        }
+        if (tl && tid == 0) tl[5] = globaltimer_ns();
+        snapshot_err();
+        return;
+    }
     for (int f = tid; f < a.T * nq; f += kCThreads) {
         const int t = f / nq, q = f % nq;
         float4* o = reinterpret_cast<float4*>(a.out + (size_t)t * H) + q0 + q;
@@ -661,7 +731,7 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
             if (span(kb, ups) > ns) return false;
     // the ring doubles as reduction scratch once every stage is consumed
     const size_t nq = (size_t)(a.H / 4 + grid - 1) / grid + 1;
-    const size_t red = ((size_t)(grid + np) * kGroupMax * nq + (size_t)np * nq) * 16;
+    const size_t red = ((size_t)(grid + np) * kGroupMax * nq + (size_t)np * nq + (size_t)a.T * nq) * 16;
     if (red > (size_t)ns * slot) return false;
     a.NS = ns;
     *smem_bytes = ctrl + (size_t)ns * slot;
@@ -680,6 +750,30 @@ bool decode_register_split_fits() {
         if ((long)at.numRegs * kDecThreads < 4L * 32 * kProdRegs + 8L * 32 * kConsRegs) return false;
     }
     return true;
+}
+
+// Cross-rank combine for the multi-kernel path: CTA s owns the same output slice as decode CTA s.
+__global__ void __launch_bounds__(256) ep_exchange_kernel(const EpExchange ep, const float* part, float* out, int T,
+                                                          int H, int accumulate, uint32_t* err, uint64_t timeout_ns) {
+    extern __shared__ __align__(16) float4 mine[];  // [T][nq]
+    __shared__ int abort_flag;
+    const int s = blockIdx.x, G = gridDim.x, H4 = H / 4;
+    const int q0 = (int)((long long)s * H4 / G), nq = (int)((long long)(s + 1) * H4 / G) - q0;
+    if (threadIdx.x == 0) abort_flag = 0;
+    for (int f = threadIdx.x; f < T * nq; f += blockDim.x) {
+        const int t = f / nq, q = f % nq;
+        mine[f] = reinterpret_cast<const float4*>(part + (size_t)t * H)[q0 + q];
+    }
+    named_bar_sync(1, blockDim.x);
+    ep_combine(ep, mine, out, T, H, q0, nq, s, accumulate, err, globaltimer_ns() + timeout_ns, blockDim.x, &abort_flag);
+}
+
+cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* out, int T, int H, int accumulate,
+                               uint32_t* err, uint64_t timeout_ns, int grid, cudaStream_t st) {
+    const int nq_max = (H / 4 + grid - 1) / grid + 1;
+    const size_t smem = (size_t)T * nq_max * 16;
+    ep_exchange_kernel<<<grid, 256, smem, st>>>(ep, part, out, T, H, accumulate, err, timeout_ns);
+    return cudaGetLastError();
 }
 
 cudaError_t decode_set_smem_limit() {

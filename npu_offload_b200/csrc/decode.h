@@ -52,6 +52,25 @@ static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0 && sizeo
               "plan structs are copied as int4");
 static_assert(alignof(PlanShared) == 16 && alignof(PlanCta) == 16, "plan structs are copied as int4");
 
+// Expert-parallel combine over NVLink peer memory.  Every rank owns an exchange buffer
+// x[2][world][kEpMaxT][H] fp32 (call parity, source rank, token) and flags[world][kPlanMaxGrid]
+// (source rank, output slice) holding the epoch of the latest slice a rank delivered.  For each
+// output slice s (the quads [s*H/4/G, (s+1)*H/4/G) that CTA s of every rank reduces) a rank stores
+// its partial into every rank's buffer, releases flags[me][s] there (system scope), waits until all
+// ranks' flags for s reach the epoch, and adds the partials in rank order -- every rank ends with
+// the same full output, bit for bit.  Buffers alternate by epoch parity, so a rank one call ahead
+// never overwrites data a slower rank still reads; flags only grow and are never reset.
+constexpr int kEpMaxT = 64;     // tokens per exchange (longer calls exchange in chunks)
+constexpr int kEpMaxWorld = 8;  // ranks of one box
+struct EpExchange {
+    float* const* peer_x;          // [world] every rank's exchange buffer (peer pointers; own = local)
+    uint32_t* const* peer_flag;    // [world] every rank's flag array
+    const float* x_local;          // this rank's exchange buffer
+    const uint32_t* flag_local;    // this rank's flags
+    int rank, world;
+    uint32_t epoch;                // this call's exchange number (same on all ranks), >= 1
+};
+
 struct PlanArgs {
     const float* logits;   // [T, E] (device memory or device-accessible pinned host memory)
     const float* bias;     // [E] or null
@@ -93,6 +112,7 @@ struct DecodeArgs {
     uint64_t* stage_log;   // optional [3][kStageLogMax] issue / landed / released stamps of CTA 0's stages
     int ns_cap;            // tuning: cap on ring stages (0 = as many as shared memory allows)
     uint32_t stage_target; // tuning: target bytes per ring stage (0 = default)
+    EpExchange ep;         // cross-rank combine (ep.world > 1 with peers attached), else world = 0
 };
 
 // Host-side planning: shared-memory size and stage geometry for (T, H, F) on `grid` CTAs.
@@ -111,6 +131,12 @@ bool decode_register_split_fits();
 cudaError_t plan_set_smem_limit();
 // Largest decode grid the plan kernel can describe (its shared memory stages one share per CTA).
 int plan_max_grid();
+
+// Cross-rank combine of out[t0 .. t0+T) for a T <= kEpMaxT chunk already holding this rank's partial
+// (multi-kernel path): `part` is the local partial [T, H], `out` receives base (accumulate) + the sum
+// over ranks; grid = the decode grid size G (same output slicing on every rank).
+cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* out, int T, int H, int accumulate,
+                               uint32_t* err, uint64_t timeout_ns, int grid, cudaStream_t st);
 
 // Partial-sum floats the decode path needs for hidden size H.
 inline size_t decode_part_floats(int H) { return (size_t)kMaxSegTotal * kGroupMax * H; }

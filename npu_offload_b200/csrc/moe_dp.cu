@@ -121,6 +121,15 @@ struct moe_ctx {
     // fused decode kernel state
     uint32_t* d_ctr = nullptr;  // [2] grid-barrier counters of the fused decode kernel
     float* d_part = nullptr;    // fused decode partial sums
+    // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
+    float* d_xbuf = nullptr;            // [2][world][kEpMaxT][H] this rank's receive buffer
+    uint32_t* d_xflag = nullptr;        // [world][kPlanMaxGrid]
+    float** d_peer_x = nullptr;         // [kEpMaxWorld] device copy of every rank's buffer pointer
+    uint32_t** d_peer_flag = nullptr;   // [kEpMaxWorld]
+    float* d_xpart = nullptr;           // multi-kernel path: this rank's partial before the exchange
+    std::vector<void*> ipc_opened;      // peer mappings to close
+    bool ep_attached = false;
+    uint32_t xepoch = 0;
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
     uint32_t epoch = 0;
@@ -261,6 +270,20 @@ int copy_in(void* dst, const void* src, size_t n, bool host, cudaStream_t st) {
     return MOE_OK;
 }
 
+// The exchange arguments of one call (next epoch); world = 0 when no peers are attached.
+EpExchange next_ep(moe_ctx* c) {
+    EpExchange ep{};
+    if (!c->ep_attached) return ep;
+    ep.peer_x = c->d_peer_x;
+    ep.peer_flag = c->d_peer_flag;
+    ep.x_local = c->d_xbuf;
+    ep.flag_local = c->d_xflag;
+    ep.rank = c->cfg.ep_rank;
+    ep.world = c->cfg.ep_world;
+    ep.epoch = ++c->xepoch;
+    return ep;
+}
+
 // Fills the fused-path arguments that do not depend on the call's buffers; false when the call does
 // not fit the fused path (then the multi-kernel path runs).
 bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) {
@@ -290,6 +313,7 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
 int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t dsmem, cudaStream_t st,
                  cudaEvent_t* marks) {
     const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
+    da.ep = next_ep(c);
     const uint32_t epoch = c->epoch++;
     PlanArgs pa{};
     pa.logits = lg;
@@ -502,6 +526,9 @@ int moe_destroy(moe_ctx* c) {
                   c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
                   c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
+    for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
+    for (void* q : {(void*)c->d_xbuf, (void*)c->d_xflag, (void*)c->d_peer_x, (void*)c->d_peer_flag, (void*)c->d_xpart})
+        if (q) cudaFree(q);
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_errsnap) cudaFreeHost(c->h_errsnap);
     for (cudaEvent_t ev : c->prof_ev) cudaEventDestroy(ev);
@@ -705,13 +732,23 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         ea.y = c->d_y;
         ea.comb_off = c->d_comb_off;
         ea.comb_p = c->d_comb_p;
-        ea.out = o;
-        ea.accumulate = (flags & MOE_F_ACCUMULATE) ? 1 : 0;
+        const bool acc = (flags & MOE_F_ACCUMULATE) != 0;
+        // expert parallel: the local partial goes to scratch, the exchange adds every rank's into out
+        ea.out = c->ep_attached ? c->d_xpart : o;
+        ea.accumulate = (acc && !c->ep_attached) ? 1 : 0;
         ea.err = c->d_err;
         ea.unit_layout = 1;  // context tables
         e = launch_experts(ea, c->sm_count, st, &n, marks ? marks + 2 : nullptr);
         c->launches += n;
         if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
+        if (c->ep_attached)
+            for (int t0 = 0; t0 < T; t0 += kEpMaxT) {
+                const int tc = std::min(kEpMaxT, T - t0);
+                e = launch_ep_exchange(next_ep(c), c->d_xpart + (size_t)t0 * H, o + (size_t)t0 * H, tc, H, acc ? 1 : 0,
+                                       c->d_err, c->timeout_ns, c->sm_count - 1, st);
+                c->launches += 1;
+                if (e != cudaSuccess) return fail(MOE_ECUDA, "exchange launch: %s", cudaGetErrorString(e));
+            }
     }
     if (T > 0) {
         const cudaMemcpyKind dk = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
@@ -974,6 +1011,84 @@ int moe_place_expert_q8(moe_ctx* c, const uint16_t* g, const uint16_t* u, const 
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaFree(tmp);
     if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise: %s", cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+// ---- expert-parallel peer exchange ----
+namespace {
+constexpr uint32_t kEpMagic = 0x4D4F4550u;  // "MOEP"
+struct EpBlob {
+    uint32_t magic, sm_count, world, rank;
+    cudaIpcMemHandle_t x, flag;
+};
+}  // namespace
+
+int moe_ep_export(moe_ctx* c, void* out, int cap) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (c->cfg.ep_world < 2 || c->cfg.ep_world > kEpMaxWorld)
+        return fail(MOE_EINVAL, "peer exchange needs 2..%d ranks (ep_world = %d)", kEpMaxWorld, c->cfg.ep_world);
+    static_assert(sizeof(EpBlob) <= MOE_EP_RECORD_BYTES, "record size");
+    if (!out || cap < MOE_EP_RECORD_BYTES) return fail(MOE_EINVAL, "handle buffer needs %d bytes", MOE_EP_RECORD_BYTES);
+    DeviceGuard dg(c->dev);
+    const int W = c->cfg.ep_world, H = c->cfg.hidden;
+    int st = MOE_OK;
+    if (!c->d_xbuf) {
+        if (!st) st = dalloc(&c->d_xbuf, (size_t)2 * W * kEpMaxT * H);
+        if (!st) st = dalloc(&c->d_xflag, (size_t)W * kPlanMaxGrid);
+        if (!st) st = dalloc(&c->d_peer_x, (size_t)kEpMaxWorld);
+        if (!st) st = dalloc(&c->d_peer_flag, (size_t)kEpMaxWorld);
+        if (!st) st = dalloc(&c->d_xpart, (size_t)kEpMaxT * H * ((c->cfg.max_tokens + kEpMaxT - 1) / kEpMaxT));
+        if (st) return st;
+        CUDA_TRY(cudaMemset(c->d_xflag, 0, sizeof(uint32_t) * W * kPlanMaxGrid));
+    }
+    EpBlob b{};
+    b.magic = kEpMagic;
+    b.sm_count = (uint32_t)c->sm_count;
+    b.world = (uint32_t)W;
+    b.rank = (uint32_t)c->cfg.ep_rank;
+    CUDA_TRY(cudaIpcGetMemHandle(&b.x, c->d_xbuf));
+    CUDA_TRY(cudaIpcGetMemHandle(&b.flag, c->d_xflag));
+    memset(out, 0, MOE_EP_RECORD_BYTES);
+    memcpy(out, &b, sizeof(b));
+    return MOE_OK;
+}
+
+int moe_ep_import(moe_ctx* c, const void* blobs, int world) {
+    if (!c || !blobs) return fail(MOE_EINVAL, "null argument");
+    if (!c->d_xbuf) return fail(MOE_ESTATE, "moe_ep_export must come first");
+    if (world != c->cfg.ep_world) return fail(MOE_EINVAL, "world %d != ep_world %d", world, c->cfg.ep_world);
+    DeviceGuard dg(c->dev);
+    std::vector<float*> px(kEpMaxWorld, nullptr);
+    std::vector<uint32_t*> pf(kEpMaxWorld, nullptr);
+    for (int r = 0; r < world; r++) {
+        EpBlob b;
+        memcpy(&b, (const char*)blobs + (size_t)r * MOE_EP_RECORD_BYTES, sizeof(b));
+        if (b.magic != kEpMagic || (int)b.world != world || (int)b.rank != r)
+            return fail(MOE_EINVAL, "peer handle %d is not rank %d of %d", r, r, world);
+        if ((int)b.sm_count != c->sm_count)
+            return fail(MOE_EINVAL, "rank %d has %u SMs, this GPU %d (the output slicing must agree)", r, b.sm_count, c->sm_count);
+        if (r == c->cfg.ep_rank) {
+            px[r] = c->d_xbuf;
+            pf[r] = c->d_xflag;
+            continue;
+        }
+        void *x = nullptr, *f = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&x, b.x, cudaIpcMemLazyEnablePeerAccess);
+        if (e == cudaSuccess) e = cudaIpcOpenMemHandle(&f, b.flag, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            if (x) cudaIpcCloseMemHandle(x);
+            return fail(MOE_ECOMM, "opening rank %d's exchange buffer: %s", r, cudaGetErrorString(e));
+        }
+        c->ipc_opened.push_back(x);
+        c->ipc_opened.push_back(f);
+        px[r] = static_cast<float*>(x);
+        pf[r] = static_cast<uint32_t*>(f);
+    }
+    CUDA_TRY(cudaMemcpy(c->d_peer_x, px.data(), sizeof(float*) * kEpMaxWorld, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(c->d_peer_flag, pf.data(), sizeof(uint32_t*) * kEpMaxWorld, cudaMemcpyHostToDevice));
+    c->ep_attached = true;
+    c->xepoch = 0;
     return MOE_OK;
 }
 

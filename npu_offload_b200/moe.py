@@ -77,11 +77,26 @@ class MoEDataPlane:
                         int(ep_rank), int(ep_world),
                         None if self._shard is None else self._shard.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
         self.ep_rank, self.ep_world = int(ep_rank), int(ep_world)
+        self.ep_attached = False
         h = ctypes.c_void_p()
         check(lib().moe_create(ctypes.byref(cfg), ctypes.byref(h)))
         self._h = h
 
     # ---- lifetime ----
+    # ---- expert-parallel peer exchange (collective set-up; see parallel.attach_peers) ----
+    def ep_export(self):
+        """This rank's exchange-buffer handle record (bytes)."""
+        from ._lib import MOE_EP_RECORD_BYTES
+        buf = ctypes.create_string_buffer(MOE_EP_RECORD_BYTES)
+        check(lib().moe_ep_export(self._h, buf, MOE_EP_RECORD_BYTES))
+        return buf.raw
+
+    def ep_import(self, records):
+        """Map every rank's exchange buffer (records of all ranks, rank order, concatenated); from
+        then on forward() returns the full combined output on every rank."""
+        check(lib().moe_ep_import(self._h, records, self.ep_world))
+        self.ep_attached = True
+
     def close(self):
         if getattr(self, "_h", None):
             lib().moe_destroy(self._h)

@@ -7,8 +7,10 @@ balanced mix of hot and cold experts.  ``top`` (contiguous rank blocks, placemen
 available for comparison.
 
 Per layer every rank routes the same tokens (identical inputs give bit-identical top-k on every
-rank), runs its local experts and produces a partial [T,H] fp32 sum; one exchange (an NCCL
-all-reduce of the partials) completes the combine.
+rank), runs its local experts and produces a partial [T,H] fp32 sum; one exchange completes the
+combine.  With ``attach_peers`` the exchange happens inside the decode kernel over NVLink peer
+memory (every rank ends with the full output); otherwise ``allreduce_partial`` (NCCL) sums the
+partials.
 """
 import numpy as np
 
@@ -37,6 +39,17 @@ def shard_map(counts_per_layer, world, policy="stripe"):
 
 def local_experts(smap, layer, rank):
     return [int(e) for e in np.nonzero(np.asarray(smap)[layer] == rank)[0]]
+
+
+def attach_peers(plane, group=None):
+    """Collective: map every rank's exchange buffer into this rank's context (CUDA IPC handles
+    all-gathered over the process group).  Afterwards plane.forward returns the full output."""
+    import torch.distributed as dist
+    mine = plane.ep_export()
+    recs = [None] * dist.get_world_size(group)
+    dist.all_gather_object(recs, mine, group=group)
+    plane.ep_import(b"".join(recs))
+    dist.barrier(group)
 
 
 def allreduce_partial(out, group=None):
