@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    ap.add_argument("--prefill-tokens", type=int, default=2048,
+                    help="configs[3] prefill measurement at N=1 (0 to skip)")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="N>1 combine: in-kernel NVLink peer exchange (p2p) or an NCCL all-reduce per layer")
     return ap.parse_args()
@@ -183,7 +185,8 @@ class Stack:
         from npu_offload_b200.parallel import shard_map
         self.T, self.L, self.ws, self.rank, self.device = T, L, ws, rank, device
         self.owner = shard_map(popularity_counts(args.seed, L), ws) if ws > 1 else np.zeros((L, E), np.int32)
-        self.plane = MoEDataPlane(H, F, E, K, n_layers=L, max_tokens=max(T, 16), device=device.index,
+        self.plane = MoEDataPlane(H, F, E, K, n_layers=L, max_tokens=max(T, 16, getattr(args, "prefill_tokens", 0)),
+                                  device=device.index,
                                   ep_rank=rank, ep_world=ws, shard_map=self.owner if ws > 1 else None)
         load_weights(self.plane, L, self.owner, rank, args.seed, device)
         if ws > 1 and getattr(args, "ep", "p2p") == "p2p":
@@ -321,6 +324,37 @@ def e2e_run(stack, steps, warmup, ws):
     h2d = L * (T * H * 2 + T * E * 4) * ws
     d2h = L * T * H * 4 * (ws if ws > 1 else 1)
     return T * L * steps / (ms / 1e3), h2d, d2h
+
+
+def prefill_run(stack, T, reps=5, warmup=2):
+    """one MoE layer (layer 0 of the stack) at T prefill tokens with uniform routing
+    (logits N(0,1), no popularity bias; ~T*K/E tokens per expert).  Device-resident inputs, CUDA
+    events around `reps` back-to-back layer calls."""
+    import torch
+    from npu_offload_b200 import synth
+    x = torch.from_numpy(synth.hidden(99, T, H).view(np.int16)).view(torch.bfloat16).to(stack.device)
+    lg = torch.from_numpy(synth.logits(99, T, E, zipf=False)).to(stack.device)
+    out = torch.empty(T, H, dtype=torch.float32, device=stack.device)
+    _, idx, _ = stack.plane.forward(0, x, lg, out=out, return_topk=True, sync=True)
+    experts = len(set(idx.cpu().numpy().ravel().tolist()))
+    for _ in range(warmup):
+        stack.plane.forward(0, x, lg, out=out)
+    torch.cuda.synchronize(stack.device)
+    l0 = stack.plane.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(reps):
+        stack.plane.forward(0, x, lg, out=out)
+    ev1.record()
+    torch.cuda.synchronize(stack.device)
+    ms = ev0.elapsed_time(ev1) / reps
+    flops = 2.0 * T * K * 3 * H * F
+    wbytes = experts * EXPERT_BYTES
+    return {"workload": f"configs[3]: 1 layer, {T} prefill tokens, uniform routing ({T * K / E:.0f} tokens/expert)",
+            "tokens_per_s": T / (ms / 1e3), "ms_per_layer": ms, "tflops": flops / (ms / 1e3) / 1e12,
+            "weights_gbs": wbytes / (ms / 1e3) / 1e9, "experts": experts,
+            "path": "grouped bf16 GEMMs (cuBLAS) + gather / SwiGLU / combine kernels",
+            "gpu_launches_per_layer": (stack.plane.launch_count - l0) / reps}
 
 
 # ---------------------------------------------------------------- CPU baseline (reference / port)
@@ -475,6 +509,9 @@ def our_arm(args):
         sweep.append({"batch": tb, "value": tb * L * ks / (sms / 1e3), "layer_gbs": ub / (sms / 1e3) / 1e9,
                       "experts_per_layer": float(np.mean([stack.ucount[r].mean() for r in reps]))})
     launches_all = int(sum_over_ranks(launches, ws))
+    prefill = None
+    if ws == 1 and args.prefill_tokens > 0:
+        prefill = prefill_run(stack, args.prefill_tokens)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -509,7 +546,7 @@ def our_arm(args):
                                  % (ubytes_main.mean() * L / 1e9),
                            "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
-                "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep}
+                "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep, "prefill": prefill}
         print(json.dumps(line), flush=True)
     if ws > 1:
         barrier(ws)  # no rank frees its exchange buffer while a peer may still use it

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libmoe_dp.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["moe_dp.cu", "route.cu", "experts.cu", "decode.cu", "plan.cu", "noalloc.cu"]
+SOURCES = ["moe_dp.cu", "route.cu", "experts.cu", "decode.cu", "plan.cu", "noalloc.cu", "prefill.cu"]
 
 
 def sources():
@@ -56,7 +56,7 @@ def build(force=False, verbose=False, extra=(), out=None):
     failed = [obj for obj, p in jobs if p.wait() != 0]
     if failed:
         raise subprocess.CalledProcessError(1, "nvcc " + " ".join(failed))
-    link = [NVCC, *ARCH, "-shared", "-o", lib + ".tmp", *[obj for obj, _ in jobs], "-lcudart"]
+    link = [NVCC, *ARCH, "-shared", "-o", lib + ".tmp", *[obj for obj, _ in jobs], "-lcudart", "-lcublas"]
     subprocess.check_call(link)
     os.replace(lib + ".tmp", lib)
     return lib

@@ -291,7 +291,14 @@ __global__ void __launch_bounds__(256) combine_kernel(ExpertArgs a) {
     for (int i = a.comb_off[t]; i < a.comb_off[t + 1]; i++) {
         const int p = a.comb_p[i];
         if (p < 0) continue;
-        const float4 v = *reinterpret_cast<const float4*>(a.y + (size_t)p * a.H + h);
+        float4 v = *reinterpret_cast<const float4*>(a.y + (size_t)p * a.H + h);
+        if (a.comb_w) {
+            const float w = a.comb_w[p];
+            v.x *= w;
+            v.y *= w;
+            v.z *= w;
+            v.w *= w;
+        }
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -320,10 +327,15 @@ cudaError_t launch_experts(const ExpertArgs& a, int sm_count, cudaStream_t st, i
         *launches += 1;
     }
     if (marks) cudaEventRecord(marks[1], st);
+    cudaError_t e = launch_combine(a, st, launches);
+    if (marks) cudaEventRecord(marks[2], st);
+    return e;
+}
+
+cudaError_t launch_combine(const ExpertArgs& a, cudaStream_t st, int* launches) {
     dim3 g((a.H / 4 + 255) / 256, a.T);
     combine_kernel<<<g, 256, 0, st>>>(a);
     *launches += 1;
-    if (marks) cudaEventRecord(marks[2], st);
     return cudaGetLastError();
 }
 

@@ -22,7 +22,21 @@ struct ExpertArgs {
     int accumulate;           // out += instead of out =
     uint32_t* err;
     int unit_layout;          // 1: every job's expert is a kLayoutUnit table; 0: kLayoutSplit
+    const float* comb_w;      // combine: null when y already carries the routing weights, else the
+                              // weight of each pair (y[p] is multiplied by comb_w[p])
 };
+
+// out[t, :] = (accumulate ? out : 0) + sum over the token's pairs (comb_off / comb_p, job order) of
+// y[p, :] (times comb_w[p] when set).
+cudaError_t launch_combine(const ExpertArgs& a, cudaStream_t st, int* launches);
+
+// Prefill helpers (prefill.cu): token-row gather and the SwiGLU epilogue between the grouped GEMMs.
+cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* ptok, int n, int H, uint16_t* xg, int sm_count,
+                               cudaStream_t st);
+cudaError_t launch_swiglu_rows(const uint16_t* g, const uint16_t* u, long count, uint16_t* act, int sm_count,
+                               cudaStream_t st);
+cudaError_t launch_combine_bf16(const uint16_t* y, const float* w, const int32_t* comb_off, const int32_t* comb_p,
+                                int T, int H, int accumulate, float* out, cudaStream_t st);
 
 // Launches the decode expert pipeline (gate/up+SwiGLU, down, combine); adds the launch count.
 // marks (nullable): three events recorded after the gate/up, down and combine stages.

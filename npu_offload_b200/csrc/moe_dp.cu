@@ -1,4 +1,5 @@
 // libmoe_dp: context, expert tables and the C ABI declared in include/moe_dp.h.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -130,6 +131,15 @@ struct moe_ctx {
     std::vector<void*> ipc_opened;      // peer mappings to close
     bool ep_attached = false;
     uint32_t xepoch = 0;
+    // prefill: grouped GEMMs on the tensor cores (cuBLAS) between our gather / SwiGLU / combine
+    bool prefill = true;
+    int prefill_min_t = 128;            // smallest batch that takes the prefill path
+    cublasHandle_t blas = nullptr;
+    uint16_t* d_pf_x = nullptr;         // [NP, H] gathered token rows (job-major pairs)
+    uint16_t* d_pf_g = nullptr;         // [NP, F] gate . x (bf16 GEMM output)
+    uint16_t* d_pf_u = nullptr;         // [NP, F] up . x
+    uint16_t* d_pf_y = nullptr;         // [NP, H] down . act
+    void** d_pf_ptr = nullptr;          // [9 * E] grouped-GEMM operand pointers
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
     uint32_t epoch = 0;
@@ -351,6 +361,99 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     return MOE_OK;
 }
 
+// Prefill: after the router has grouped the pairs (d_jobs, d_ptok, d_pw, combine lists), the expert
+// FFN runs as two grouped GEMMs over the context's unit tables, read in place through their leading
+// dimensions (column-major view; bf16 operands, fp32 accumulation, bf16 outputs):
+//   gate/up  C^T[F x n] = W^T(op T) . X^T   A = gate (or up) rows, lda = unit pitch 3H; B = gathered x
+//   down     Y^T[H x n] = W2 . act^T        A = the down columns, which are W2 column-major (lda 3H)
+// Sets *done when it ran (every local job bf16); the caller runs the CUDA-core path otherwise.
+int run_prefill(moe_ctx* c, int T, const uint16_t* x, float* o, int accumulate, cudaStream_t st, bool* done) {
+    *done = false;
+    const int H = c->cfg.hidden, F = c->cfg.inter, E = c->cfg.n_experts;
+    const size_t NP = (size_t)c->cfg.max_tokens * c->cfg.top_k;
+    int s;
+    if ((s = c->job_stage.reserve(sizeof(int32_t) + sizeof(Job) * E + 64))) return s;
+    char* hp = (char*)c->job_stage.host;
+    CUDA_TRY(cudaMemcpyAsync(hp, c->d_nlj, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(hp + 16, c->d_jobs, sizeof(Job) * E, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    const int nj = std::min(*(int32_t*)hp, E);
+    std::vector<Job> jobs((Job*)(hp + 16), (Job*)(hp + 16) + nj);
+    int np = 0;
+    for (const Job& j : jobs) {
+        if (j.ex.kind != kKindBF16 || j.ex.layout != kLayoutUnit) return MOE_OK;  // int8 experts: CUDA cores
+        np = std::max(np, j.p0 + j.n);
+    }
+    if (!c->blas) {
+        if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "cublasCreate failed");
+    }
+    if (!c->d_pf_x) {
+        int st2 = dalloc(&c->d_pf_x, NP * H);
+        if (!st2) st2 = dalloc(&c->d_pf_g, NP * F);
+        if (!st2) st2 = dalloc(&c->d_pf_u, NP * F);
+        if (!st2) st2 = dalloc(&c->d_pf_y, NP * H);
+        if (!st2) st2 = dalloc(&c->d_pf_ptr, (size_t)9 * E);
+        if (st2) return st2;
+    }
+    int launches = 0;
+    if (nj > 0) {
+        CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
+        launches++;
+        // problem arrays: [gate_0..gate_nj-1, up_0..up_nj-1] then [down_0..down_nj-1]
+        const int P1 = 2 * nj;
+        std::vector<cublasOperation_t> ta(P1, CUBLAS_OP_T), tb(P1, CUBLAS_OP_N), ta2(nj, CUBLAS_OP_N), tb2(nj, CUBLAS_OP_N);
+        std::vector<int> m1(P1, F), n1(P1), k1(P1, H), lda1(P1, 3 * H), ldb1(P1, H), ldc1(P1, F), gs1(P1, 1);
+        std::vector<int> m2(nj, H), n2(nj), k2(nj, F), lda2(nj, 3 * H), ldb2(nj, F), ldc2(nj, H), gs2(nj, 1);
+        std::vector<float> one1(P1, 1.f), zero1(P1, 0.f), one2(nj, 1.f), zero2(nj, 0.f);
+        std::vector<void*> ptr((size_t)9 * E, nullptr);
+        void** A1 = ptr.data();
+        void** B1 = A1 + P1;
+        void** C1 = B1 + P1;
+        void** A2 = C1 + P1;
+        void** B2 = A2 + nj;
+        void** C2 = B2 + nj;
+        for (int j = 0; j < nj; j++) {
+            const uint16_t* w = static_cast<const uint16_t*>(jobs[j].ex.w1);
+            const int p0 = jobs[j].p0, n = jobs[j].n;
+            n1[j] = n1[nj + j] = n2[j] = n;
+            A1[j] = (void*)w;                      // gate rows
+            A1[nj + j] = (void*)(w + H);           // up rows
+            B1[j] = B1[nj + j] = c->d_pf_x + (size_t)p0 * H;
+            C1[j] = c->d_pf_g + (size_t)p0 * F;
+            C1[nj + j] = c->d_pf_u + (size_t)p0 * F;
+            A2[j] = (void*)(w + 2 * (size_t)H);    // down columns = W2 column-major
+            B2[j] = c->d_act + (size_t)p0 * F;
+            C2[j] = c->d_pf_y + (size_t)p0 * H;
+        }
+        void** dA1 = c->d_pf_ptr;
+        void** dB1 = dA1 + P1;
+        void** dC1 = dB1 + P1;
+        void** dA2 = dC1 + P1;
+        void** dB2 = dA2 + nj;
+        void** dC2 = dB2 + nj;
+        CUDA_TRY(cudaMemcpyAsync(c->d_pf_ptr, ptr.data(), sizeof(void*) * (3 * P1 + 3 * nj), cudaMemcpyHostToDevice, st));
+        CUDA_TRY(cudaStreamSynchronize(st));  // the host arrays above are read by cuBLAS at launch
+        cublasSetStream(c->blas, st);
+        cublasStatus_t bs = cublasGemmGroupedBatchedEx(
+            c->blas, ta.data(), tb.data(), m1.data(), n1.data(), k1.data(), one1.data(), (const void* const*)dA1,
+            CUDA_R_16BF, lda1.data(), (const void* const*)dB1, CUDA_R_16BF, ldb1.data(), zero1.data(), dC1, CUDA_R_16BF,
+            ldc1.data(), P1, gs1.data(), CUBLAS_COMPUTE_32F);
+        if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped gate/up GEMM: cuBLAS status %d", (int)bs);
+        CUDA_TRY(launch_swiglu_rows(c->d_pf_g, c->d_pf_u, (long)np * F, c->d_act, c->sm_count, st));
+        launches++;
+        bs = cublasGemmGroupedBatchedEx(c->blas, ta2.data(), tb2.data(), m2.data(), n2.data(), k2.data(), one2.data(),
+                                        (const void* const*)dA2, CUDA_R_16BF, lda2.data(), (const void* const*)dB2,
+                                        CUDA_R_16BF, ldb2.data(), zero2.data(), dC2, CUDA_R_16BF, ldc2.data(), nj,
+                                        gs2.data(), CUBLAS_COMPUTE_32F);
+        if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped down GEMM: cuBLAS status %d", (int)bs);
+    }
+    CUDA_TRY(launch_combine_bf16(c->d_pf_y, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
+    launches++;
+    c->launches += launches;
+    *done = true;
+    return MOE_OK;
+}
+
 // Host buffers on the fused path.  Pinned host memory is device-accessible under unified addressing,
 // so the kernels use it in place: the plan kernel reads the logits, the decode kernel writes the
 // output and leaves its error bits in a pinned word; only the hidden states are copied to the device
@@ -526,6 +629,9 @@ int moe_destroy(moe_ctx* c) {
                   c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
                   c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
+    if (c->blas) cublasDestroy(c->blas);
+    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_ptr})
+        if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
     for (void* q : {(void*)c->d_xbuf, (void*)c->d_xflag, (void*)c->d_peer_x, (void*)c->d_peer_flag, (void*)c->d_xpart})
         if (q) cudaFree(q);
@@ -738,9 +844,18 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         ea.accumulate = (acc && !c->ep_attached) ? 1 : 0;
         ea.err = c->d_err;
         ea.unit_layout = 1;  // context tables
-        e = launch_experts(ea, c->sm_count, st, &n, marks ? marks + 2 : nullptr);
+        bool done = false;
         c->launches += n;
-        if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
+        n = 0;
+        if (c->prefill && T >= c->prefill_min_t && !marks) {
+            int r = run_prefill(c, T, x, ea.out, ea.accumulate, st, &done);
+            if (r) return r;
+        }
+        if (!done) {
+            e = launch_experts(ea, c->sm_count, st, &n, marks ? marks + 2 : nullptr);
+            c->launches += n;
+            if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
+        }
         if (c->ep_attached)
             for (int t0 = 0; t0 < T; t0 += kEpMaxT) {
                 const int tc = std::min(kEpMaxT, T - t0);
@@ -1116,6 +1231,11 @@ int moe_set_option(moe_ctx* c, int option, int64_t value) {
         case MOE_OPT_RING_STAGES:
             if (value < 0 || value > 16) return fail(MOE_EINVAL, "ring stages %lld not in [0,16]", (long long)value);
             c->ns_cap = (int)value;
+            return MOE_OK;
+        case MOE_OPT_PREFILL_MIN_T:
+            if (value < 0 || value > kMaxTokens) return fail(MOE_EINVAL, "prefill batch %lld not in [0,%d]", (long long)value, kMaxTokens);
+            c->prefill = value > 0;
+            c->prefill_min_t = (int)std::max<int64_t>(1, value);
             return MOE_OK;
         case MOE_OPT_STAGE_BYTES:
             if (value < 0 || value > 196608) return fail(MOE_EINVAL, "stage bytes %lld not in [0,196608]", (long long)value);

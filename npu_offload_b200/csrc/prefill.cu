@@ -1,0 +1,97 @@
+// Prefill (many tokens per expert) for the B200 MoE data plane: the expert FFN as grouped dense GEMMs.
+//
+// Semantics as the decode path (solar_hybrid/cpu_moe.cpp:38-96): g, u = gate/up rows . x_t,
+// act = bf16_rne(g / (1 + exp(-g)) * u), y = down . act, out[t] = sum of w * y over the token's
+// experts in job order.  The two contractions run as grouped GEMMs on the tensor cores (bf16
+// operands, fp32 accumulation), reading the context's unit tables in place; the grouped GEMM
+// interface returns bf16, so g, u and y are rounded to bf16 once at the GEMM outputs (the decode
+// paths keep them in fp32).  The kernels here supply the token gather, the SwiGLU epilogue and the
+// weighted combine (fp32).
+#include <algorithm>
+
+#include "common.cuh"
+#include "experts.h"
+
+namespace moe {
+
+// xg[p, :] = x[ptok[p], :] for the n pairs of the local jobs (job-major): 16-byte vectors.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, const int32_t* ptok, int n, int H,
+                                                          uint16_t* xg) {
+    const int per = H / 8;
+    const long total = (long)n * per;
+    for (long i = blockIdx.x * 256L + threadIdx.x; i < total; i += (long)gridDim.x * 256) {
+        const int p = (int)(i / per), c = (int)(i % per);
+        reinterpret_cast<uint4*>(xg + (size_t)p * H)[c] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)ptok[p] * H) + c);
+    }
+}
+
+// act[i] = bf16_rne(g[i] / (1 + exp(-g[i])) * u[i]) over n * F values (cpu_moe.cpp:70-77); g and u
+// arrive as bf16 GEMM outputs (fp32 accumulation, one rounding).
+__global__ void __launch_bounds__(256) swiglu_rows_kernel(const uint16_t* g, const uint16_t* u, long count,
+                                                          uint16_t* act) {
+    for (long i = (blockIdx.x * 256L + threadIdx.x) * 8; i < count; i += (long)gridDim.x * 256 * 8) {
+        const uint4 gv = *reinterpret_cast<const uint4*>(g + i);
+        const uint4 uv = *reinterpret_cast<const uint4*>(u + i);
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            o[k] = (uint32_t)swiglu_bf16(bf_lo(gw[k]), bf_lo(uw[k])) |
+                   ((uint32_t)swiglu_bf16(bf_hi(gw[k]), bf_hi(uw[k])) << 16);
+        *reinterpret_cast<uint4*>(act + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// out[t, h] = (accumulate ? out : 0) + sum over the token's pairs (comb lists, job order) of
+// w[p] * y[p, h], y the bf16 output of the down GEMM.
+__global__ void __launch_bounds__(256) combine_bf16_kernel(const uint16_t* y, const float* w, const int32_t* comb_off,
+                                                           const int32_t* comb_p, int H, int accumulate, float* out) {
+    const int t = blockIdx.y;
+    const int h = (blockIdx.x * 256 + threadIdx.x) * 8;
+    if (h >= H) return;
+    float acc[8];
+    float* o = out + (size_t)t * H + h;
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc[k] = accumulate ? o[k] : 0.f;
+    for (int i = comb_off[t]; i < comb_off[t + 1]; i++) {
+        const int p = comb_p[i];
+        if (p < 0) continue;
+        const float wp = w[p];
+        const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)p * H + h);
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            acc[2 * k] = fmaf(wp, bf_lo(vw[k]), acc[2 * k]);
+            acc[2 * k + 1] = fmaf(wp, bf_hi(vw[k]), acc[2 * k + 1]);
+        }
+    }
+    reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+cudaError_t launch_combine_bf16(const uint16_t* y, const float* w, const int32_t* comb_off, const int32_t* comb_p,
+                                int T, int H, int accumulate, float* out, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    dim3 g((H / 8 + 255) / 256, T);
+    combine_bf16_kernel<<<g, 256, 0, st>>>(y, w, comb_off, comb_p, H, accumulate, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* ptok, int n, int H, uint16_t* xg, int sm_count,
+                               cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const long total = (long)n * (H / 8);
+    const int grid = (int)std::min<long>((total + 255) / 256, (long)sm_count * 16);
+    gather_rows_kernel<<<grid, 256, 0, st>>>(x, ptok, n, H, xg);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_rows(const uint16_t* g, const uint16_t* u, long count, uint16_t* act, int sm_count,
+                               cudaStream_t st) {
+    if (count <= 0) return cudaSuccess;
+    const int grid = (int)std::min<long>((count / 8 + 255) / 256, (long)sm_count * 16);
+    swiglu_rows_kernel<<<grid, 256, 0, st>>>(g, u, count, act);
+    return cudaGetLastError();
+}
+
+}  // namespace moe
