@@ -192,6 +192,9 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 128) run the expert
  *                               FFN as grouped tensor-core GEMMs when every routed local expert is
  *                               bf16; 0 keeps every batch on the CUDA-core paths.
+ *   MOE_OPT_PREFILL_TC          1 (default): the prefill gate/up GEMM runs on the library's tcgen05
+ *                               kernel with the SwiGLU fused (fp32 accumulators); 0: a grouped library
+ *                               GEMM with bf16 outputs followed by a SwiGLU kernel.
  *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
  *                               globaltimer / cycle slots (0 start, 1 plan share loaded, 2 all stages
  *                               issued, 3 all segments done, 4 grid-wide arrival seen, 5 reduction
@@ -205,6 +208,7 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 #define MOE_OPT_RING_STAGES 5
 #define MOE_OPT_STAGE_BYTES 6
 #define MOE_OPT_PREFILL_MIN_T 7
+#define MOE_OPT_PREFILL_TC 8
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
 /* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see

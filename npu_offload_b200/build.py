@@ -15,7 +15,24 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libmoe_dp.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["moe_dp.cu", "route.cu", "experts.cu", "decode.cu", "plan.cu", "noalloc.cu", "prefill.cu"]
+SOURCES = ["moe_dp.cu", "route.cu", "experts.cu", "decode.cu", "plan.cu", "noalloc.cu", "prefill.cu", "prefill_tc.cu"]
+
+
+def cute_include():
+    """CuTe / CUTLASS headers (descriptor and type definitions for the tcgen05 kernels): the header
+    tree vendored with flashinfer, or $CUTLASS_INCLUDE."""
+    cand = [os.environ.get("CUTLASS_INCLUDE", "")]
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("flashinfer")
+        if spec and spec.submodule_search_locations:
+            cand.append(os.path.join(list(spec.submodule_search_locations)[0], "data", "cutlass", "include"))
+    except Exception:
+        pass
+    for d in cand:
+        if d and os.path.exists(os.path.join(d, "cute", "arch", "mma_sm100_desc.hpp")):
+            return [d]
+    raise RuntimeError("CuTe headers not found: set CUTLASS_INCLUDE to a CUTLASS include directory")
 
 
 def sources():
@@ -43,7 +60,7 @@ def build(force=False, verbose=False, extra=(), out=None):
     objdir = os.path.join(HERE, "_build", tag)
     os.makedirs(objdir, exist_ok=True)
     common = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-              "-I", os.path.join(ROOT, "include"), "-I", CSRC, *extra]
+              "-I", os.path.join(ROOT, "include"), "-I", CSRC, *[a for d in cute_include() for a in ("-I", d)], *extra]
     if verbose:
         common.insert(1, "-Xptxas=-v")
     jobs = []

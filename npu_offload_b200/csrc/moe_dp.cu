@@ -12,6 +12,7 @@
 #include "../../include/moe_dp.h"
 #include "common.cuh"
 #include "decode.h"
+#include "prefill_tc.h"
 #include "experts.h"
 #include "route.h"
 
@@ -140,6 +141,9 @@ struct moe_ctx {
     uint16_t* d_pf_u = nullptr;         // [NP, F] up . x
     uint16_t* d_pf_y = nullptr;         // [NP, H] down . act
     void** d_pf_ptr = nullptr;          // [9 * E] grouped-GEMM operand pointers
+    bool prefill_tc = true;             // gate/up on our tcgen05 kernel (fused SwiGLU); else cuBLAS
+    TcItem* d_tc_items = nullptr;       // tile list of the tcgen05 gate/up kernel
+    int tc_items_cap = 0;
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
     uint32_t epoch = 0;
@@ -367,7 +371,7 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
 //   gate/up  C^T[F x n] = W^T(op T) . X^T   A = gate (or up) rows, lda = unit pitch 3H; B = gathered x
 //   down     Y^T[H x n] = W2 . act^T        A = the down columns, which are W2 column-major (lda 3H)
 // Sets *done when it ran (every local job bf16); the caller runs the CUDA-core path otherwise.
-int run_prefill(moe_ctx* c, int T, const uint16_t* x, float* o, int accumulate, cudaStream_t st, bool* done) {
+int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int accumulate, cudaStream_t st, bool* done) {
     *done = false;
     const int H = c->cfg.hidden, F = c->cfg.inter, E = c->cfg.n_experts;
     const size_t NP = (size_t)c->cfg.max_tokens * c->cfg.top_k;
@@ -432,15 +436,40 @@ int run_prefill(moe_ctx* c, int T, const uint16_t* x, float* o, int accumulate, 
         void** dB2 = dA2 + nj;
         void** dC2 = dB2 + nj;
         CUDA_TRY(cudaMemcpyAsync(c->d_pf_ptr, ptr.data(), sizeof(void*) * (3 * P1 + 3 * nj), cudaMemcpyHostToDevice, st));
-        CUDA_TRY(cudaStreamSynchronize(st));  // the host arrays above are read by cuBLAS at launch
+        const bool tc = c->prefill_tc && tc_available() && F % 128 == 0 && H % 64 == 0;
+        std::vector<TcItem> items;
+        if (tc) {  // tiles of 256 pairs x 128 intermediate indices per job
+            for (int j = 0; j < nj; j++) {
+                const long slot = ((const char*)jobs[j].ex.w1 - (const char*)c->arena[layer]) / (long)c->stride;
+                for (int m0 = 0; m0 < jobs[j].n; m0 += 256)
+                    for (int f0 = 0; f0 < F; f0 += 128)
+                        items.push_back(TcItem{jobs[j].p0 + m0, std::min(256, jobs[j].n - m0), (int)slot, f0});
+            }
+            if ((int)items.size() > c->tc_items_cap) {
+                if (c->d_tc_items) cudaFree(c->d_tc_items);
+                c->d_tc_items = nullptr;
+                c->tc_items_cap = 0;
+                if ((s = dalloc(&c->d_tc_items, items.size()))) return s;
+                c->tc_items_cap = (int)items.size();
+            }
+            CUDA_TRY(cudaMemcpyAsync(c->d_tc_items, items.data(), sizeof(TcItem) * items.size(), cudaMemcpyHostToDevice, st));
+        }
+        CUDA_TRY(cudaStreamSynchronize(st));  // the host arrays above are read at launch
         cublasSetStream(c->blas, st);
-        cublasStatus_t bs = cublasGemmGroupedBatchedEx(
-            c->blas, ta.data(), tb.data(), m1.data(), n1.data(), k1.data(), one1.data(), (const void* const*)dA1,
-            CUDA_R_16BF, lda1.data(), (const void* const*)dB1, CUDA_R_16BF, ldb1.data(), zero1.data(), dC1, CUDA_R_16BF,
-            ldc1.data(), P1, gs1.data(), CUBLAS_COMPUTE_32F);
-        if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped gate/up GEMM: cuBLAS status %d", (int)bs);
-        CUDA_TRY(launch_swiglu_rows(c->d_pf_g, c->d_pf_u, (long)np * F, c->d_act, c->sm_count, st));
-        launches++;
+        cublasStatus_t bs;
+        if (tc) {
+            CUDA_TRY(launch_gateup_tc(c->d_pf_x, np, c->arena[layer], std::max(1, c->n_local[layer]), c->stride,
+                                      c->d_tc_items, (int)items.size(), H, F, c->d_act, c->d_err, c->timeout_ns, st));
+            launches++;
+        } else {
+            bs = cublasGemmGroupedBatchedEx(c->blas, ta.data(), tb.data(), m1.data(), n1.data(), k1.data(), one1.data(),
+                                            (const void* const*)dA1, CUDA_R_16BF, lda1.data(), (const void* const*)dB1,
+                                            CUDA_R_16BF, ldb1.data(), zero1.data(), dC1, CUDA_R_16BF, ldc1.data(), P1,
+                                            gs1.data(), CUBLAS_COMPUTE_32F);
+            if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped gate/up GEMM: cuBLAS status %d", (int)bs);
+            CUDA_TRY(launch_swiglu_rows(c->d_pf_g, c->d_pf_u, (long)np * F, c->d_act, c->sm_count, st));
+            launches++;
+        }
         bs = cublasGemmGroupedBatchedEx(c->blas, ta2.data(), tb2.data(), m2.data(), n2.data(), k2.data(), one2.data(),
                                         (const void* const*)dA2, CUDA_R_16BF, lda2.data(), (const void* const*)dB2,
                                         CUDA_R_16BF, ldb2.data(), zero2.data(), dC2, CUDA_R_16BF, ldc2.data(), nj,
@@ -607,6 +636,10 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     }
     if (!st && !decode_register_split_fits()) c->fused = false;  // this build cannot run the fused kernel
     if (!st) {
+        cudaError_t e = tc_set_smem_limit();
+        if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
+    }
+    if (!st) {
         cudaError_t e = route_set_smem_limits();
         if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
     }
@@ -630,7 +663,8 @@ int moe_destroy(moe_ctx* c) {
                   c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
     if (c->blas) cublasDestroy(c->blas);
-    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_ptr})
+    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_ptr,
+                    (void*)c->d_tc_items})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
     for (void* q : {(void*)c->d_xbuf, (void*)c->d_xflag, (void*)c->d_peer_x, (void*)c->d_peer_flag, (void*)c->d_xpart})
@@ -848,7 +882,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         c->launches += n;
         n = 0;
         if (c->prefill && T >= c->prefill_min_t && !marks) {
-            int r = run_prefill(c, T, x, ea.out, ea.accumulate, st, &done);
+            int r = run_prefill(c, layer, T, x, ea.out, ea.accumulate, st, &done);
             if (r) return r;
         }
         if (!done) {
@@ -1236,6 +1270,9 @@ int moe_set_option(moe_ctx* c, int option, int64_t value) {
             if (value < 0 || value > kMaxTokens) return fail(MOE_EINVAL, "prefill batch %lld not in [0,%d]", (long long)value, kMaxTokens);
             c->prefill = value > 0;
             c->prefill_min_t = (int)std::max<int64_t>(1, value);
+            return MOE_OK;
+        case MOE_OPT_PREFILL_TC:
+            c->prefill_tc = value != 0;
             return MOE_OK;
         case MOE_OPT_STAGE_BYTES:
             if (value < 0 || value > 196608) return fail(MOE_EINVAL, "stage bytes %lld not in [0,196608]", (long long)value);

@@ -1,0 +1,24 @@
+// Tensor-core (tcgen05) prefill kernels: launch interface.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace moe {
+
+// One output tile of the gate/up GEMM: gathered rows [row0, row0 + rows) (<= 256) of one job, whose
+// expert sits in arena slot `slot`, intermediate indices [f0, f0 + 128).
+struct TcItem {
+    int32_t row0, rows, slot, f0;
+};
+
+bool tc_available();  // the driver's tensor-map encoder is reachable
+cudaError_t tc_set_smem_limit();
+
+// act[p, f] for every item (fused SwiGLU, bf16).  xg: gathered token rows [xrows][H] bf16; arena: the
+// layer's unit tables (n_slots slots of slot_bytes).  H % 64 == 0, F % 128 == 0.
+cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, int n_slots, size_t slot_bytes,
+                             const TcItem* items, int n_items, int H, int F, uint16_t* act, uint32_t* err,
+                             uint64_t timeout_ns, cudaStream_t st);
+
+}  // namespace moe

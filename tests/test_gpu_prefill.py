@@ -22,9 +22,10 @@ def _plane(H, F, E, K, seed, q8=()):
     return p, W
 
 
-def _run(p, x, lg, prefill):
-    from npu_offload_b200._lib import MOE_OPT_PREFILL_MIN_T
+def _run(p, x, lg, prefill, tc=True):
+    from npu_offload_b200._lib import MOE_OPT_PREFILL_MIN_T, MOE_OPT_PREFILL_TC
     p.set_option(MOE_OPT_PREFILL_MIN_T, 64 if prefill else 0)
+    p.set_option(MOE_OPT_PREFILL_TC, 1 if tc else 0)
     xd = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda()
     out, idx, w = p.forward(0, xd, torch.from_numpy(lg).cuda(), return_topk=True, sync=True)
     return out.cpu().numpy(), idx.cpu().numpy()
@@ -59,7 +60,10 @@ def test_prefill_solar_shape_and_int8_fallback():
         lg = synth.logits(7, T, E, zipf=False)
         pre, _ = _run(p, x, lg, True)
         core, _ = _run(p, x, lg, False)
-        assert_close(pre, core, what="prefill vs cuda cores, Solar shape")
+        lib_gemm, _ = _run(p, x, lg, True, tc=False)
+        # tcgen05 gate/up keeps g and u in fp32 like the CUDA-core path; the library down GEMM rounds y
+        assert_close(pre, core, what="tcgen05 prefill vs cuda cores, Solar shape")
+        assert_close(lib_gemm, core, what="library-GEMM prefill vs cuda cores, Solar shape")
         # a routed int8 expert keeps the batch on the CUDA-core path (same bits as forcing it)
         p.quantize_expert_q8(0, 3)
         pre8, _ = _run(p, x, lg, True)
