@@ -353,7 +353,7 @@ def prefill_run(stack, T, reps=5, warmup=2):
     return {"workload": f"configs[3]: 1 layer, {T} prefill tokens, uniform routing ({T * K / E:.0f} tokens/expert)",
             "tokens_per_s": T / (ms / 1e3), "ms_per_layer": ms, "tflops": flops / (ms / 1e3) / 1e12,
             "weights_gbs": wbytes / (ms / 1e3) / 1e9, "experts": experts,
-            "path": "gate/up: tcgen05 kernel with fused SwiGLU; down: grouped library GEMM; gather + combine kernels",
+            "path": "tcgen05 kernels: gate/up with fused SwiGLU, down with fp32 output; gather + combine kernels",
             "gpu_launches_per_layer": (stack.plane.launch_count - l0) / reps}
 
 

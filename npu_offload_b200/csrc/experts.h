@@ -37,6 +37,8 @@ cudaError_t launch_swiglu_rows(const uint16_t* g, const uint16_t* u, long count,
                                cudaStream_t st);
 cudaError_t launch_combine_bf16(const uint16_t* y, const float* w, const int32_t* comb_off, const int32_t* comb_p,
                                 int T, int H, int accumulate, float* out, cudaStream_t st);
+cudaError_t launch_combine_rows(const float* y, const float* w, const int32_t* comb_off, const int32_t* comb_p, int T,
+                                int H, int accumulate, float* out, cudaStream_t st);
 
 // Launches the decode expert pipeline (gate/up+SwiGLU, down, combine); adds the launch count.
 // marks (nullable): three events recorded after the gate/up, down and combine stages.

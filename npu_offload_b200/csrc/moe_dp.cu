@@ -139,10 +139,11 @@ struct moe_ctx {
     uint16_t* d_pf_x = nullptr;         // [NP, H] gathered token rows (job-major pairs)
     uint16_t* d_pf_g = nullptr;         // [NP, F] gate . x (bf16 GEMM output)
     uint16_t* d_pf_u = nullptr;         // [NP, F] up . x
-    uint16_t* d_pf_y = nullptr;         // [NP, H] down . act
+    uint16_t* d_pf_y = nullptr;         // [NP, H] down . act (library path, bf16)
+    float* d_pf_yf = nullptr;           // [NP, H] down . act (tensor-core path, fp32)
     void** d_pf_ptr = nullptr;          // [9 * E] grouped-GEMM operand pointers
-    bool prefill_tc = true;             // gate/up on our tcgen05 kernel (fused SwiGLU); else cuBLAS
-    TcItem* d_tc_items = nullptr;       // tile list of the tcgen05 gate/up kernel
+    bool prefill_tc = true;             // gate/up and down on the tcgen05 kernels; else cuBLAS
+    TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels
     int tc_items_cap = 0;
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
@@ -366,8 +367,11 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
 }
 
 // Prefill: after the router has grouped the pairs (d_jobs, d_ptok, d_pw, combine lists), the expert
-// FFN runs as two grouped GEMMs over the context's unit tables, read in place through their leading
-// dimensions (column-major view; bf16 operands, fp32 accumulation, bf16 outputs):
+// FFN runs as two grouped GEMMs over the context's unit tables, read in place.
+// Tensor-core path (tcgen05 kernels, fp32 accumulation, g / u / y kept in fp32 like the decode paths):
+//   gate/up  tiles of 256 pairs x 128 f: act = SwiGLU(gate . x, up . x) fused in the epilogue
+//   down     tiles of 256 pairs x 256 h: y = down . act, the down columns as an MN-major operand
+// Library path (cuBLAS grouped GEMM, column-major view, bf16 outputs):
 //   gate/up  C^T[F x n] = W^T(op T) . X^T   A = gate (or up) rows, lda = unit pitch 3H; B = gathered x
 //   down     Y^T[H x n] = W2 . act^T        A = the down columns, which are W2 column-major (lda 3H)
 // Sets *done when it ran (every local job bf16); the caller runs the CUDA-core path otherwise.
@@ -388,7 +392,8 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         if (j.ex.kind != kKindBF16 || j.ex.layout != kLayoutUnit) return MOE_OK;  // int8 experts: CUDA cores
         np = std::max(np, j.p0 + j.n);
     }
-    if (!c->blas) {
+    const bool tc = c->prefill_tc && tc_available() && F % 128 == 0 && H % 256 == 0;
+    if (!tc && !c->blas) {
         if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "cublasCreate failed");
     }
     if (!c->d_pf_x) {
@@ -396,88 +401,97 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         if (!st2) st2 = dalloc(&c->d_pf_g, NP * F);
         if (!st2) st2 = dalloc(&c->d_pf_u, NP * F);
         if (!st2) st2 = dalloc(&c->d_pf_y, NP * H);
+        if (!st2) st2 = dalloc(&c->d_pf_yf, NP * H);
         if (!st2) st2 = dalloc(&c->d_pf_ptr, (size_t)9 * E);
         if (st2) return st2;
     }
     int launches = 0;
-    if (nj > 0) {
-        CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
-        launches++;
-        // problem arrays: [gate_0..gate_nj-1, up_0..up_nj-1] then [down_0..down_nj-1]
-        const int P1 = 2 * nj;
-        std::vector<cublasOperation_t> ta(P1, CUBLAS_OP_T), tb(P1, CUBLAS_OP_N), ta2(nj, CUBLAS_OP_N), tb2(nj, CUBLAS_OP_N);
-        std::vector<int> m1(P1, F), n1(P1), k1(P1, H), lda1(P1, 3 * H), ldb1(P1, H), ldc1(P1, F), gs1(P1, 1);
-        std::vector<int> m2(nj, H), n2(nj), k2(nj, F), lda2(nj, 3 * H), ldb2(nj, F), ldc2(nj, H), gs2(nj, 1);
-        std::vector<float> one1(P1, 1.f), zero1(P1, 0.f), one2(nj, 1.f), zero2(nj, 0.f);
-        std::vector<void*> ptr((size_t)9 * E, nullptr);
-        void** A1 = ptr.data();
-        void** B1 = A1 + P1;
-        void** C1 = B1 + P1;
-        void** A2 = C1 + P1;
-        void** B2 = A2 + nj;
-        void** C2 = B2 + nj;
-        for (int j = 0; j < nj; j++) {
-            const uint16_t* w = static_cast<const uint16_t*>(jobs[j].ex.w1);
-            const int p0 = jobs[j].p0, n = jobs[j].n;
-            n1[j] = n1[nj + j] = n2[j] = n;
-            A1[j] = (void*)w;                      // gate rows
-            A1[nj + j] = (void*)(w + H);           // up rows
-            B1[j] = B1[nj + j] = c->d_pf_x + (size_t)p0 * H;
-            C1[j] = c->d_pf_g + (size_t)p0 * F;
-            C1[nj + j] = c->d_pf_u + (size_t)p0 * F;
-            A2[j] = (void*)(w + 2 * (size_t)H);    // down columns = W2 column-major
-            B2[j] = c->d_act + (size_t)p0 * F;
-            C2[j] = c->d_pf_y + (size_t)p0 * H;
-        }
-        void** dA1 = c->d_pf_ptr;
-        void** dB1 = dA1 + P1;
-        void** dC1 = dB1 + P1;
-        void** dA2 = dC1 + P1;
-        void** dB2 = dA2 + nj;
-        void** dC2 = dB2 + nj;
-        CUDA_TRY(cudaMemcpyAsync(c->d_pf_ptr, ptr.data(), sizeof(void*) * (3 * P1 + 3 * nj), cudaMemcpyHostToDevice, st));
-        const bool tc = c->prefill_tc && tc_available() && F % 128 == 0 && H % 64 == 0;
+    if (nj > 0 && tc) {
+        // tile lists: gate/up tiles (TcItem.f0 = first f), then down tiles (TcItem.f0 = first output h)
         std::vector<TcItem> items;
-        if (tc) {  // tiles of 256 pairs x 128 intermediate indices per job
+        int n_gu = 0;
+        for (int pass = 0; pass < 2; pass++) {
             for (int j = 0; j < nj; j++) {
                 const long slot = ((const char*)jobs[j].ex.w1 - (const char*)c->arena[layer]) / (long)c->stride;
                 for (int m0 = 0; m0 < jobs[j].n; m0 += 256)
-                    for (int f0 = 0; f0 < F; f0 += 128)
-                        items.push_back(TcItem{jobs[j].p0 + m0, std::min(256, jobs[j].n - m0), (int)slot, f0});
+                    for (int n0 = 0; n0 < (pass ? H : F); n0 += (pass ? 256 : 128))
+                        items.push_back(TcItem{jobs[j].p0 + m0, std::min(256, jobs[j].n - m0), (int)slot, n0});
             }
-            if ((int)items.size() > c->tc_items_cap) {
-                if (c->d_tc_items) cudaFree(c->d_tc_items);
-                c->d_tc_items = nullptr;
-                c->tc_items_cap = 0;
-                if ((s = dalloc(&c->d_tc_items, items.size()))) return s;
-                c->tc_items_cap = (int)items.size();
-            }
-            CUDA_TRY(cudaMemcpyAsync(c->d_tc_items, items.data(), sizeof(TcItem) * items.size(), cudaMemcpyHostToDevice, st));
+            if (!pass) n_gu = (int)items.size();
         }
-        CUDA_TRY(cudaStreamSynchronize(st));  // the host arrays above are read at launch
-        cublasSetStream(c->blas, st);
-        cublasStatus_t bs;
-        if (tc) {
-            CUDA_TRY(launch_gateup_tc(c->d_pf_x, np, c->arena[layer], std::max(1, c->n_local[layer]), c->stride,
-                                      c->d_tc_items, (int)items.size(), H, F, c->d_act, c->d_err, c->timeout_ns, st));
+        if ((int)items.size() > c->tc_items_cap) {
+            if (c->d_tc_items) cudaFree(c->d_tc_items);
+            c->d_tc_items = nullptr;
+            c->tc_items_cap = 0;
+            if ((s = dalloc(&c->d_tc_items, items.size()))) return s;
+            c->tc_items_cap = (int)items.size();
+        }
+        // pageable source: the copy has completed when the call returns, so items may go out of scope
+        CUDA_TRY(cudaMemcpyAsync(c->d_tc_items, items.data(), sizeof(TcItem) * items.size(), cudaMemcpyHostToDevice, st));
+        const int n_slots = std::max(1, c->n_local[layer]);
+        CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
+        CUDA_TRY(launch_gateup_tc(c->d_pf_x, np, c->arena[layer], n_slots, c->stride, c->d_tc_items, n_gu, H, F, c->d_act,
+                                  c->d_err, c->timeout_ns, st));
+        CUDA_TRY(launch_down_tc(c->d_act, np, c->arena[layer], n_slots, c->stride, c->d_tc_items + n_gu,
+                                (int)items.size() - n_gu, H, F, c->d_pf_yf, c->d_err, c->timeout_ns, st));
+        CUDA_TRY(launch_combine_rows(c->d_pf_yf, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
+        launches += 4;
+    } else {
+        if (nj > 0) {
+            CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
             launches++;
-        } else {
-            bs = cublasGemmGroupedBatchedEx(c->blas, ta.data(), tb.data(), m1.data(), n1.data(), k1.data(), one1.data(),
-                                            (const void* const*)dA1, CUDA_R_16BF, lda1.data(), (const void* const*)dB1,
-                                            CUDA_R_16BF, ldb1.data(), zero1.data(), dC1, CUDA_R_16BF, ldc1.data(), P1,
-                                            gs1.data(), CUBLAS_COMPUTE_32F);
+            // problem arrays: [gate_0..gate_nj-1, up_0..up_nj-1] then [down_0..down_nj-1]
+            const int P1 = 2 * nj;
+            std::vector<cublasOperation_t> ta(P1, CUBLAS_OP_T), tb(P1, CUBLAS_OP_N), ta2(nj, CUBLAS_OP_N), tb2(nj, CUBLAS_OP_N);
+            std::vector<int> m1(P1, F), n1(P1), k1(P1, H), lda1(P1, 3 * H), ldb1(P1, H), ldc1(P1, F), gs1(P1, 1);
+            std::vector<int> m2(nj, H), n2(nj), k2(nj, F), lda2(nj, 3 * H), ldb2(nj, F), ldc2(nj, H), gs2(nj, 1);
+            std::vector<float> one1(P1, 1.f), zero1(P1, 0.f), one2(nj, 1.f), zero2(nj, 0.f);
+            std::vector<void*> ptr((size_t)9 * E, nullptr);
+            void** A1 = ptr.data();
+            void** B1 = A1 + P1;
+            void** C1 = B1 + P1;
+            void** A2 = C1 + P1;
+            void** B2 = A2 + nj;
+            void** C2 = B2 + nj;
+            for (int j = 0; j < nj; j++) {
+                const uint16_t* w = static_cast<const uint16_t*>(jobs[j].ex.w1);
+                const int p0 = jobs[j].p0, n = jobs[j].n;
+                n1[j] = n1[nj + j] = n2[j] = n;
+                A1[j] = (void*)w;                      // gate rows
+                A1[nj + j] = (void*)(w + H);           // up rows
+                B1[j] = B1[nj + j] = c->d_pf_x + (size_t)p0 * H;
+                C1[j] = c->d_pf_g + (size_t)p0 * F;
+                C1[nj + j] = c->d_pf_u + (size_t)p0 * F;
+                A2[j] = (void*)(w + 2 * (size_t)H);    // down columns = W2 column-major
+                B2[j] = c->d_act + (size_t)p0 * F;
+                C2[j] = c->d_pf_y + (size_t)p0 * H;
+            }
+            void** dA1 = c->d_pf_ptr;
+            void** dB1 = dA1 + P1;
+            void** dC1 = dB1 + P1;
+            void** dA2 = dC1 + P1;
+            void** dB2 = dA2 + nj;
+            void** dC2 = dB2 + nj;
+            CUDA_TRY(cudaMemcpyAsync(c->d_pf_ptr, ptr.data(), sizeof(void*) * (3 * P1 + 3 * nj), cudaMemcpyHostToDevice, st));
+            CUDA_TRY(cudaStreamSynchronize(st));  // the host arrays above are read at launch
+            cublasSetStream(c->blas, st);
+            cublasStatus_t bs =
+                cublasGemmGroupedBatchedEx(c->blas, ta.data(), tb.data(), m1.data(), n1.data(), k1.data(), one1.data(),
+                                           (const void* const*)dA1, CUDA_R_16BF, lda1.data(), (const void* const*)dB1,
+                                           CUDA_R_16BF, ldb1.data(), zero1.data(), dC1, CUDA_R_16BF, ldc1.data(), P1,
+                                           gs1.data(), CUBLAS_COMPUTE_32F);
             if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped gate/up GEMM: cuBLAS status %d", (int)bs);
             CUDA_TRY(launch_swiglu_rows(c->d_pf_g, c->d_pf_u, (long)np * F, c->d_act, c->sm_count, st));
             launches++;
+            bs = cublasGemmGroupedBatchedEx(c->blas, ta2.data(), tb2.data(), m2.data(), n2.data(), k2.data(), one2.data(),
+                                            (const void* const*)dA2, CUDA_R_16BF, lda2.data(), (const void* const*)dB2,
+                                            CUDA_R_16BF, ldb2.data(), zero2.data(), dC2, CUDA_R_16BF, ldc2.data(), nj,
+                                            gs2.data(), CUBLAS_COMPUTE_32F);
+            if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped down GEMM: cuBLAS status %d", (int)bs);
         }
-        bs = cublasGemmGroupedBatchedEx(c->blas, ta2.data(), tb2.data(), m2.data(), n2.data(), k2.data(), one2.data(),
-                                        (const void* const*)dA2, CUDA_R_16BF, lda2.data(), (const void* const*)dB2,
-                                        CUDA_R_16BF, ldb2.data(), zero2.data(), dC2, CUDA_R_16BF, ldc2.data(), nj,
-                                        gs2.data(), CUBLAS_COMPUTE_32F);
-        if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped down GEMM: cuBLAS status %d", (int)bs);
+        CUDA_TRY(launch_combine_bf16(c->d_pf_y, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
+        launches++;
     }
-    CUDA_TRY(launch_combine_bf16(c->d_pf_y, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
-    launches++;
     c->launches += launches;
     *done = true;
     return MOE_OK;
@@ -663,7 +677,7 @@ int moe_destroy(moe_ctx* c) {
                   c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
     if (c->blas) cublasDestroy(c->blas);
-    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_ptr,
+    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_yf, (void*)c->d_pf_ptr,
                     (void*)c->d_tc_items})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);

@@ -2,11 +2,11 @@
 //
 // Semantics as the decode path (solar_hybrid/cpu_moe.cpp:38-96): g, u = gate/up rows . x_t,
 // act = bf16_rne(g / (1 + exp(-g)) * u), y = down . act, out[t] = sum of w * y over the token's
-// experts in job order.  The two contractions run as grouped GEMMs on the tensor cores (bf16
-// operands, fp32 accumulation), reading the context's unit tables in place; the grouped GEMM
-// interface returns bf16, so g, u and y are rounded to bf16 once at the GEMM outputs (the decode
-// paths keep them in fp32).  The kernels here supply the token gather, the SwiGLU epilogue and the
-// weighted combine (fp32).
+// experts in job order.  The two contractions run on the tensor cores (bf16 operands, fp32
+// accumulation), reading the context's unit tables in place: either the tcgen05 kernels of
+// prefill_tc.cu (g, u and y stay fp32, SwiGLU fused) or the library grouped GEMM, whose interface
+// returns bf16, so there g, u and y are rounded to bf16 once at the GEMM outputs.  The kernels here
+// supply the token gather, the library path's SwiGLU and the weighted combine (fp32).
 #include <algorithm>
 
 #include "common.cuh"
@@ -43,8 +43,20 @@ __global__ void __launch_bounds__(256) swiglu_rows_kernel(const uint16_t* g, con
 }
 
 // out[t, h] = (accumulate ? out : 0) + sum over the token's pairs (comb lists, job order) of
-// w[p] * y[p, h], y the bf16 output of the down GEMM.
-__global__ void __launch_bounds__(256) combine_bf16_kernel(const uint16_t* y, const float* w, const int32_t* comb_off,
+// w[p] * y[p, h]; y is the down GEMM's output, fp32 (tensor-core kernels) or bf16 (library GEMM).
+__device__ __forceinline__ void load8(const float* y, float v[8]) {
+    const float4 a = reinterpret_cast<const float4*>(y)[0], b = reinterpret_cast<const float4*>(y)[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const uint16_t* y, float v[8]) {
+    const uint4 q = *reinterpret_cast<const uint4*>(y);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[2 * k] = bf_lo(w[k]), v[2 * k + 1] = bf_hi(w[k]);
+}
+
+template <typename Y>
+__global__ void __launch_bounds__(256) combine_rows_kernel(const Y* y, const float* w, const int32_t* comb_off,
                                                            const int32_t* comb_p, int H, int accumulate, float* out) {
     const int t = blockIdx.y;
     const int h = (blockIdx.x * 256 + threadIdx.x) * 8;
@@ -57,24 +69,32 @@ __global__ void __launch_bounds__(256) combine_bf16_kernel(const uint16_t* y, co
         const int p = comb_p[i];
         if (p < 0) continue;
         const float wp = w[p];
-        const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)p * H + h);
-        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+        float v[8];
+        load8(y + (size_t)p * H + h, v);
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            acc[2 * k] = fmaf(wp, bf_lo(vw[k]), acc[2 * k]);
-            acc[2 * k + 1] = fmaf(wp, bf_hi(vw[k]), acc[2 * k + 1]);
-        }
+        for (int k = 0; k < 8; k++) acc[k] = fmaf(wp, v[k], acc[k]);
     }
     reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-cudaError_t launch_combine_bf16(const uint16_t* y, const float* w, const int32_t* comb_off, const int32_t* comb_p,
-                                int T, int H, int accumulate, float* out, cudaStream_t st) {
+template <typename Y>
+static cudaError_t launch_combine_y(const Y* y, const float* w, const int32_t* comb_off, const int32_t* comb_p, int T,
+                                   int H, int accumulate, float* out, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     dim3 g((H / 8 + 255) / 256, T);
-    combine_bf16_kernel<<<g, 256, 0, st>>>(y, w, comb_off, comb_p, H, accumulate, out);
+    combine_rows_kernel<Y><<<g, 256, 0, st>>>(y, w, comb_off, comb_p, H, accumulate, out);
     return cudaGetLastError();
+}
+
+cudaError_t launch_combine_bf16(const uint16_t* y, const float* w, const int32_t* comb_off, const int32_t* comb_p,
+                                int T, int H, int accumulate, float* out, cudaStream_t st) {
+    return launch_combine_y(y, w, comb_off, comb_p, T, H, accumulate, out, st);
+}
+
+cudaError_t launch_combine_rows(const float* y, const float* w, const int32_t* comb_off, const int32_t* comb_p, int T,
+                                int H, int accumulate, float* out, cudaStream_t st) {
+    return launch_combine_y(y, w, comb_off, comb_p, T, H, accumulate, out, st);
 }
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* ptok, int n, int H, uint16_t* xg, int sm_count,

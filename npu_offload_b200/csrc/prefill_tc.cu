@@ -1,6 +1,8 @@
-// Prefill gate/up GEMM on the 5th-generation tensor cores (tcgen05, sm_100a) with the SwiGLU
-// epilogue fused: act[p, f] = bf16_rne(g / (1 + exp(-g)) * u), g / u = gate / up row f . x_p in fp32
-// (solar_hybrid/cpu_moe.cpp:63-77), for the pairs p of every local bf16 expert job.
+// Prefill expert GEMMs on the 5th-generation tensor cores (tcgen05, sm_100a), for the pairs p of
+// every local bf16 expert job (solar_hybrid/cpu_moe.cpp:63-93):
+//   gate/up  act[p, f] = bf16_rne(g / (1 + exp(-g)) * u), g / u = gate / up row f . x_p in fp32
+//            (SwiGLU fused into the epilogue)
+//   down     y[p, h] = down row h . act_p in fp32 (MN-major weight operand: the stored down columns)
 //
 // One CTA = one tile: 256 pairs (two 128-row halves) x 128 intermediate indices of one job.
 //   producer warp   TMA (cp.async.bulk.tensor, 128-byte swizzle) of the gathered token rows
@@ -229,6 +231,134 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// ---- down projection: y[p, h] = sum_f act[p, f] * W2[h, f] (fp32) ----
+// One CTA = 256 pairs (two halves) x 256 outputs of one job.  A = activation rows (K-major, as above);
+// B = the job's down columns for f in the K step: a [64 f x 64 h] box per 64 outputs, i.e. MN-major
+// with 128-byte swizzle -- 64 h (128 bytes) contiguous per f row, 8-row swizzle atoms 1 KB apart
+// (SBO), the four 64-output chunks 8 KB apart (LBO); a K=16 step advances two whole atoms (2 KB).
+constexpr int kDnBN = 256;
+constexpr uint32_t kDnBBytes = kTcBK * kDnBN * 2;
+constexpr uint32_t kDnStageBytes = kTcABytes + kDnBBytes;
+constexpr size_t kDnSmem = (size_t)kTcStages * kDnStageBytes + 1024 + 256;
+
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr) {
+    cute::UMMA::SmemDescriptor d;
+    d.desc_ = 0;
+    d.start_address_ = (uint16_t)(saddr >> 4);
+    d.leading_byte_offset_ = (kTcBK * 128) >> 4;  // next 64-output chunk
+    d.stride_byte_offset_ = 1024 >> 4;            // next 8 K rows
+    d.version_ = 1;
+    d.base_offset_ = 0;
+    d.lbo_mode_ = 0;
+    d.layout_type_ = (uint8_t)cute::UMMA::LayoutType::SWIZZLE_128B;
+    return d.desc_;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    down_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_d,
+                   const TcItem* __restrict__ items, int H, int F, float* __restrict__ y, uint32_t* err,
+                   uint64_t timeout_ns) {
+    extern __shared__ __align__(1024) unsigned char tsm[];
+    unsigned char* ring = reinterpret_cast<unsigned char*>(((uintptr_t)tsm + 1023) & ~(uintptr_t)1023);
+    TcCtrl& c = *reinterpret_cast<TcCtrl*>(ring + (size_t)kTcStages * kDnStageBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const TcItem it = items[blockIdx.x];  // f0 holds the first output h of the tile
+    const int nk = F / kTcBK;
+    const bool two = it.rows > 128;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStages; s++) {
+            mbar_init(&c.full[s], 1);
+            mbar_init(&c.empty[s], 1);
+        }
+        mbar_init(&c.accum, 1);
+        mbar_init(&c.done, 1);
+        c.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kTcMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&c.tmem)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = c.tmem;
+    const uint64_t deadline = globaltimer_ns() + timeout_ns;
+
+    if (warp == kTcProdWarp) {
+        if (lane == 0) {
+            int k = 0;
+            for (; k < nk; k++) {
+                const int s = k % kTcStages;
+                if (k >= kTcStages && !tc_wait(&c.empty[s], ((k / kTcStages) & 1) ^ 1, &c.abort, err, deadline)) break;
+                unsigned char* st = ring + (size_t)s * kDnStageBytes;
+                mbar_arrive_expect_tx(&c.full[s], kDnStageBytes);
+                tma_load_2d(st, &map_a, k * kTcBK, it.row0, &c.full[s]);
+#pragma unroll
+                for (int j = 0; j < kDnBN / 64; j++)
+                    tma_load_3d(st + kTcABytes + j * (kTcBK * 128), &map_d, 2 * H + it.f0 + j * 64, k * kTcBK, it.slot,
+                                &c.full[s]);
+            }
+            const uint64_t dd = globaltimer_ns() + timeout_ns;
+            for (int q = k > kTcStages ? k - kTcStages : 0; q < k; q++)
+                while (!mbar_try_wait(&c.full[q % kTcStages], (q / kTcStages) & 1))
+                    if (globaltimer_ns() > dd) break;
+        }
+    } else if (warp == kTcMmaWarp) {
+        if (lane == 0) {
+            const uint32_t idesc = (uint32_t)cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, kDnBN,
+                                                                          cute::UMMA::Major::K, cute::UMMA::Major::MN>();
+            for (int k = 0; k < nk; k++) {
+                const int s = k % kTcStages;
+                if (!tc_wait(&c.full[s], (k / kTcStages) & 1, &c.abort, err, deadline)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(ring + (size_t)s * kDnStageBytes), sb = sa + kTcABytes;
+#pragma unroll
+                for (int kk = 0; kk < kTcBK / 16; kk++) {
+                    const uint32_t acc = (k | kk) != 0;
+                    const uint64_t db = sw128_mn_desc(sb + kk * 2048);
+                    umma_bf16(tmem + 0, sw128_desc(sa + kk * 32), db, idesc, acc);
+                    if (two) umma_bf16(tmem + 256, sw128_desc(sa + 128 * 128 + kk * 32), db, idesc, acc);
+                }
+                umma_commit(&c.empty[s]);
+            }
+            umma_commit(&c.accum);
+        }
+    } else {
+        const int h = warp / 4, q = warp % 4;
+        const int r = h * 128 + q * 32 + lane;
+        if (tc_wait(&c.accum, 0, &c.abort, err, deadline) && (h == 0 || two)) {
+            tc_fence_after();
+            const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+            for (int c0 = 0; c0 < kDnBN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_addr + h * 256 + c0, v);
+                tmem_wait_ld();
+                if (r < it.rows) {
+                    float4* dst = reinterpret_cast<float4*>(y + (size_t)(it.row0 + r) * H + it.f0 + c0);
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                             __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                }
+            }
+        }
+    }
+    if (warp == kTcMmaWarp && lane == 0 && *(volatile int*)&c.abort) {
+        umma_commit(&c.done);
+        const uint64_t dd = globaltimer_ns() + timeout_ns;
+        while (!mbar_try_wait(&c.done, 0))
+            if (globaltimer_ns() > dd) break;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kTcMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+}
+
 // ---- host side ----
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -254,7 +384,38 @@ static EncodeTiledFn encode_fn() {
 bool tc_available() { return encode_fn() != nullptr; }
 
 cudaError_t tc_set_smem_limit() {
-    return cudaFuncSetAttribute(gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    cudaError_t e = cudaFuncSetAttribute(gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDnSmem);
+    return e;
+}
+
+cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, int n_slots, size_t slot_bytes,
+                           const TcItem* items, int n_items, int H, int F, float* y, uint32_t* err, uint64_t timeout_ns,
+                           cudaStream_t st) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    if (H % kDnBN || F % kTcBK || slot_bytes % 16 || ((uintptr_t)act | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
+    CUtensorMap ma, md;
+    {  // activation rows: [arows][F] bf16
+        const cuuint64_t dims[2] = {(cuuint64_t)F, (cuuint64_t)arows};
+        const cuuint64_t strides[1] = {(cuuint64_t)F * 2};
+        const cuuint32_t box[2] = {kTcBK, kTcBM}, es[2] = {1, 1};
+        if (enc(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)act, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {  // unit tables, down columns at element 2H of each unit: boxes of 64 outputs x 64 f
+        const cuuint64_t dims[3] = {(cuuint64_t)3 * H, (cuuint64_t)F, (cuuint64_t)n_slots};
+        const cuuint64_t strides[2] = {(cuuint64_t)6 * H, (cuuint64_t)slot_bytes};
+        const cuuint32_t box[3] = {64, kTcBK, 1}, es[3] = {1, 1, 1};
+        if (enc(&md, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void*)arena, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    if (n_items <= 0) return cudaSuccess;
+    down_tc_kernel<<<n_items, kTcThreads, kDnSmem, st>>>(ma, md, items, H, F, y, err, timeout_ns);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, int n_slots, size_t slot_bytes,

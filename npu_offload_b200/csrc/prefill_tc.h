@@ -21,4 +21,10 @@ cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, i
                              const TcItem* items, int n_items, int H, int F, uint16_t* act, uint32_t* err,
                              uint64_t timeout_ns, cudaStream_t st);
 
+// y[p, h] (fp32) for every item (TcItem.f0 = first output h, 256 per tile).  act: [arows][F] bf16
+// activation rows; arena as above.  H % 256 == 0, F % 64 == 0.
+cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, int n_slots, size_t slot_bytes,
+                           const TcItem* items, int n_items, int H, int F, float* y, uint32_t* err, uint64_t timeout_ns,
+                           cudaStream_t st);
+
 }  // namespace moe
