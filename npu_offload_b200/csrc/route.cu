@@ -23,9 +23,19 @@ __global__ void __launch_bounds__(256) route_topk_kernel(RouteArgs a) {
     if (t < a.T) route_token_warp(a, t, scr[warp]);
 }
 
-// Counting-sort permutation of the routed pairs; one 1024-thread block.  Shared use:
-// counts/firstpos/jrank [E] ints, plus 8-bit copies of idx [T*K].
-__device__ void permute_block(const RouteArgs& a, unsigned char* idx8) {
+// Counting-sort permutation of the routed pairs; one 1024-thread block.  Tokens are taken in tiles
+// of 32 (one token per lane, one warp per tile): a tile's pairs of expert e are the lanes set in a
+// per-warp 32-bit mask, so a pair's rank inside its tile is a popcount and the tile's count of e
+// one more; an exclusive scan over the tiles per expert turns the counts into tile bases.  Every
+// result is a pure function of idx (masks are ORed, first positions taken by min), so the
+// permutation is deterministic.  Dynamic shared layout (permute_smem_bytes): per-warp masks
+// [32][E] u32, tile counts / bases [ceil(T/32)][E] u16 (a per-expert count is at most T), then
+// 8-bit copies of idx [T*K].
+__host__ __device__ constexpr size_t permute_smem_bytes(int T, int K, int E) {
+    return (size_t)32 * E * 4 + (((size_t)(T + 31) / 32 * E * 2 + 15) & ~(size_t)15) + (size_t)T * K;
+}
+
+__device__ void permute_block(const RouteArgs& a, unsigned char* dyn) {
     __shared__ int counts[kMaxExperts];
     __shared__ int firstpos[kMaxExperts];
     __shared__ int offs[kMaxExperts + 1];
@@ -34,11 +44,14 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* idx8) {
     const int E = a.E, K = a.K, T = a.T, NP = T * K;
     const int tid = threadIdx.x, nth = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = nth >> 5;
-    for (int e = tid; e < E; e += nth) {
-        counts[e] = 0;
-        firstpos[e] = 0x7fffffff;
-    }
-    __syncthreads();
+    const int ntiles = (T + 31) / 32;
+    uint32_t* wmask = reinterpret_cast<uint32_t*>(dyn) + warp * E;  // this warp's masks
+    uint16_t* tcnt = reinterpret_cast<uint16_t*>(dyn + (size_t)32 * E * 4);
+    unsigned char* idx8 = dyn + permute_smem_bytes(T, K, E) - (size_t)NP;
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int e = tid; e < E; e += nth) firstpos[e] = 0x7fffffff;
+    for (int i = tid; i < 32 * E; i += nth) reinterpret_cast<uint32_t*>(dyn)[i] = 0;
+    for (int i = tid; i < ntiles * E; i += nth) tcnt[i] = 0;
     for (int q = tid; q < NP; q += nth) {
         int e = a.idx[q];
         if (e < 0 || e >= E) {  // only reachable through a corrupted idx buffer
@@ -46,8 +59,38 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* idx8) {
             e = 0;
         }
         idx8[q] = (unsigned char)e;
-        atomicAdd(&counts[e], 1);
-        atomicMin(&firstpos[e], q);
+    }
+    __syncthreads();
+    // per-tile counts and first appearances (the lowest lane of a mask holds the tile's first pair)
+    for (int tile = warp; tile < ntiles; tile += nwarps) {
+        const int t = tile * 32 + lane;
+        const bool on = t < T;
+        for (int k = 0; k < K; k++)
+            if (on) atomicOr(&wmask[idx8[t * K + k]], 1u << lane);
+        __syncwarp();
+        for (int k = 0; k < K; k++)
+            if (on) {
+                const int e = idx8[t * K + k];
+                const uint32_t m = wmask[e];
+                if (!(m & lt)) {
+                    tcnt[tile * E + e] = (uint16_t)__popc(m);
+                    atomicMin(&firstpos[e], t * K + k);
+                }
+            }
+        __syncwarp();
+        for (int k = 0; k < K; k++)
+            if (on) wmask[idx8[t * K + k]] = 0;
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nth) {  // exclusive scan over tiles: counts -> tile bases
+        int acc = 0;
+        for (int tile = 0; tile < ntiles; tile++) {
+            const int c = tcnt[tile * E + e];
+            tcnt[tile * E + e] = (uint16_t)acc;
+            acc += c;
+        }
+        counts[e] = acc;
     }
     __syncthreads();
     if (tid == 0) {
@@ -105,27 +148,27 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* idx8) {
     }
     if (tid == 0 && a.offsets) a.offsets[E] = offs[E];
     __syncthreads();
-    // stable placement: warp per expert, tokens ascending via ballot ranks
-    for (int e = warp; e < E; e += nwarps) {
-        if (counts[e] == 0) continue;
-        int base = offs[e];
-        for (int t0 = 0; t0 < T; t0 += 32) {
-            int t = t0 + lane;
-            int kk = -1;
-            if (t < T)
-                for (int k = 0; k < K; k++)
-                    if (idx8[t * K + k] == e) kk = k;
-            unsigned bal = __ballot_sync(0xffffffffu, kk >= 0);
-            if (kk >= 0) {
-                int pos = base + __popc(bal & ((1u << lane) - 1u));
-                int q = t * K + kk;
+    // stable placement: position = expert offset + tile base + rank inside the tile (tokens ascending)
+    for (int tile = warp; tile < ntiles; tile += nwarps) {
+        const int t = tile * 32 + lane;
+        const bool on = t < T;
+        for (int k = 0; k < K; k++)
+            if (on) atomicOr(&wmask[idx8[t * K + k]], 1u << lane);
+        __syncwarp();
+        for (int k = 0; k < K; k++)
+            if (on) {
+                const int e = idx8[t * K + k];
+                const int pos = offs[e] + tcnt[tile * E + e] + __popc(wmask[e] & lt);
+                const int q = t * K + k;
                 if (a.perm) a.perm[pos] = q;
                 if (a.ptok) a.ptok[pos] = t;
                 if (a.pw) a.pw[pos] = a.w[q];
                 if (a.pairpos) a.pairpos[q] = pos;
             }
-            base += __popc(bal);
-        }
+        __syncwarp();
+        for (int k = 0; k < K; k++)
+            if (on) wmask[idx8[t * K + k]] = 0;
+        __syncwarp();
     }
     __syncthreads();
     // per-token pair list in job order (the order the reference accumulates, cpu_moe.cpp:81-93);
@@ -158,30 +201,29 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* idx8) {
 }
 
 __global__ void __launch_bounds__(1024) permute_kernel(RouteArgs a) {
-    extern __shared__ unsigned char idx8[];
-    permute_block(a, idx8);
+    extern __shared__ __align__(16) unsigned char pdyn[];
+    permute_block(a, pdyn);
 }
 
 // Small batches: routing and permutation in one launch.
 __global__ void __launch_bounds__(1024) route_fused_kernel(RouteArgs a) {
     extern __shared__ __align__(16) unsigned char dyn[];
     float* scr = reinterpret_cast<float*>(dyn);  // [32][2 * kMaxExperts]
-    unsigned char* idx8 = dyn + 32 * 2 * kMaxExperts * sizeof(float);
     const int warp = threadIdx.x >> 5;
     for (int t = warp; t < a.T; t += 32) route_token_warp(a, t, scr + warp * 2 * kMaxExperts);
     __syncthreads();
-    permute_block(a, idx8);
+    permute_block(a, dyn + 32 * 2 * kMaxExperts * sizeof(float));
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     if (a.T <= 64) {
-        size_t sm = 32 * 2 * kMaxExperts * sizeof(float) + (size_t)a.T * a.K;
+        size_t sm = 32 * 2 * kMaxExperts * sizeof(float) + permute_smem_bytes(a.T, a.K, a.E);
         route_fused_kernel<<<1, 1024, sm, st>>>(a);
         if (launches) *launches += 1;
         return cudaGetLastError();
     }
     if (a.T > 0) route_topk_kernel<<<(a.T + 7) / 8, 256, 0, st>>>(a);
-    size_t sm = (size_t)a.T * a.K;
+    size_t sm = permute_smem_bytes(a.T, a.K, a.E);
     permute_kernel<<<1, 1024, sm, st>>>(a);
     if (launches) *launches += a.T > 0 ? 2 : 1;
     return cudaGetLastError();
@@ -189,10 +231,10 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
 
 cudaError_t route_set_smem_limits() {
     cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kMaxTokens * kMaxTopK);
+                                         (int)permute_smem_bytes(kMaxTokens, kMaxTopK, kMaxExperts));
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                32 * 2 * kMaxExperts * sizeof(float) + 64 * kMaxTopK);
+                                (int)(32 * 2 * kMaxExperts * sizeof(float) + permute_smem_bytes(64, kMaxTopK, kMaxExperts)));
 }
 
 }  // namespace moe

@@ -102,6 +102,14 @@ def test_route_other_shapes(planes, E, K):
     _check_route(planes(E, K).route(lg), lg, K, E)
 
 
+@pytest.mark.parametrize("E,K,T", [(256, 16, 4096), (200, 7, 1000), (16, 4, 33)])
+def test_permutation_large_and_ragged(planes, E, K, T):
+    """Largest shared-memory footprint (4096 tokens x top-16 over 256 experts) and ragged token tiles."""
+    from npu_offload_b200 import synth
+    lg = synth.logits(11 + T, T, E, zipf=True)
+    _check_route(planes(E, K).route(lg), lg, K, E)
+
+
 def test_route_sigmoid_reference_golden(planes, golden):
     g = golden("route_sigmoid.npz")
     E, K = g["logits"].shape[1], int(g["K"])
