@@ -35,52 +35,136 @@ __host__ __device__ constexpr size_t permute_smem_bytes(int T, int K, int E) {
     return (size_t)32 * E * 4 + (((size_t)(T + 31) / 32 * E * 2 + 15) & ~(size_t)15) + (size_t)T * K;
 }
 
+struct PermShared {
+    int firstpos[kMaxExperts];  // first pair index q = t*K + k of each expert (INT_MAX: absent)
+    int counts[kMaxExperts];
+    int offs[kMaxExperts + 1];  // expert-major grouped offsets (expert id order)
+    int jrank[kMaxExperts];     // first-appearance rank among active experts (-1: absent)
+    int lrank[kMaxExperts];     // the same among active local experts
+    unsigned char remote[kMaxExperts];
+};
+
+// Count pass over one tile: idx -> idx8 (validated), tile counts, first appearances.
+template <int KM>
+__device__ __forceinline__ void permute_count_tile(const RouteArgs& a, PermShared& ps, uint32_t* wmask, uint16_t* tcnt,
+                                                   unsigned char* idx8, int tile) {
+    const int lane = threadIdx.x & 31, K = a.K, E = a.E;
+    const int t = tile * 32 + lane;
+    const bool on = t < a.T;
+    const uint32_t lt = (1u << lane) - 1u;
+    int ek[KM];
+#pragma unroll
+    for (int k = 0; k < KM; k++) ek[k] = (on && k < K) ? a.idx[(size_t)t * K + k] : 0;
+#pragma unroll
+    for (int k = 0; k < KM; k++)
+        if (on && k < K) {
+            if (ek[k] < 0 || ek[k] >= E) {  // only reachable through a corrupted idx buffer
+                atomicOr(a.err, kErrBadIndex);
+                ek[k] = 0;
+            }
+            idx8[t * K + k] = (unsigned char)ek[k];
+            atomicOr(&wmask[ek[k]], 1u << lane);
+        }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < KM; k++)
+        if (on && k < K) {
+            const uint32_t m = wmask[ek[k]];
+            if (!(m & lt)) {  // the tile's first pair of this expert
+                tcnt[tile * E + ek[k]] = (uint16_t)__popc(m);
+                atomicMin(&ps.firstpos[ek[k]], t * K + k);
+            }
+        }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < KM; k++)
+        if (on && k < K) wmask[ek[k]] = 0;
+    __syncwarp();
+}
+
+// Placement pass over one tile: grouped position = expert offset + tile base + rank in the tile
+// (tokens ascending, cpu_moe's per-expert token lists); the token's combine list is its positions
+// ordered by job rank (the order the reference accumulates, cpu_moe.cpp:81-93), pairs owned by
+// another rank marked -1.
+template <int KM>
+__device__ __forceinline__ void permute_place_tile(const RouteArgs& a, const PermShared& ps, uint32_t* wmask,
+                                                   const uint16_t* tcnt, const unsigned char* idx8, int tile) {
+    const int lane = threadIdx.x & 31, K = a.K, E = a.E;
+    const int t = tile * 32 + lane;
+    const bool on = t < a.T;
+    const uint32_t lt = (1u << lane) - 1u;
+    int ek[KM];
+    float wk[KM];
+#pragma unroll
+    for (int k = 0; k < KM; k++) {
+        ek[k] = (on && k < K) ? idx8[t * K + k] : 0;
+        wk[k] = (on && k < K && a.pw) ? a.w[(size_t)t * K + k] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < KM; k++)
+        if (on && k < K) atomicOr(&wmask[ek[k]], 1u << lane);
+    __syncwarp();
+    int rk[KM], pp[KM];
+#pragma unroll
+    for (int k = 0; k < KM; k++) {
+        rk[k] = 0x7fffffff;
+        pp[k] = -1;
+        if (on && k < K) {
+            const int e = ek[k];
+            const int pos = ps.offs[e] + tcnt[tile * E + e] + __popc(wmask[e] & lt);
+            const int q = t * K + k;
+            if (a.perm) a.perm[pos] = q;
+            if (a.ptok) a.ptok[pos] = t;
+            if (a.pw) a.pw[pos] = wk[k];
+            if (a.pairpos) a.pairpos[q] = pos;
+            rk[k] = ps.jrank[e];
+            pp[k] = ps.remote[e] ? -1 : pos;
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < KM; k++)
+        if (on && k < K) wmask[ek[k]] = 0;
+    __syncwarp();
+    if (a.comb_p && on) {
+        // odd-even transposition sort by job rank (distinct for a token's distinct experts)
+#pragma unroll
+        for (int r = 0; r < KM; r++)
+#pragma unroll
+            for (int i = r & 1; i + 1 < KM; i += 2)
+                if (rk[i] > rk[i + 1]) {
+                    const int tr = rk[i], tp = pp[i];
+                    rk[i] = rk[i + 1], pp[i] = pp[i + 1];
+                    rk[i + 1] = tr, pp[i + 1] = tp;
+                }
+#pragma unroll
+        for (int k = 0; k < KM; k++)
+            if (k < K) a.comb_p[t * K + k] = pp[k];
+        a.comb_off[t] = t * K;
+    }
+}
+
 __device__ void permute_block(const RouteArgs& a, unsigned char* dyn) {
-    __shared__ int counts[kMaxExperts];
-    __shared__ int firstpos[kMaxExperts];
-    __shared__ int offs[kMaxExperts + 1];
-    __shared__ int jrank[kMaxExperts];
-    __shared__ int lrank[kMaxExperts];
-    const int E = a.E, K = a.K, T = a.T, NP = T * K;
+    __shared__ PermShared ps;
+    const int E = a.E, K = a.K, T = a.T;
     const int tid = threadIdx.x, nth = blockDim.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = nth >> 5;
     const int ntiles = (T + 31) / 32;
     uint32_t* wmask = reinterpret_cast<uint32_t*>(dyn) + warp * E;  // this warp's masks
     uint16_t* tcnt = reinterpret_cast<uint16_t*>(dyn + (size_t)32 * E * 4);
-    unsigned char* idx8 = dyn + permute_smem_bytes(T, K, E) - (size_t)NP;
-    const uint32_t lt = (1u << lane) - 1u;
-    for (int e = tid; e < E; e += nth) firstpos[e] = 0x7fffffff;
+    unsigned char* idx8 = dyn + permute_smem_bytes(T, K, E) - (size_t)T * K;
+    for (int e = tid; e < E; e += nth) {
+        ps.firstpos[e] = 0x7fffffff;
+        ps.remote[e] = a.desc != nullptr && a.desc[e].kind == kKindRemote;
+    }
     for (int i = tid; i < 32 * E; i += nth) reinterpret_cast<uint32_t*>(dyn)[i] = 0;
     for (int i = tid; i < ntiles * E; i += nth) tcnt[i] = 0;
-    for (int q = tid; q < NP; q += nth) {
-        int e = a.idx[q];
-        if (e < 0 || e >= E) {  // only reachable through a corrupted idx buffer
-            atomicOr(a.err, kErrBadIndex);
-            e = 0;
-        }
-        idx8[q] = (unsigned char)e;
-    }
     __syncthreads();
-    // per-tile counts and first appearances (the lowest lane of a mask holds the tile's first pair)
     for (int tile = warp; tile < ntiles; tile += nwarps) {
-        const int t = tile * 32 + lane;
-        const bool on = t < T;
-        for (int k = 0; k < K; k++)
-            if (on) atomicOr(&wmask[idx8[t * K + k]], 1u << lane);
-        __syncwarp();
-        for (int k = 0; k < K; k++)
-            if (on) {
-                const int e = idx8[t * K + k];
-                const uint32_t m = wmask[e];
-                if (!(m & lt)) {
-                    tcnt[tile * E + e] = (uint16_t)__popc(m);
-                    atomicMin(&firstpos[e], t * K + k);
-                }
-            }
-        __syncwarp();
-        for (int k = 0; k < K; k++)
-            if (on) wmask[idx8[t * K + k]] = 0;
-        __syncwarp();
+        if (K <= 8)
+            permute_count_tile<8>(a, ps, wmask, tcnt, idx8, tile);
+        else
+            permute_count_tile<kMaxTopK>(a, ps, wmask, tcnt, idx8, tile);
     }
     __syncthreads();
     for (int e = tid; e < E; e += nth) {  // exclusive scan over tiles: counts -> tile bases
@@ -90,49 +174,67 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* dyn) {
             tcnt[tile * E + e] = (uint16_t)acc;
             acc += c;
         }
-        counts[e] = acc;
+        ps.counts[e] = acc;
     }
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0;
-        for (int e = 0; e < E; e++) {
-            offs[e] = acc;
-            acc += counts[e];
+    if (warp == 0) {  // expert offsets (ascending id), job counts: one warp, E/32 experts per lane
+        const int per = (E + 31) / 32, e0 = lane * per;
+        int sum = 0, nj = 0, nl = 0;
+        for (int e = e0; e < e0 + per && e < E; e++) {
+            sum += ps.counts[e];
+            nj += ps.counts[e] > 0;
+            nl += ps.counts[e] > 0 && !ps.remote[e];
         }
-        offs[E] = acc;
-    }
-    // job rank = rank of the first appearance among active experts (runtime.py:343-354)
-    for (int e = tid; e < E; e += nth) {
-        int r = -1, lr = -1;
-        if (counts[e] > 0) {
-            r = 0;
-            lr = 0;
-            for (int e2 = 0; e2 < E; e2++)
-                if (counts[e2] > 0 && firstpos[e2] < firstpos[e]) {
-                    r++;
-                    if (a.desc == nullptr || a.desc[e2].kind != kKindRemote) lr++;
-                }
+        int inc = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
         }
-        jrank[e] = r;
-        lrank[e] = lr;
+        int acc = inc - sum;
+        for (int e = e0; e < e0 + per && e < E; e++) {
+            ps.offs[e] = acc;
+            acc += ps.counts[e];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            nj += __shfl_xor_sync(0xffffffffu, nj, o);
+            nl += __shfl_xor_sync(0xffffffffu, nl, o);
+        }
+        if (lane == 31) ps.offs[E] = inc;
+        if (lane == 0) {
+            if (a.n_jobs) *a.n_jobs = nj;
+            if (a.n_ljobs) *a.n_ljobs = nl;
+        }
     }
-    __syncthreads();
-    if (tid == 0) {
-        int nj = 0, nl = 0;
-        for (int e = 0; e < E; e++)
-            if (counts[e] > 0) {
-                nj++;
-                if (a.desc == nullptr || a.desc[e].kind != kKindRemote) nl++;
+    // job rank = rank of the first appearance among active experts (runtime.py:343-354): a warp per
+    // expert, the lanes splitting the comparison set
+    for (int e = warp; e < E; e += nwarps) {
+        const int fp = ps.firstpos[e];
+        int r = 0, lr = 0;
+        for (int e2 = lane; e2 < E; e2 += 32)
+            if (ps.firstpos[e2] < fp) {
+                r++;
+                lr += !ps.remote[e2];
             }
-        if (a.n_jobs) *a.n_jobs = nj;
-        if (a.n_ljobs) *a.n_ljobs = nl;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            r += __shfl_xor_sync(0xffffffffu, r, o);
+            lr += __shfl_xor_sync(0xffffffffu, lr, o);
+        }
+        if (lane == 0) {
+            ps.jrank[e] = fp == 0x7fffffff ? -1 : r;
+            ps.lrank[e] = fp == 0x7fffffff || ps.remote[e] ? -1 : lr;
+        }
     }
+    __syncthreads();
     for (int e = tid; e < E; e += nth) {
-        if (a.counts) a.counts[e] = counts[e];
-        if (a.offsets) a.offsets[e] = offs[e];
-        if (counts[e] > 0) {
-            if (a.job_order) a.job_order[jrank[e]] = e;
-            if (a.jobs && lrank[e] >= 0 && (a.desc == nullptr || a.desc[e].kind != kKindRemote)) {
+        const int cnt = ps.counts[e];
+        if (a.counts) a.counts[e] = cnt;
+        if (a.offsets) a.offsets[e] = ps.offs[e];
+        if (cnt > 0) {
+            if (a.job_order) a.job_order[ps.jrank[e]] = e;
+            if (a.jobs && ps.lrank[e] >= 0) {
                 Job jb;
                 if (a.desc) {
                     jb.ex = a.desc[e];
@@ -140,64 +242,20 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* dyn) {
                 } else {
                     jb.ex = ExpDesc{nullptr, nullptr, nullptr, 0, 0};
                 }
-                jb.p0 = offs[e];
-                jb.n = jb.ex.kind == kKindBF16 || jb.ex.kind == kKindQ8 ? counts[e] : 0;
-                a.jobs[lrank[e]] = jb;
+                jb.p0 = ps.offs[e];
+                jb.n = jb.ex.kind == kKindBF16 || jb.ex.kind == kKindQ8 ? cnt : 0;
+                a.jobs[ps.lrank[e]] = jb;
             }
         }
     }
-    if (tid == 0 && a.offsets) a.offsets[E] = offs[E];
-    __syncthreads();
-    // stable placement: position = expert offset + tile base + rank inside the tile (tokens ascending)
+    if (tid == 0 && a.offsets) a.offsets[E] = ps.offs[E];
     for (int tile = warp; tile < ntiles; tile += nwarps) {
-        const int t = tile * 32 + lane;
-        const bool on = t < T;
-        for (int k = 0; k < K; k++)
-            if (on) atomicOr(&wmask[idx8[t * K + k]], 1u << lane);
-        __syncwarp();
-        for (int k = 0; k < K; k++)
-            if (on) {
-                const int e = idx8[t * K + k];
-                const int pos = offs[e] + tcnt[tile * E + e] + __popc(wmask[e] & lt);
-                const int q = t * K + k;
-                if (a.perm) a.perm[pos] = q;
-                if (a.ptok) a.ptok[pos] = t;
-                if (a.pw) a.pw[pos] = a.w[q];
-                if (a.pairpos) a.pairpos[q] = pos;
-            }
-        __syncwarp();
-        for (int k = 0; k < K; k++)
-            if (on) wmask[idx8[t * K + k]] = 0;
-        __syncwarp();
+        if (K <= 8)
+            permute_place_tile<8>(a, ps, wmask, tcnt, idx8, tile);
+        else
+            permute_place_tile<kMaxTopK>(a, ps, wmask, tcnt, idx8, tile);
     }
-    __syncthreads();
-    // per-token pair list in job order (the order the reference accumulates, cpu_moe.cpp:81-93);
-    // pairs of experts owned by another rank are marked -1
-    if (a.comb_p) {
-        for (int t = tid; t < T; t += nth) {
-            int rk[kMaxTopK], pp[kMaxTopK];
-            for (int k = 0; k < K; k++) {
-                int e = idx8[t * K + k];
-                rk[k] = jrank[e];
-                bool remote = a.desc != nullptr && a.desc[e].kind == kKindRemote;
-                pp[k] = remote ? -1 : a.pairpos[t * K + k];
-            }
-            for (int i = 1; i < K; i++) {  // insertion sort by job rank
-                int r = rk[i], p = pp[i], j = i - 1;
-                while (j >= 0 && rk[j] > r) {
-                    rk[j + 1] = rk[j];
-                    pp[j + 1] = pp[j];
-                    j--;
-                }
-                rk[j + 1] = r;
-                pp[j + 1] = p;
-            }
-            for (int k = 0; k < K; k++) a.comb_p[t * K + k] = pp[k];
-            a.comb_off[t] = t * K;
-            if (t == T - 1) a.comb_off[T] = T * K;
-        }
-        if (T == 0 && tid == 0) a.comb_off[0] = 0;
-    }
+    if (a.comb_p && tid == 0) a.comb_off[T] = T * K;
 }
 
 __global__ void __launch_bounds__(1024) permute_kernel(RouteArgs a) {
