@@ -41,7 +41,7 @@ METRIC = "MoE-layer decode tokens/s and achieved HBM GB/s vs peak"
 UNIT = "MoE-layer tokens/s"
 # DRAM bytes (read + write) per algorithmic byte of decode_kernel, from the committed ncu capture of
 # one T=1 layer (profiles/decode_kernel_T1.md); None until a capture exists.
-TRAFFIC_RATIO = 255.278 / 251.658
+TRAFFIC_RATIO = 255.443 / 251.658
 TRAFFIC_SOURCE = "profiles/decode_kernel_T1.md"
 
 

@@ -155,7 +155,7 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
     for (int t = 0; t < NT; t++)
 #pragma unroll
         for (int cc = 0; cc < CH; cc++) {
-            const uint4 xv = valid[cc] ? __ldg(reinterpret_cast<const uint4*>(a.x + (size_t)sg.tok[t] * H + eoff[cc]))
+            const uint4 xv = valid[cc] ? ld_cg_u4(a.x + (size_t)sg.tok[t] * H + eoff[cc])
                                        : make_uint4(0, 0, 0, 0);
             xw[t][cc][0] = xv.x;
             xw[t][cc][1] = xv.y;

@@ -86,6 +86,8 @@ struct PlanArgs {
     int gmax;              // tokens per token group (<= kGroupMax)
     int ups_bf16, ups_q8;  // units per ring stage of each kind
     uint64_t* timeline;    // optional kTimelineSlots phase stamps of the plan kernel, else null
+    const uint16_t* x_src; // optional: hidden states in device-accessible pinned host memory, copied
+    uint16_t* x_dst;       //   by the plan kernel to x_dst ([T, H] bf16) before it publishes the plan
 };
 
 struct DecodeArgs {

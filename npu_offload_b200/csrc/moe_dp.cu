@@ -144,6 +144,7 @@ struct moe_ctx {
     void** d_pf_ptr = nullptr;          // [9 * E] grouped-GEMM operand pointers
     bool prefill_tc = true;             // gate/up and down on the tcgen05 kernels; else cuBLAS
     TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels
+    uint32_t* d_tc_sched = nullptr;     // [4] tile-schedule counters (gate/up, down), left zero by each launch
     int tc_items_cap = 0;
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
@@ -326,7 +327,7 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
 
 // Launches plan_kernel + decode_kernel for one layer (da prepared by prepare_fused, x / out set).
 int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t dsmem, cudaStream_t st,
-                 cudaEvent_t* marks) {
+                 cudaEvent_t* marks, const uint16_t* x_host = nullptr) {
     const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
     da.ep = next_ep(c);
     const uint32_t epoch = c->epoch++;
@@ -351,6 +352,10 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     pa.ups_bf16 = da.ups_bf16;
     pa.ups_q8 = da.ups_q8;
     pa.timeline = c->d_timeline ? c->d_timeline + (size_t)(c->sm_count - 1) * kTimelineSlots : nullptr;
+    if (x_host) {  // the plan kernel moves the hidden states: da.x is the device copy it writes
+        pa.x_src = x_host;
+        pa.x_dst = const_cast<uint16_t*>(da.x);
+    }
     cudaError_t e = launch_plan(pa, st);
     if (e != cudaSuccess) return fail(MOE_ECUDA, "plan launch: %s", cudaGetErrorString(e));
     if (marks) cudaEventRecord(marks[1], st);
@@ -403,15 +408,21 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         if (!st2) st2 = dalloc(&c->d_pf_y, NP * H);
         if (!st2) st2 = dalloc(&c->d_pf_yf, NP * H);
         if (!st2) st2 = dalloc(&c->d_pf_ptr, (size_t)9 * E);
+        if (!st2) st2 = dalloc(&c->d_tc_sched, 4);
+        if (!st2 && cudaMemset(c->d_tc_sched, 0, 4 * sizeof(uint32_t)) != cudaSuccess) st2 = fail(MOE_ECUDA, "memset");
         if (st2) return st2;
     }
     int launches = 0;
     if (nj > 0 && tc) {
         // tile lists: gate/up tiles (TcItem.f0 = first f), then down tiles (TcItem.f0 = first output h)
+        // jobs with the most pairs first (their tiles carry both halves), so the schedule ends on light tiles
+        std::vector<int> order(nj);
+        for (int j = 0; j < nj; j++) order[j] = j;
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return jobs[a].n > jobs[b].n; });
         std::vector<TcItem> items;
         int n_gu = 0;
         for (int pass = 0; pass < 2; pass++) {
-            for (int j = 0; j < nj; j++) {
+            for (int j : order) {
                 const long slot = ((const char*)jobs[j].ex.w1 - (const char*)c->arena[layer]) / (long)c->stride;
                 for (int m0 = 0; m0 < jobs[j].n; m0 += 256)
                     for (int n0 = 0; n0 < (pass ? H : F); n0 += (pass ? 256 : 128))
@@ -431,9 +442,10 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         const int n_slots = std::max(1, c->n_local[layer]);
         CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
         CUDA_TRY(launch_gateup_tc(c->d_pf_x, np, c->arena[layer], n_slots, c->stride, c->d_tc_items, n_gu, H, F, c->d_act,
-                                  c->d_err, c->timeout_ns, st));
+                                  c->d_tc_sched, c->d_err, c->timeout_ns, c->sm_count, st));
         CUDA_TRY(launch_down_tc(c->d_act, np, c->arena[layer], n_slots, c->stride, c->d_tc_items + n_gu,
-                                (int)items.size() - n_gu, H, F, c->d_pf_yf, c->d_err, c->timeout_ns, st));
+                                (int)items.size() - n_gu, H, F, c->d_pf_yf, c->d_tc_sched + 2, c->d_err, c->timeout_ns,
+                                c->sm_count, st));
         CUDA_TRY(launch_combine_rows(c->d_pf_yf, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
         launches += 4;
     } else {
@@ -498,27 +510,30 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
 }
 
 // Host buffers on the fused path.  Pinned host memory is device-accessible under unified addressing,
-// so the kernels use it in place: the plan kernel reads the logits, the decode kernel writes the
-// output and leaves its error bits in a pinned word; only the hidden states are copied to the device
-// (every decode CTA reads them).  Unpinned (or, for the output, unaligned) buffers go through the
+// so the kernels use it in place: the plan kernel reads the logits and copies the hidden states to
+// the device (every decode CTA reads them) before it publishes the plan, the decode kernel writes
+// the output and leaves its error bits in a pinned word.  No copy is issued on the stream.  Unpinned (or, for the output, unaligned) buffers go through the
 // context's pinned staging.  One stream synchronisation ends the call.
 int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, const float* logits, float* out,
                        int32_t* topk_idx, float* topk_w, int flags, cudaStream_t st, DecodeArgs& da, size_t dsmem) {
     const int H = c->cfg.hidden, E = c->cfg.n_experts, K = c->cfg.top_k;
     const size_t hb = (size_t)T * H * 2, lb = (size_t)T * E * 4, ob = (size_t)T * H * 4;
-    const bool pin_x = is_pinned_host(hidden), pin_l = device_mapped(logits);
+    const bool pin_x = device_mapped(hidden) && ((uintptr_t)hidden & 15u) == 0, pin_l = device_mapped(logits);
     const bool pin_o = device_mapped(out) && ((uintptr_t)out & 15u) == 0;
     int s;
     const float* lg = logits;
+    const uint16_t* xs = hidden;  // pinned source the plan kernel copies to the device
     if (!pin_x || !pin_l) {
         if ((s = c->in_stage.reserve(align_up(hb, 256) + lb))) return s;
         if (!pin_l) {
             memcpy((char*)c->in_stage.host + align_up(hb, 256), logits, lb);
             lg = reinterpret_cast<const float*>((char*)c->in_stage.host + align_up(hb, 256));
         }
-        if (!pin_x) memcpy(c->in_stage.host, hidden, hb);
+        if (!pin_x) {
+            memcpy(c->in_stage.host, hidden, hb);
+            xs = static_cast<const uint16_t*>(c->in_stage.host);
+        }
     }
-    CUDA_TRY(cudaMemcpyAsync(c->d_hidden, pin_x ? (const void*)hidden : c->in_stage.host, hb, cudaMemcpyHostToDevice, st));
     float* o = out;
     if (!pin_o) {
         if ((s = c->out_stage.reserve(ob))) return s;
@@ -529,7 +544,7 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
     da.x = c->d_hidden;
     da.out = o;
     da.err_host = c->h_errsnap;
-    if ((s = launch_fused(c, layer, lg, da, dsmem, st, nullptr))) return s;
+    if ((s = launch_fused(c, layer, lg, da, dsmem, st, nullptr, xs))) return s;
     if (!pin_x || !pin_l) c->in_stage.mark(st);
     if (topk_idx) CUDA_TRY(cudaMemcpyAsync(topk_idx, c->d_idx, sizeof(int32_t) * T * K, cudaMemcpyDeviceToHost, st));
     if (topk_w) CUDA_TRY(cudaMemcpyAsync(topk_w, c->d_w, sizeof(float) * T * K, cudaMemcpyDeviceToHost, st));
@@ -677,7 +692,7 @@ int moe_destroy(moe_ctx* c) {
                   c->d_plan_flag, c->d_part};
     for (void* p : ps) cudaFree(p);
     if (c->blas) cublasDestroy(c->blas);
-    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_yf, (void*)c->d_pf_ptr,
+    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_yf, (void*)c->d_pf_ptr, (void*)c->d_tc_sched,
                     (void*)c->d_tc_items})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);

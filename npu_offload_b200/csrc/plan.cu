@@ -66,11 +66,13 @@ static_assert(sizeof(Seg) % 16 == 0, "segments are copied as int4");
 // scores and keys (route_core.cuh), the group's warps count the keys ordered before each key over a
 // slice of the experts each (shared-memory atomics sum the partial counts), and the first warp
 // selects the top-k.  Same bits as route_token (the rank is an exact count).
+__device__ __forceinline__ int plan_wpt(int T) { return T == 1 ? 16 : T == 2 ? 8 : T <= 4 ? 4 : T <= 8 ? 2 : 1; }
+
 template <int S>
 __device__ void plan_route(const PlanArgs& a, PlanSmem& m) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = a.T, E = a.E, K = a.K;
-    const int wpt = T == 1 ? 16 : T == 2 ? 8 : T <= 4 ? 4 : T <= 8 ? 2 : 1;  // warps per token
+    const int wpt = plan_wpt(T);  // warps per token
     const int t = warp / wpt, g = warp % wpt;
     unsigned long long mine[S];
     float val[S];
@@ -123,12 +125,25 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     // The decode grid may be scheduled at once: it acquires this call's flag (bounded) before it
     // reads the plan, and its griddepcontrol.wait still waits for this grid to complete.
     if (tid == 0) griddep_launch_dependents();
+    // host-buffer calls: the hidden states come straight from pinned host memory and the release of
+    // the plan flag publishes them with the plan.  The warps that do not score a token copy them
+    // while the scoring warps route (T <= 8); otherwise every thread copies after routing.
+    const int wpt = plan_wpt(T);
+    const uint4* xsrc = reinterpret_cast<const uint4*>(a.x_src);
+    uint4* xdst = reinterpret_cast<uint4*>(a.x_dst);
+    const int n16 = T * H / 8;
+    if (a.x_src && wpt > 1 && !(warp % wpt == 0 && warp / wpt < T)) {
+        const int below = min(T, (warp + wpt - 1) / wpt);  // scoring warps below this one
+        for (int i = tid - 32 * below; i < n16; i += kPlanThreads - 32 * T) xdst[i] = xsrc[i];
+    }
 
     // ---- routing ----
     if (E <= 32) plan_route<1>(a, m);
     else if (E <= 64) plan_route<2>(a, m);
     else if (E <= 128) plan_route<4>(a, m);
     else plan_route<8>(a, m);
+    if (a.x_src && wpt == 1)
+        for (int i = tid; i < n16; i += kPlanThreads) xdst[i] = xsrc[i];
     for (int e = tid; e < E; e += kPlanThreads) {
         m.counts[e] = 0;
         m.firstpos[e] = INT_MAX;

@@ -4,20 +4,26 @@
 //            (SwiGLU fused into the epilogue)
 //   down     y[p, h] = down row h . act_p in fp32 (MN-major weight operand: the stored down columns)
 //
-// One CTA = one tile: 256 pairs (two 128-row halves) x 128 intermediate indices of one job.
-//   producer warp   TMA (cp.async.bulk.tensor, 128-byte swizzle) of the gathered token rows
-//                   [256 x 64] and the job's gate and up rows [128 x 64] per K step into a 3-stage
-//                   shared-memory ring (mbarrier complete_tx)
+// Persistent kernel, one CTA per SM, taking tiles from a global counter (dynamic schedule; the last
+// CTA to exit re-arms it).  A tile is 256 pairs (two 128-row halves) of one job x 128 intermediate
+// indices (gate/up) or 256 outputs (down).
+//   producer warp   TMA (cp.async.bulk.tensor, 128-byte swizzle) per K step of 64: the A rows (one
+//                   [128 x 64] box per populated half) and the job's weights (gate/up: gate and up
+//                   rows [128 x 64] K-major; down: four [64 f x 64 h] boxes MN-major) into a 3-stage
+//                   shared-memory ring (mbarrier complete_tx) that runs on across tiles
 //   MMA warp        allocates 512 TMEM columns; one thread issues tcgen05.mma kind::f16 (bf16 x bf16
-//                   -> fp32, M 128, N 128, K 16) into four accumulators (gate / up x two halves) and
-//                   commits each stage back to the producer; the second half is skipped when the job
-//                   has <= 128 pairs in the tile
+//                   -> fp32, M 128, N 256, K 16; gate/up: the gate and up rows form one 256-row
+//                   operand) for each populated half, commits each stage back to the producer and the
+//                   finished accumulators to the epilogue
 //   8 epilogue warps  tcgen05.ld the fp32 accumulators (warp w: TMEM lanes 32 (w % 4) .., half w / 4),
-//                   apply SwiGLU, round to bf16, store the pair's 128 activations
+//                   gate/up: SwiGLU -> bf16 act rows; down: fp32 y rows; then hand the TMEM back
+//                   (the producer keeps prefetching the next tile meanwhile)
 // Weights are read in place from the unit tables through a 3-D tensor map (unit element, f, expert
-// slot); the gathered rows through a 2-D map.  Every wait is bounded; a CTA that gives up raises
-// kErrTimeout, lets its in-flight MMAs finish and frees its TMEM before returning.
+// slot); the A rows through a 2-D map.  Every wait is bounded; a CTA that gives up raises kErrTimeout,
+// lets its in-flight copies and MMAs finish and frees its TMEM before returning.
 #include <cuda.h>
+
+#include <algorithm>
 
 #include <cute/arch/mma_sm100_desc.hpp>
 
@@ -27,18 +33,20 @@
 
 namespace moe {
 
-constexpr int kTcBM = 256, kTcBN = 128, kTcBK = 64, kTcStages = 3;
+constexpr int kTcBK = 64, kTcStages = 3;
 constexpr int kTcEpiWarps = 8, kTcProdWarp = kTcEpiWarps, kTcMmaWarp = kTcEpiWarps + 1, kTcThreads = 10 * 32;
-constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2, kTcBBytes = kTcBN * kTcBK * 2;
-constexpr uint32_t kTcStageBytes = kTcABytes + 2 * kTcBBytes;  // A, gate, up
-constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes + 1024 + 256;
+constexpr uint32_t kTcHalfA = 128 * kTcBK * 2;                 // one 128-row half of A per K step
+constexpr uint32_t kTcBBytes = 32768;                          // gate + up [2 x 128 x 64] or down [64 x 256]
+constexpr uint32_t kTcStage = 2 * kTcHalfA + kTcBBytes;        // 64 KB
+constexpr size_t kTcSmem = (size_t)kTcStages * kTcStage + 1024 + 256;
 
 struct TcCtrl {
-    uint64_t full[kTcStages], empty[kTcStages], accum, done;
+    uint64_t full[kTcStages], empty[kTcStages], accum, tfree, done;
+    uint64_t tq_full[2], tq_empty[2];  // tile-index hand-off: producer -> MMA thread + epilogue warps
+    int tq[2];
     uint32_t tmem;
     int abort;
 };
-
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* abort, uint32_t* err, uint64_t deadline) {
     while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
         if (*(volatile int*)abort) return false;
@@ -67,19 +75,21 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return d.desc_;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], "
+        "[%2], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
+                                            uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4, "
+        "%5}], [%2], %6;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
         : "memory");
 }
 
@@ -111,142 +121,16 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kTcThreads, 1)
-    gateup_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                     const TcItem* __restrict__ items, int H, int F, uint16_t* __restrict__ act, uint32_t* err,
-                     uint64_t timeout_ns) {
-    extern __shared__ __align__(1024) unsigned char tsm[];
-    unsigned char* ring = reinterpret_cast<unsigned char*>(((uintptr_t)tsm + 1023) & ~(uintptr_t)1023);
-    TcCtrl& c = *reinterpret_cast<TcCtrl*>(ring + (size_t)kTcStages * kTcStageBytes);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const TcItem it = items[blockIdx.x];
-    const int nk = H / kTcBK;
-    const bool two = it.rows > 128;  // the second 128-row half has pairs of this job
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; s++) {
-            mbar_init(&c.full[s], 1);
-            mbar_init(&c.empty[s], 1);
-        }
-        mbar_init(&c.accum, 1);
-        mbar_init(&c.done, 1);
-        c.abort = 0;
-        fence_mbar_init();
-    }
-    if (warp == kTcMmaWarp) {  // whole warp: allocate the four 128-column accumulators
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&c.tmem)),
-                     "r"(512));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = c.tmem;
-    const uint64_t deadline = globaltimer_ns() + timeout_ns;
 
-    if (warp == kTcProdWarp) {
-        if (lane == 0) {
-            int k = 0;
-            for (; k < nk; k++) {
-                const int s = k % kTcStages;
-                if (k >= kTcStages && !tc_wait(&c.empty[s], ((k / kTcStages) & 1) ^ 1, &c.abort, err, deadline)) break;
-                unsigned char* st = ring + (size_t)s * kTcStageBytes;
-                mbar_arrive_expect_tx(&c.full[s], kTcStageBytes);
-                tma_load_2d(st, &map_x, k * kTcBK, it.row0, &c.full[s]);
-                tma_load_3d(st + kTcABytes, &map_w, k * kTcBK, it.f0, it.slot, &c.full[s]);
-                tma_load_3d(st + kTcABytes + kTcBBytes, &map_w, H + k * kTcBK, it.f0, it.slot, &c.full[s]);
-            }
-            // every issued copy lands before the CTA may exit
-            const uint64_t dd = globaltimer_ns() + timeout_ns;
-            for (int q = k > kTcStages ? k - kTcStages : 0; q < k; q++)
-                while (!mbar_try_wait(&c.full[q % kTcStages], (q / kTcStages) & 1))
-                    if (globaltimer_ns() > dd) break;
-        }
-    } else if (warp == kTcMmaWarp) {
-        if (lane == 0) {
-            const uint32_t idesc = (uint32_t)cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, 128,
-                                                                          cute::UMMA::Major::K, cute::UMMA::Major::K>();
-            for (int k = 0; k < nk; k++) {
-                const int s = k % kTcStages;
-                if (!tc_wait(&c.full[s], (k / kTcStages) & 1, &c.abort, err, deadline)) break;
-                tc_fence_after();
-                const uint32_t sa = smem_u32(ring + (size_t)s * kTcStageBytes);
-                const uint32_t sg = sa + kTcABytes, su = sg + kTcBBytes;
-#pragma unroll
-                for (int kk = 0; kk < kTcBK / 16; kk++) {
-                    const uint32_t acc = (k | kk) != 0;
-                    const uint64_t dg = sw128_desc(sg + kk * 32), du = sw128_desc(su + kk * 32);
-                    const uint64_t da0 = sw128_desc(sa + kk * 32);
-                    umma_bf16(tmem + 0, da0, dg, idesc, acc);    // gate, rows 0..127
-                    umma_bf16(tmem + 128, da0, du, idesc, acc);  // up,   rows 0..127
-                    if (two) {
-                        const uint64_t da1 = sw128_desc(sa + 128 * 128 + kk * 32);
-                        umma_bf16(tmem + 256, da1, dg, idesc, acc);  // gate, rows 128..255
-                        umma_bf16(tmem + 384, da1, du, idesc, acc);  // up,   rows 128..255
-                    }
-                }
-                umma_commit(&c.empty[s]);  // the stage is free once these MMAs have read it
-            }
-            umma_commit(&c.accum);  // accumulators complete (also the final fence for every MMA issued)
-        }
-    } else {
-        // epilogue: warp w -> TMEM lanes [32 (w % 4), +32), half w / 4
-        const int h = warp / 4, q = warp % 4;
-        const int r = h * 128 + q * 32 + lane;  // row of the tile this thread writes
-        if (tc_wait(&c.accum, 0, &c.abort, err, deadline) && (h == 0 || two)) {
-            tc_fence_after();
-            const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-            for (int c0 = 0; c0 < kTcBN; c0 += 32) {
-                uint32_t g[32], u[32];
-                tmem_ld32(tmem + lane_addr + h * 256 + c0, g);
-                tmem_ld32(tmem + lane_addr + h * 256 + 128 + c0, u);
-                tmem_wait_ld();
-                if (r < it.rows) {
-                    uint32_t o[16];
-#pragma unroll
-                    for (int e = 0; e < 16; e++)
-                        o[e] = (uint32_t)swiglu_bf16(__uint_as_float(g[2 * e]), __uint_as_float(u[2 * e])) |
-                               ((uint32_t)swiglu_bf16(__uint_as_float(g[2 * e + 1]), __uint_as_float(u[2 * e + 1])) << 16);
-                    uint4* dst = reinterpret_cast<uint4*>(act + (size_t)(it.row0 + r) * F + it.f0 + c0);
-                    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                    dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
-                    dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
-                }
-            }
-        }
-    }
-    // all MMAs are complete before TMEM is released: the accum commit covers them; after an abort the
-    // MMA thread commits once more and waits (bounded) for it
-    if (warp == kTcMmaWarp && lane == 0 && *(volatile int*)&c.abort) {
-        umma_commit(&c.done);
-        const uint64_t dd = globaltimer_ns() + timeout_ns;
-        while (!mbar_try_wait(&c.done, 0))
-            if (globaltimer_ns() > dd) break;
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == kTcMmaWarp) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
-    }
-}
-
-// ---- down projection: y[p, h] = sum_f act[p, f] * W2[h, f] (fp32) ----
-// One CTA = 256 pairs (two halves) x 256 outputs of one job.  A = activation rows (K-major, as above);
-// B = the job's down columns for f in the K step: a [64 f x 64 h] box per 64 outputs, i.e. MN-major
-// with 128-byte swizzle -- 64 h (128 bytes) contiguous per f row, 8-row swizzle atoms 1 KB apart
-// (SBO), the four 64-output chunks 8 KB apart (LBO); a K=16 step advances two whole atoms (2 KB).
-constexpr int kDnBN = 256;
-constexpr uint32_t kDnBBytes = kTcBK * kDnBN * 2;
-constexpr uint32_t kDnStageBytes = kTcABytes + kDnBBytes;
-constexpr size_t kDnSmem = (size_t)kTcStages * kDnStageBytes + 1024 + 256;
-
+// MN-major operand (down columns): 64 outputs (128 bytes) contiguous per f row as TMA writes a
+// [64 f x 64 h] box with 128-byte swizzle; 8-row swizzle atoms 1 KB apart along K (SBO), the
+// 64-output chunks 8 KB apart along N (LBO); a K=16 step advances two whole atoms (2 KB).
 __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr) {
     cute::UMMA::SmemDescriptor d;
     d.desc_ = 0;
     d.start_address_ = (uint16_t)(saddr >> 4);
-    d.leading_byte_offset_ = (kTcBK * 128) >> 4;  // next 64-output chunk
-    d.stride_byte_offset_ = 1024 >> 4;            // next 8 K rows
+    d.leading_byte_offset_ = (kTcBK * 128) >> 4;
+    d.stride_byte_offset_ = 1024 >> 4;
     d.version_ = 1;
     d.base_offset_ = 0;
     d.lbo_mode_ = 0;
@@ -254,28 +138,32 @@ __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr) {
     return d.desc_;
 }
 
+template <bool DOWN>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    down_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_d,
-                   const TcItem* __restrict__ items, int H, int F, float* __restrict__ y, uint32_t* err,
-                   uint64_t timeout_ns) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                   const TcItem* __restrict__ items, int n_items, int H, int F, void* __restrict__ out, uint32_t* sched,
+                   uint32_t* err, uint64_t timeout_ns) {
     extern __shared__ __align__(1024) unsigned char tsm[];
     unsigned char* ring = reinterpret_cast<unsigned char*>(((uintptr_t)tsm + 1023) & ~(uintptr_t)1023);
-    TcCtrl& c = *reinterpret_cast<TcCtrl*>(ring + (size_t)kTcStages * kDnStageBytes);
+    TcCtrl& c = *reinterpret_cast<TcCtrl*>(ring + (size_t)kTcStages * kTcStage);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const TcItem it = items[blockIdx.x];  // f0 holds the first output h of the tile
-    const int nk = F / kTcBK;
-    const bool two = it.rows > 128;
+    const int nk = (DOWN ? F : H) / kTcBK;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; s++) {
             mbar_init(&c.full[s], 1);
             mbar_init(&c.empty[s], 1);
         }
         mbar_init(&c.accum, 1);
+        mbar_init(&c.tfree, kTcEpiWarps);
         mbar_init(&c.done, 1);
+        for (int q = 0; q < 2; q++) {
+            mbar_init(&c.tq_full[q], 1);
+            mbar_init(&c.tq_empty[q], 1 + kTcEpiWarps);
+        }
         c.abort = 0;
         fence_mbar_init();
     }
-    if (warp == kTcMmaWarp) {
+    if (warp == kTcMmaWarp) {  // whole warp: 512 columns = the accumulators of both halves
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&c.tmem)),
                      "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -284,67 +172,153 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = c.tmem;
-    const uint64_t deadline = globaltimer_ns() + timeout_ns;
 
     if (warp == kTcProdWarp) {
         if (lane == 0) {
-            int k = 0;
-            for (; k < nk; k++) {
-                const int s = k % kTcStages;
-                if (k >= kTcStages && !tc_wait(&c.empty[s], ((k / kTcStages) & 1) ^ 1, &c.abort, err, deadline)) break;
-                unsigned char* st = ring + (size_t)s * kDnStageBytes;
-                mbar_arrive_expect_tx(&c.full[s], kDnStageBytes);
-                tma_load_2d(st, &map_a, k * kTcBK, it.row0, &c.full[s]);
+            uint32_t g = 0;  // stages issued over all tiles
+            bool ok = true;
+            const uint64_t pol_w = l2_evict_first(), pol_a = l2_evict_last();  // weights read once; rows reused
+            for (int n = 0; ok; n++) {
+                const uint64_t deadline = globaltimer_ns() + timeout_ns;
+                const int slot = n & 1;
+                if (n >= 2 && !tc_wait(&c.tq_empty[slot], ((n >> 1) & 1) ^ 1, &c.abort, err, deadline)) break;
+                const int i = (int)atomicAdd(&sched[0], 1u);  // dynamic tile schedule
+                c.tq[slot] = i;
+                mbar_arrive(&c.tq_full[slot]);  // release: the index is visible to the waiters
+                if (i >= n_items) break;
+                const TcItem it = items[i];
+                const bool two = it.rows > 128;
+                for (int k = 0; k < nk; k++, g++) {
+                    const int s = g % kTcStages;
+                    if (g >= kTcStages &&
+                        !tc_wait(&c.empty[s], ((g / kTcStages) & 1) ^ 1, &c.abort, err, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = ring + (size_t)s * kTcStage;
+                    unsigned char* sb = st + 2 * kTcHalfA;
+                    mbar_arrive_expect_tx(&c.full[s], (two ? 2 : 1) * kTcHalfA + kTcBBytes);
+                    tma_load_2d(st, &map_a, k * kTcBK, it.row0, &c.full[s], pol_a);
+                    if (two) tma_load_2d(st + kTcHalfA, &map_a, k * kTcBK, it.row0 + 128, &c.full[s], pol_a);
+                    if (DOWN) {
 #pragma unroll
-                for (int j = 0; j < kDnBN / 64; j++)
-                    tma_load_3d(st + kTcABytes + j * (kTcBK * 128), &map_d, 2 * H + it.f0 + j * 64, k * kTcBK, it.slot,
-                                &c.full[s]);
+                        for (int j = 0; j < 4; j++)
+                            tma_load_3d(sb + j * (kTcBK * 128), &map_w, 2 * H + it.f0 + j * 64, k * kTcBK, it.slot,
+                                        &c.full[s], pol_w);
+                    } else {  // gate rows then up rows: one 256-row K-major operand
+                        tma_load_3d(sb, &map_w, k * kTcBK, it.f0, it.slot, &c.full[s], pol_w);
+                        tma_load_3d(sb + kTcBBytes / 2, &map_w, H + k * kTcBK, it.f0, it.slot, &c.full[s], pol_w);
+                    }
+                }
             }
+            // every issued copy lands before the CTA may exit
             const uint64_t dd = globaltimer_ns() + timeout_ns;
-            for (int q = k > kTcStages ? k - kTcStages : 0; q < k; q++)
+            for (uint32_t q = g > (uint32_t)kTcStages ? g - kTcStages : 0; q < g; q++)
                 while (!mbar_try_wait(&c.full[q % kTcStages], (q / kTcStages) & 1))
                     if (globaltimer_ns() > dd) break;
         }
     } else if (warp == kTcMmaWarp) {
         if (lane == 0) {
-            const uint32_t idesc = (uint32_t)cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, kDnBN,
-                                                                          cute::UMMA::Major::K, cute::UMMA::Major::MN>();
-            for (int k = 0; k < nk; k++) {
-                const int s = k % kTcStages;
-                if (!tc_wait(&c.full[s], (k / kTcStages) & 1, &c.abort, err, deadline)) break;
+            const uint32_t idesc =
+                DOWN ? (uint32_t)cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, 256,
+                                                             cute::UMMA::Major::K, cute::UMMA::Major::MN>()
+                     : (uint32_t)cute::UMMA::make_instr_desc<cute::bfloat16_t, cute::bfloat16_t, float, 128, 256,
+                                                             cute::UMMA::Major::K, cute::UMMA::Major::K>();
+            uint32_t g = 0;
+            bool ok = true;
+            for (int n = 0; ok; n++) {
+                const uint64_t deadline = globaltimer_ns() + timeout_ns;
+                const int slot = n & 1;
+                if (!tc_wait(&c.tq_full[slot], (n >> 1) & 1, &c.abort, err, deadline)) break;
+                const int i = *(volatile int*)&c.tq[slot];
+                mbar_arrive(&c.tq_empty[slot]);
+                if (i >= n_items) break;
+                const bool two = items[i].rows > 128;
+                if (n > 0 && !tc_wait(&c.tfree, (n - 1) & 1, &c.abort, err, deadline)) break;  // TMEM drained
                 tc_fence_after();
-                const uint32_t sa = smem_u32(ring + (size_t)s * kDnStageBytes), sb = sa + kTcABytes;
+                for (int k = 0; k < nk; k++, g++) {
+                    const int s = g % kTcStages;
+                    if (!tc_wait(&c.full[s], (g / kTcStages) & 1, &c.abort, err, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(ring + (size_t)s * kTcStage), sb = sa + 2 * kTcHalfA;
 #pragma unroll
-                for (int kk = 0; kk < kTcBK / 16; kk++) {
-                    const uint32_t acc = (k | kk) != 0;
-                    const uint64_t db = sw128_mn_desc(sb + kk * 2048);
-                    umma_bf16(tmem + 0, sw128_desc(sa + kk * 32), db, idesc, acc);
-                    if (two) umma_bf16(tmem + 256, sw128_desc(sa + 128 * 128 + kk * 32), db, idesc, acc);
+                    for (int kk = 0; kk < kTcBK / 16; kk++) {
+                        const uint32_t acc = (k | kk) != 0;
+                        const uint64_t da0 = sw128_desc(sa + kk * 32), da1 = sw128_desc(sa + kTcHalfA + kk * 32);
+                        // gate/up: columns [0, 128) gate, [128, 256) up of each half's accumulator
+                        const uint64_t db = DOWN ? sw128_mn_desc(sb + kk * 2048) : sw128_desc(sb + kk * 32);
+                        umma_bf16(tmem + 0, da0, db, idesc, acc);
+                        if (two) umma_bf16(tmem + 256, da1, db, idesc, acc);
+                    }
+                    umma_commit(&c.empty[s]);  // the stage is free once these MMAs have read it
                 }
-                umma_commit(&c.empty[s]);
+                if (ok) umma_commit(&c.accum);  // this tile's accumulators are complete
             }
-            umma_commit(&c.accum);
         }
     } else {
+        // epilogue: warp w -> TMEM lanes [32 (w % 4), +32), half w / 4
         const int h = warp / 4, q = warp % 4;
-        const int r = h * 128 + q * 32 + lane;
-        if (tc_wait(&c.accum, 0, &c.abort, err, deadline) && (h == 0 || two)) {
+        const int r = h * 128 + q * 32 + lane;  // row of the tile this thread writes
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + h * 256;
+        for (int n = 0;; n++) {
+            const uint64_t deadline = globaltimer_ns() + timeout_ns;
+            const int slot = n & 1;
+            if (!tc_wait(&c.tq_full[slot], (n >> 1) & 1, &c.abort, err, deadline)) break;
+            const int i = *(volatile int*)&c.tq[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&c.tq_empty[slot]);
+            if (i >= n_items) break;
+            const TcItem it = items[i];
+            if (!tc_wait(&c.accum, n & 1, &c.abort, err, deadline)) break;
             tc_fence_after();
-            const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-            for (int c0 = 0; c0 < kDnBN; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + h * 256 + c0, v);
-                tmem_wait_ld();
-                if (r < it.rows) {
-                    float4* dst = reinterpret_cast<float4*>(y + (size_t)(it.row0 + r) * H + it.f0 + c0);
+            if (h == 0 || it.rows > 128) {
+                if (DOWN) {
+                    float* y = static_cast<float*>(out);
+                    for (int c0 = 0; c0 < 256; c0 += 32) {
+                        uint32_t v[32];
+                        tmem_ld32(taddr + c0, v);
+                        tmem_wait_ld();
+                        if (r < it.rows) {
+                            float4* dst = reinterpret_cast<float4*>(y + (size_t)(it.row0 + r) * H + it.f0 + c0);
 #pragma unroll
-                    for (int e = 0; e < 8; e++)
-                        dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                             __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                            for (int e = 0; e < 8; e++)
+                                dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                                     __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                        }
+                    }
+                } else {
+                    uint16_t* act = static_cast<uint16_t*>(out);
+                    for (int c0 = 0; c0 < 128; c0 += 32) {
+                        uint32_t g[32], u[32];
+                        tmem_ld32(taddr + c0, g);
+                        tmem_ld32(taddr + 128 + c0, u);
+                        tmem_wait_ld();
+                        if (r < it.rows) {
+                            uint32_t o[16];
+#pragma unroll
+                            for (int e = 0; e < 16; e++)
+                                o[e] = (uint32_t)swiglu_bf16(__uint_as_float(g[2 * e]), __uint_as_float(u[2 * e])) |
+                                       ((uint32_t)swiglu_bf16(__uint_as_float(g[2 * e + 1]), __uint_as_float(u[2 * e + 1]))
+                                        << 16);
+                            uint4* dst = reinterpret_cast<uint4*>(act + (size_t)(it.row0 + r) * F + it.f0 + c0);
+                            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                            dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+                            dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+                        }
+                    }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&c.tfree);  // this warp's TMEM reads are complete
         }
     }
+    // all MMAs are complete before TMEM is released: the last accum commit covers them; after an abort
+    // the MMA thread commits once more and waits (bounded) for it
     if (warp == kTcMmaWarp && lane == 0 && *(volatile int*)&c.abort) {
         umma_commit(&c.done);
         const uint64_t dd = globaltimer_ns() + timeout_ns;
@@ -356,6 +330,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == kTcMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+    // the last CTA out re-arms the schedule for the next launch (every tile index has been taken)
+    if (threadIdx.x == 0 && atomicAdd(&sched[1], 1u) == gridDim.x - 1) {
+        atomicExch(&sched[0], 0u);
+        atomicExch(&sched[1], 0u);
     }
 }
 
@@ -384,65 +363,62 @@ static EncodeTiledFn encode_fn() {
 bool tc_available() { return encode_fn() != nullptr; }
 
 cudaError_t tc_set_smem_limit() {
-    cudaError_t e = cudaFuncSetAttribute(gateup_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDnSmem);
+        e = cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     return e;
 }
 
+// [rows][cols] bf16, 128-row x 64-column boxes, 128-byte swizzle
+static bool encode_rows(EncodeTiledFn enc, CUtensorMap* m, const void* base, int cols, int rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {kTcBK, 128}, es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// the layer's unit tables as [slot][f][3H] bf16 with the given box (inner, f)
+static bool encode_units(EncodeTiledFn enc, CUtensorMap* m, const void* arena, int H, int F, int n_slots,
+                         size_t slot_bytes, cuuint32_t box_x, cuuint32_t box_f) {
+    const cuuint64_t dims[3] = {(cuuint64_t)3 * H, (cuuint64_t)F, (cuuint64_t)n_slots};
+    const cuuint64_t strides[2] = {(cuuint64_t)6 * H, (cuuint64_t)slot_bytes};
+    const cuuint32_t box[3] = {box_x, box_f, 1}, es[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(arena), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, int n_slots, size_t slot_bytes,
-                           const TcItem* items, int n_items, int H, int F, float* y, uint32_t* err, uint64_t timeout_ns,
-                           cudaStream_t st) {
+                           const TcItem* items, int n_items, int H, int F, float* y, uint32_t* sched, uint32_t* err,
+                           uint64_t timeout_ns, int grid_max, cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
-    if (H % kDnBN || F % kTcBK || slot_bytes % 16 || ((uintptr_t)act | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
+    if (H % 256 || F % kTcBK || slot_bytes % 16 || ((uintptr_t)act | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
     CUtensorMap ma, md;
-    {  // activation rows: [arows][F] bf16
-        const cuuint64_t dims[2] = {(cuuint64_t)F, (cuuint64_t)arows};
-        const cuuint64_t strides[1] = {(cuuint64_t)F * 2};
-        const cuuint32_t box[2] = {kTcBK, kTcBM}, es[2] = {1, 1};
-        if (enc(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)act, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
-    {  // unit tables, down columns at element 2H of each unit: boxes of 64 outputs x 64 f
-        const cuuint64_t dims[3] = {(cuuint64_t)3 * H, (cuuint64_t)F, (cuuint64_t)n_slots};
-        const cuuint64_t strides[2] = {(cuuint64_t)6 * H, (cuuint64_t)slot_bytes};
-        const cuuint32_t box[3] = {64, kTcBK, 1}, es[3] = {1, 1, 1};
-        if (enc(&md, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void*)arena, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
+    // activation rows [arows][F]; down columns at element 2H of each unit, boxes of 64 outputs x 64 f
+    if (!encode_rows(enc, &ma, act, F, arows) || !encode_units(enc, &md, arena, H, F, n_slots, slot_bytes, 64, kTcBK))
+        return cudaErrorInvalidValue;
     if (n_items <= 0) return cudaSuccess;
-    down_tc_kernel<<<n_items, kTcThreads, kDnSmem, st>>>(ma, md, items, H, F, y, err, timeout_ns);
+    tc_gemm_kernel<true><<<std::min(n_items, grid_max), kTcThreads, kTcSmem, st>>>(ma, md, items, n_items, H, F, y, sched,
+                                                                                  err, timeout_ns);
     return cudaGetLastError();
 }
 
 cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, int n_slots, size_t slot_bytes,
-                             const TcItem* items, int n_items, int H, int F, uint16_t* act, uint32_t* err,
-                             uint64_t timeout_ns, cudaStream_t st) {
+                             const TcItem* items, int n_items, int H, int F, uint16_t* act, uint32_t* sched,
+                             uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
-    if (H % kTcBK || F % kTcBN || slot_bytes % 16 || ((uintptr_t)xg | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
+    if (H % kTcBK || F % 128 || slot_bytes % 16 || ((uintptr_t)xg | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
     CUtensorMap mx, mw;
-    {  // gathered token rows: [xrows][H] bf16
-        const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)xrows};
-        const cuuint64_t strides[1] = {(cuuint64_t)H * 2};
-        const cuuint32_t box[2] = {kTcBK, kTcBM}, es[2] = {1, 1};
-        if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)xg, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
-    {  // unit tables: [slot][f][3H] bf16 (gate row f at element 0 of unit f, up row at element H)
-        const cuuint64_t dims[3] = {(cuuint64_t)3 * H, (cuuint64_t)F, (cuuint64_t)n_slots};
-        const cuuint64_t strides[2] = {(cuuint64_t)6 * H, (cuuint64_t)slot_bytes};
-        const cuuint32_t box[3] = {kTcBK, kTcBN, 1}, es[3] = {1, 1, 1};
-        if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void*)arena, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
+    // gathered token rows [xrows][H]; gate row f at element 0 of unit f, up row at element H
+    if (!encode_rows(enc, &mx, xg, H, xrows) || !encode_units(enc, &mw, arena, H, F, n_slots, slot_bytes, kTcBK, 128))
+        return cudaErrorInvalidValue;
     if (n_items <= 0) return cudaSuccess;
-    gateup_tc_kernel<<<n_items, kTcThreads, kTcSmem, st>>>(mx, mw, items, H, F, act, err, timeout_ns);
+    tc_gemm_kernel<false><<<std::min(n_items, grid_max), kTcThreads, kTcSmem, st>>>(mx, mw, items, n_items, H, F, act,
+                                                                                   sched, err, timeout_ns);
     return cudaGetLastError();
 }
 

@@ -107,6 +107,13 @@ __device__ __forceinline__ uint64_t l2_evict_first() {
     return p;
 }
 
+// L2 policy for data re-read by other CTAs soon (gathered token rows of a prefill tile): evict last.
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
