@@ -192,9 +192,9 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 128) run the expert
  *                               FFN as grouped tensor-core GEMMs when every routed local expert is
  *                               bf16; 0 keeps every batch on the CUDA-core paths.
- *   MOE_OPT_PREFILL_TC          1 (default): the prefill gate/up GEMM runs on the library's tcgen05
- *                               kernel with the SwiGLU fused (fp32 accumulators); 0: a grouped library
- *                               GEMM with bf16 outputs followed by a SwiGLU kernel.
+ *   MOE_OPT_PREFILL_TC          1 (default): the prefill gate/up and down GEMMs run on the library's
+ *                               persistent tcgen05 kernels (SwiGLU fused, g / u / y kept in fp32);
+ *                               0: cuBLAS grouped GEMMs with bf16 outputs and a SwiGLU kernel.
  *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
  *                               globaltimer / cycle slots (0 start, 1 plan share loaded, 2 all stages
  *                               issued, 3 all segments done, 4 grid-wide arrival seen, 5 reduction
