@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="configs[3] prefill measurement at N=1 (0 to skip)")
+    ap.add_argument("--no-block", action="store_true", help="skip the moe_block_forward measurement")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="N>1 combine: in-kernel NVLink peer exchange (p2p) or an NCCL all-reduce per layer")
     return ap.parse_args()
@@ -357,6 +358,61 @@ def prefill_run(stack, T, reps=5, warmup=2):
             "gpu_launches_per_layer": (stack.plane.launch_count - l0) / reps}
 
 
+def block_run(stack, steps, warmup, T=1):
+    """The whole MoE block around the path: router GEMV producing the logits,
+    routed experts, the shared expert and the residual combine into the next layer's input
+    (moe_block_forward), per layer of the stack, device-resident inputs, CUDA events."""
+    import torch
+    from npu_offload_b200 import synth
+    L, R, dev = stack.L, stack.R, stack.device
+    gen = torch.Generator(device=dev)
+    for l in range(L):
+        gen.manual_seed(7919 + l)
+        w = [(torch.randn(*shape, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+             for shape in ((F, H), (F, H), (H, F), (E, H))]
+        stack.plane.load_shared(l, *w)
+    h2 = torch.from_numpy(np.stack([np.stack([synth.hidden(500 + 31 * r + l, T, H) for l in range(L)])
+                                    for r in range(R)]).view(np.int16)).view(torch.bfloat16).to(dev)
+    x2 = torch.from_numpy(np.stack([np.stack([synth.hidden(900 + 31 * r + l, T, H) for l in range(L)])
+                                    for r in range(R)]).view(np.int16)).view(torch.bfloat16).to(dev)
+    routed = np.zeros((R, L))
+    for r in range(R):
+        for l in range(L):
+            _, _, lg = stack.plane.block_forward(l, h2[r, l], x2[r, l], return_parts=True)
+            top = np.argsort(-lg.cpu().numpy(), axis=1, kind="stable")[:, :K]
+            routed[r, l] = len(set(top.ravel().tolist()))
+    xn = torch.empty(L, T, H, dtype=torch.bfloat16, device=dev)
+    from npu_offload_b200._lib import check, lib
+    fn, h = lib().moe_block_forward, stack.plane.handle
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def one(s):
+        r = s % R
+        for l in range(L):
+            check(fn(h, l, T, ctypes.c_void_p(h2[r, l].data_ptr()), ctypes.c_void_p(x2[r, l].data_ptr()), None,
+                     ctypes.c_void_p(xn[l].data_ptr()), None, None, 0, sp))
+
+    for s in range(warmup):
+        one(s)
+    torch.cuda.synchronize(dev)
+    l0 = stack.plane.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for s in range(steps):
+        one(warmup + s)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    reps = [(warmup + s) % R for s in range(steps)]
+    nbytes = sum(routed[r].sum() for r in reps) * EXPERT_BYTES + steps * L * (EXPERT_BYTES + E * H * 2)
+    us_layer = ms * 1e3 / (steps * L)
+    return {"workload": f"moe_block_forward: router GEMV + routed experts + shared expert + residual combine, "
+                        f"batch {T}, {L} layers",
+            "us_per_layer": us_layer, "tokens_per_s": T * L * steps / (ms / 1e3),
+            "bytes_per_layer": nbytes / (steps * L), "gbs": nbytes / (ms / 1e3) / 1e9,
+            "gpu_launches_per_layer": (stack.plane.launch_count - l0) / (steps * L)}
+
+
 # ---------------------------------------------------------------- CPU baseline (reference / port)
 def cpu_threads():
     try:
@@ -512,6 +568,9 @@ def our_arm(args):
     prefill = None
     if ws == 1 and args.prefill_tokens > 0:
         prefill = prefill_run(stack, args.prefill_tokens)
+    block = None
+    if ws == 1 and not args.no_block:
+        block = block_run(stack, max(1, args.steps // 4), min(args.warmup, 3))
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -546,7 +605,8 @@ def our_arm(args):
                                  % (ubytes_main.mean() * L / 1e9),
                            "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
-                "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep, "prefill": prefill}
+                "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep, "prefill": prefill,
+                "block": block}
         print(json.dumps(line), flush=True)
     if ws > 1:
         barrier(ws)  # no rank frees its exchange buffer while a peer may still use it

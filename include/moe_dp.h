@@ -159,6 +159,41 @@ MOE_API int moe_ck_moe_q8w(moe_ctx* ctx, int E, const int8_t* const* q, const fl
 MOE_API int moe_place_expert_q8(moe_ctx* ctx, const uint16_t* g, const uint16_t* u, const uint16_t* d, int8_t* q, float* sc,
                         int32_t* rs, int flags, void* stream);
 
+/* ---- The steps either side of the routed experts in one Solar MoE block
+ * (track2_opt/solar_engine/src/layer.rs:1-6: combine -> attention -> shared expert + router). ----
+ *
+ * moe_load_shared: layer `layer`'s shared expert (gate [F*H], up [F*H] rows, down [H*F] row-major,
+ * the routed experts' layout) and router weights Wr [E*H] row-major, bf16.  Either part may be NULL
+ * (then left as loaded before).  Copied; host pointers with MOE_F_HOST.  Replaces the host-side
+ * placement of dense/shared.rs's WG / WD / WR tables (shared.rs:5-31).
+ *
+ * moe_shared_router: the router-logit producer + shared expert, dense/shared.rs:1-3, :192-210
+ * (`shared_router`), T tokens, device pointers:
+ *   logits [T,E] f32  = h2 . Wr^T (fp32 accumulate)                        (skipped if NULL)
+ *   y_out  [T,H] bf16 = bf16(x2 + down . (silu(gate . h2) * (up . h2)))    (skipped if NULL)
+ * The shared expert uses cpu_moe's rounding points (g, u fp32, act bf16); the reference's device
+ * kernel also rounds g and u to bf16 (its host checker expert_ref, solar_engine/src/host_util.rs:35-46).
+ *
+ * moe_combine_residual: the next layer's input, dense/combine.rs:1-77 (`combine`) and layer.rs:4:
+ *   x_next [T,H] bf16 = bf16((y + extra) + moe_out), fp32 math, one rounding; extra may be NULL.
+ *   moe_out is the combined routed-expert output (what moe_forward returns: sum_k w_k expert_k).
+ *
+ * moe_block_forward: all three around moe_forward in one call (no host round trip):
+ *   logits = h2 . Wr^T; moe_out = routed experts on (h2, logits); y = bf16(x2 + shared(h2));
+ *   x_next = bf16((y + extra) + moe_out).
+ * y_out / logits_out may be NULL (kept in the context).  Device pointers, or host pointers with
+ * MOE_F_HOST (then synchronous).  Expert-parallel contexts need moe_ep_import first (every rank
+ * computes the shared expert itself and returns the same x_next). */
+MOE_API int moe_load_shared(moe_ctx* ctx, int layer, const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                            const uint16_t* router, int flags);
+MOE_API int moe_shared_router(moe_ctx* ctx, int layer, int T, const uint16_t* h2, const uint16_t* x2,
+                              uint16_t* y_out, float* logits, int flags, void* stream);
+MOE_API int moe_combine_residual(moe_ctx* ctx, int T, const uint16_t* y, const float* extra, const float* moe_out,
+                                 uint16_t* x_next, int flags, void* stream);
+MOE_API int moe_block_forward(moe_ctx* ctx, int layer, int T, const uint16_t* h2, const uint16_t* x2,
+                              const float* extra, uint16_t* x_next, uint16_t* y_out, float* logits_out, int flags,
+                              void* stream);
+
 /* Expert-parallel combine over NVLink peer memory (no counterpart in the reference, whose chips
  * return partial sums to one host).  Collective set-up, once per context, every rank of the box:
  *   moe_ep_export(ctx, buf, cap)      writes this rank's MOE_EP_RECORD_BYTES handle record into buf;

@@ -57,6 +57,10 @@ _SIGS = {
     "moe_status": (_i, [_vp, _vp]),
     "moe_launch_count": (ctypes.c_int64, [_vp]),
     "moe_ck_moe3_noalloc": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "moe_load_shared": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i]),
+    "moe_shared_router": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
+    "moe_combine_residual": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i, _vp]),
+    "moe_block_forward": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
     "moe_ep_export": (_i, [_vp, _vp, _i]),
     "moe_ep_import": (_i, [_vp, _vp, _i]),
     "moe_set_option": (_i, [_vp, _i, ctypes.c_int64]),

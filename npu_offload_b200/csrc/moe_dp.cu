@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "decode.h"
 #include "prefill_tc.h"
+#include "block.h"
 #include "experts.h"
 #include "route.h"
 
@@ -146,6 +147,16 @@ struct moe_ctx {
     TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels
     uint32_t* d_tc_sched = nullptr;     // [4] tile-schedule counters (gate/up, down), left zero by each launch
     int tc_items_cap = 0;
+    // MoE-block calls (moe_load_shared, moe_shared_router, moe_block_forward)
+    moe_ctx* shared = nullptr;          // one-expert context holding each layer's shared expert
+    std::vector<uint16_t*> d_router;    // [L] router weights [E, H] bf16 (null until loaded)
+    float* d_blk_zero = nullptr;        // [max_tokens] zero logits: the shared context routes with weight 1
+    float* d_blk_logits = nullptr;      // [max_tokens, E]
+    float* d_blk_shared = nullptr;      // [max_tokens, H] shared-expert output
+    float* d_blk_moe = nullptr;         // [max_tokens, H] routed-expert output
+    uint16_t* d_blk_y = nullptr;        // [max_tokens, H] y = bf16(x2 + shared)
+    uint16_t* d_blk_io = nullptr;       // [3][max_tokens, H] host-buffer calls: h2, x2, x_next
+    float* d_blk_extra = nullptr;       // [max_tokens, H] host-buffer calls: extra
     DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
     uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
     uint32_t epoch = 0;
@@ -684,6 +695,11 @@ int moe_destroy(moe_ctx* c) {
     if (!c) return MOE_OK;
     DeviceGuard dg(c->dev);
     cudaDeviceSynchronize();
+    if (c->shared) moe_destroy(c->shared);
+    for (uint16_t* r : c->d_router) cudaFree(r);
+    for (void* q : {(void*)c->d_blk_zero, (void*)c->d_blk_logits, (void*)c->d_blk_shared, (void*)c->d_blk_moe,
+                    (void*)c->d_blk_y, (void*)c->d_blk_io, (void*)c->d_blk_extra})
+        if (q) cudaFree(q);
     for (void* p : c->arena) cudaFree(p);
     if (c->d_timeline) cudaFree(c->d_timeline);
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
@@ -1270,16 +1286,186 @@ int moe_ep_import(moe_ctx* c, const void* blobs, int world) {
     return MOE_OK;
 }
 
+// ---------------- MoE-block calls: the steps either side of the routed experts ----------------
+
+static int ensure_shared(moe_ctx* c) {
+    if (c->shared) return MOE_OK;
+    moe_config k = c->cfg;
+    k.n_experts = 1;  // softmax over one zero logit: weight exactly 1 for every token
+    k.top_k = 1;
+    k.scoring = MOE_SCORING_SOFTMAX;
+    k.ep_rank = 0;
+    k.ep_world = 1;   // replicated on every expert-parallel rank: identical y everywhere
+    k.shard_map = nullptr;
+    int st = moe_create(&k, &c->shared);
+    if (st) return st;
+    moe_ctx* s = c->shared;
+    s->fused = c->fused;
+    s->timeout_ns = c->timeout_ns;
+    s->prefill = c->prefill;
+    s->prefill_min_t = c->prefill_min_t;
+    s->prefill_tc = c->prefill_tc;
+    s->ns_cap = c->ns_cap;
+    s->stage_target = c->stage_target;
+    const size_t NT = c->cfg.max_tokens, H = c->cfg.hidden, E = c->cfg.n_experts;
+    if (!st) st = dalloc(&c->d_blk_zero, NT);
+    if (!st) st = dalloc(&c->d_blk_logits, NT * E);
+    if (!st) st = dalloc(&c->d_blk_shared, NT * H);
+    if (!st) st = dalloc(&c->d_blk_moe, NT * H);
+    if (!st) st = dalloc(&c->d_blk_y, NT * H);
+    if (!st) st = dalloc(&c->d_blk_io, 3 * NT * H);
+    if (!st) st = dalloc(&c->d_blk_extra, NT * H);
+    if (!st && cudaMemset(c->d_blk_zero, 0, NT * sizeof(float)) != cudaSuccess) st = fail(MOE_ECUDA, "memset");
+    if (!st) c->d_router.assign(c->cfg.n_layers, nullptr);
+    return st;
+}
+
+int moe_load_shared(moe_ctx* c, int layer, const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                    const uint16_t* router, int flags) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(MOE_EINVAL, "layer %d out of range [0,%d)", layer, c->cfg.n_layers);
+    if (!gate != !up || !gate != !down) return fail(MOE_EINVAL, "the shared expert needs gate, up and down together");
+    DeviceGuard dg(c->dev);
+    int st = ensure_shared(c);
+    if (st) return st;
+    if (gate && (st = moe_load_expert_bf16(c->shared, layer, 0, gate, up, down, flags))) return st;
+    if (router) {
+        const size_t n = (size_t)c->cfg.n_experts * c->cfg.hidden;
+        if (!c->d_router[layer] && (st = dalloc(&c->d_router[layer], n))) return st;
+        CUDA_TRY(cudaMemcpy(c->d_router[layer], router, n * 2,
+                            (flags & MOE_F_HOST) ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice));
+    }
+    return MOE_OK;
+}
+
+static int block_checks(moe_ctx* c, int layer, int T) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (layer < 0 || layer >= c->cfg.n_layers) return fail(MOE_EINVAL, "layer %d out of range [0,%d)", layer, c->cfg.n_layers);
+    if (T < 0 || T > c->cfg.max_tokens) return fail(MOE_EINVAL, "T=%d not in [0,%d]", T, c->cfg.max_tokens);
+    return MOE_OK;
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Both contexts' latched device status (the shared context's calls run without MOE_F_SYNC).
+static int block_sync(moe_ctx* c, cudaStream_t st) {
+    const int a = finish_sync(c, st);
+    const int b = c->shared ? finish_sync(c->shared, st) : MOE_OK;
+    return a ? a : b;
+}
+
+int moe_shared_router(moe_ctx* c, int layer, int T, const uint16_t* h2, const uint16_t* x2, uint16_t* y_out,
+                      float* logits, int flags, void* stream) {
+    int st = block_checks(c, layer, T);
+    if (st) return st;
+    if (flags & MOE_F_HOST) return fail(MOE_EINVAL, "moe_shared_router takes device pointers");
+    if (T == 0) return MOE_OK;
+    if (!h2 || (y_out && !x2)) return fail(MOE_EINVAL, "null h2 / x2");
+    if (!aligned16(h2) || !aligned16(x2) || !aligned16(y_out)) return fail(MOE_EINVAL, "buffers must be 16-byte aligned");
+    DeviceGuard dg(c->dev);
+    cudaStream_t s = (cudaStream_t)stream;
+    const int H = c->cfg.hidden, E = c->cfg.n_experts;
+    if (logits) {
+        if (c->d_router.empty() || !c->d_router[layer]) return fail(MOE_ESTATE, "no router weights loaded for layer %d", layer);
+        CUDA_TRY(launch_router_gemv(c->d_router[layer], h2, T, E, H, logits, s));
+        c->launches++;
+    }
+    if (y_out) {
+        if (!c->shared || moe_expert_kind(c->shared, layer, 0) != kKindBF16)
+            return fail(MOE_ESTATE, "no shared expert loaded for layer %d", layer);
+        if ((st = moe_forward(c->shared, layer, T, h2, c->d_blk_zero, c->d_blk_shared, nullptr, nullptr, 0, s))) return st;
+        CUDA_TRY(launch_residual(nullptr, x2, c->d_blk_shared, nullptr, nullptr, (long)T * H, y_out, nullptr, c->sm_count, s));
+        c->launches++;
+    }
+    return (flags & MOE_F_SYNC) ? block_sync(c, s) : MOE_OK;
+}
+
+int moe_combine_residual(moe_ctx* c, int T, const uint16_t* y, const float* extra, const float* moe_out,
+                         uint16_t* x_next, int flags, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (T < 0 || T > c->cfg.max_tokens) return fail(MOE_EINVAL, "T=%d not in [0,%d]", T, c->cfg.max_tokens);
+    if (flags & MOE_F_HOST) return fail(MOE_EINVAL, "moe_combine_residual takes device pointers");
+    if (T == 0) return MOE_OK;
+    if (!y || !moe_out || !x_next) return fail(MOE_EINVAL, "null y / moe_out / x_next");
+    if (!aligned16(y) || !aligned16(extra) || !aligned16(moe_out) || !aligned16(x_next))
+        return fail(MOE_EINVAL, "buffers must be 16-byte aligned");
+    DeviceGuard dg(c->dev);
+    cudaStream_t s = (cudaStream_t)stream;
+    CUDA_TRY(launch_residual(y, nullptr, nullptr, extra, moe_out, (long)T * c->cfg.hidden, nullptr, x_next, c->sm_count, s));
+    c->launches++;
+    return (flags & MOE_F_SYNC) ? finish_sync(c, s) : MOE_OK;
+}
+
+int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const uint16_t* x2, const float* extra,
+                      uint16_t* x_next, uint16_t* y_out, float* logits_out, int flags, void* stream) {
+    int st = block_checks(c, layer, T);
+    if (st) return st;
+    if (T > 0 && (!h2 || !x2 || !x_next)) return fail(MOE_EINVAL, "null h2 / x2 / x_next");
+    if (c->cfg.ep_world > 1 && !c->ep_attached)
+        return fail(MOE_ESTATE, "expert-parallel block calls need the peer exchange (moe_ep_import)");
+    if (!c->shared || moe_expert_kind(c->shared, layer, 0) != kKindBF16 || !c->d_router[layer])
+        return fail(MOE_ESTATE, "layer %d needs its shared expert and router weights (moe_load_shared)", layer);
+    const bool host = flags & MOE_F_HOST;
+    if (!host && (!aligned16(h2) || !aligned16(x2) || !aligned16(extra) || !aligned16(x_next) || !aligned16(y_out) ||
+                  !aligned16(logits_out)))
+        return fail(MOE_EINVAL, "buffers must be 16-byte aligned");
+    if (T == 0) return MOE_OK;
+    DeviceGuard dg(c->dev);
+    cudaStream_t s = (cudaStream_t)stream;
+    const int H = c->cfg.hidden, E = c->cfg.n_experts;
+    const size_t NT = c->cfg.max_tokens, n = (size_t)T * H;
+    const uint16_t* dh = h2;
+    const uint16_t* dx = x2;
+    const float* de = extra;
+    uint16_t* dn = x_next;
+    if (host) {  // inputs to the device, outputs back, one synchronisation at the end
+        uint16_t* io = c->d_blk_io;
+        CUDA_TRY(cudaMemcpyAsync(io, h2, n * 2, cudaMemcpyHostToDevice, s));
+        CUDA_TRY(cudaMemcpyAsync(io + NT * H, x2, n * 2, cudaMemcpyHostToDevice, s));
+        if (extra) CUDA_TRY(cudaMemcpyAsync(c->d_blk_extra, extra, n * 4, cudaMemcpyHostToDevice, s));
+        dh = io;
+        dx = io + NT * H;
+        de = extra ? c->d_blk_extra : nullptr;
+        dn = io + 2 * NT * H;
+    }
+    float* lg = (logits_out && !host) ? logits_out : c->d_blk_logits;
+    uint16_t* y = (y_out && !host) ? y_out : c->d_blk_y;
+    // router-logit producer, routed experts (their plan runs as soon as the logits exist), shared
+    // expert (its plan overlaps the routed stream), then one element-wise pass for y and x_next
+    CUDA_TRY(launch_router_gemv(c->d_router[layer], dh, T, E, H, lg, s));
+    c->launches++;
+    if ((st = moe_forward(c, layer, T, dh, lg, c->d_blk_moe, nullptr, nullptr, 0, s))) return st;
+    if ((st = moe_forward(c->shared, layer, T, dh, c->d_blk_zero, c->d_blk_shared, nullptr, nullptr, 0, s))) return st;
+    CUDA_TRY(launch_residual(nullptr, dx, c->d_blk_shared, de, c->d_blk_moe, (long)n, y, dn, c->sm_count, s));
+    c->launches++;
+    if (host) {
+        CUDA_TRY(cudaMemcpyAsync(x_next, dn, n * 2, cudaMemcpyDeviceToHost, s));
+        if (y_out) CUDA_TRY(cudaMemcpyAsync(y_out, y, n * 2, cudaMemcpyDeviceToHost, s));
+        if (logits_out) CUDA_TRY(cudaMemcpyAsync(logits_out, lg, (size_t)T * E * 4, cudaMemcpyDeviceToHost, s));
+    }
+    return (host || (flags & MOE_F_SYNC)) ? block_sync(c, s) : MOE_OK;
+}
+
 int moe_status(moe_ctx* c, void* stream) {
     if (!c) return fail(MOE_EINVAL, "null context");
     DeviceGuard dg(c->dev);
     return finish_sync(c, (cudaStream_t)stream);
 }
 
-int64_t moe_launch_count(moe_ctx* c) { return c ? c->launches : -1; }
+int64_t moe_launch_count(moe_ctx* c) { return c ? c->launches + (c->shared ? c->shared->launches : 0) : -1; }
+
+static int set_option_one(moe_ctx* c, int option, int64_t value);
 
 int moe_set_option(moe_ctx* c, int option, int64_t value) {
     if (!c) return fail(MOE_EINVAL, "null context");
+    const int st = set_option_one(c, option, value);
+    // the shared-expert context follows the path options (not the test hook, not instrumentation)
+    if (st == MOE_OK && c->shared && option != MOE_OPT_INJECT_WAIT_TIMEOUT && option != MOE_OPT_TIMELINE)
+        return set_option_one(c->shared, option, value);
+    return st;
+}
+
+static int set_option_one(moe_ctx* c, int option, int64_t value) {
     switch (option) {
         case MOE_OPT_FUSED_DECODE:
             c->fused = value != 0;

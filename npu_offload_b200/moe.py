@@ -175,6 +175,66 @@ class MoEDataPlane:
                                 _stream_ptr(stream, x.device)))
         return (out, idx, w) if return_topk else out
 
+    # ---- the steps either side of the routed experts (one Solar MoE block, solar_engine/src/layer.rs:1-6) ----
+    def load_shared(self, layer, gate=None, up=None, down=None, router=None):
+        """Shared expert gate/up [F,H], down [H,F] and router weights [E,H] (bf16) of one layer."""
+        ws = [None if a is None else as_bf16(a) for a in (gate, up, down, router)]
+        on_dev = [w.is_cuda for w in ws if w is not None]
+        dev = bool(on_dev) and on_dev[0]
+        ws = [None if w is None else (w.to(self.device) if dev else w.cpu()) for w in ws]
+        if ws[0] is not None:
+            assert ws[0].shape == (self.F, self.H) and ws[1].shape == (self.F, self.H) and ws[2].shape == (self.H, self.F)
+        if ws[3] is not None:
+            assert ws[3].shape == (self.E, self.H)
+        check(lib().moe_load_shared(self._h, layer, *[_vp(w) for w in ws], 0 if dev else MOE_F_HOST))
+
+    def shared_router(self, layer, h2, x2, y=True, logits=True, stream=None, sync=False):
+        """(y bf16 [T,H] = bf16(x2 + shared(h2)), logits f32 [T,E] = h2 . Wr^T) on the device
+        (dense/shared.rs:1-3); either may be skipped."""
+        h = as_bf16(h2)
+        T = h.shape[0]
+        x = as_bf16(x2) if y else None
+        yo = torch.empty(T, self.H, dtype=torch.bfloat16, device=h.device) if y else None
+        lo = torch.empty(T, self.E, dtype=torch.float32, device=h.device) if logits else None
+        check(lib().moe_shared_router(self._h, layer, T, _vp(h), _vp(x), _vp(yo), _vp(lo), MOE_F_SYNC if sync else 0,
+                                      _stream_ptr(stream, h.device)))
+        return yo, lo
+
+    def combine_residual(self, y, moe_out, extra=None, stream=None, sync=False):
+        """x_next bf16 [T,H] = bf16((y + extra) + moe_out) (dense/combine.rs:1)."""
+        yy = as_bf16(y)
+        m = _as(moe_out, torch.float32)
+        e = None if extra is None else _as(extra, torch.float32)
+        T = yy.shape[0]
+        xn = torch.empty(T, self.H, dtype=torch.bfloat16, device=yy.device)
+        check(lib().moe_combine_residual(self._h, T, _vp(yy), _vp(e), _vp(m), _vp(xn), MOE_F_SYNC if sync else 0,
+                                         _stream_ptr(stream, yy.device)))
+        return xn
+
+    def block_forward(self, layer, h2, x2, extra=None, return_parts=False, stream=None, sync=False):
+        """One MoE block: x_next = bf16((bf16(x2 + shared(h2)) + extra) + routed(h2, h2 . Wr^T)).
+        Device tensors in, device x_next out (with y and the logits when return_parts)."""
+        h = as_bf16(h2)
+        x = as_bf16(x2)
+        e = None if extra is None else _as(extra, torch.float32)
+        T = h.shape[0]
+        xn = torch.empty(T, self.H, dtype=torch.bfloat16, device=h.device)
+        yo = torch.empty(T, self.H, dtype=torch.bfloat16, device=h.device) if return_parts else None
+        lo = torch.empty(T, self.E, dtype=torch.float32, device=h.device) if return_parts else None
+        check(lib().moe_block_forward(self._h, layer, T, _vp(h), _vp(x), _vp(e), _vp(xn), _vp(yo), _vp(lo),
+                                      MOE_F_SYNC if sync else 0, _stream_ptr(stream, h.device)))
+        return (xn, yo, lo) if return_parts else xn
+
+    def block_forward_host(self, layer, h2, x2, extra=None):
+        """block_forward with host buffers (synchronous): returns x_next as a CPU bf16 tensor."""
+        h = as_bf16(h2).cpu()
+        x = as_bf16(x2).cpu()
+        e = None if extra is None else _as(extra, torch.float32).cpu()
+        xn = torch.empty(h.shape[0], self.H, dtype=torch.bfloat16)
+        check(lib().moe_block_forward(self._h, layer, h.shape[0], _vp(h), _vp(x), _vp(e), _vp(xn), None, None,
+                                      MOE_F_HOST, _stream_ptr(None, self.device)))
+        return xn
+
     def forward_host(self, layer, hidden, logits, out=None, return_topk=False, accumulate=False):
         """Host buffers in and out (numpy or CPU tensors).  On the fused path pinned logits and
         16-byte-aligned pinned outputs are used in place by the kernels; others are staged."""

@@ -375,3 +375,59 @@ int or_moe_layer(int T, int H, int F, int E, int K, int scoring, const uint16_t*
     free(jgu); free(jd); free(jq); free(jsc); free(toff); free(toks); free(ws);
     return st;
 }
+
+/*
+ * Router-logit producer, track2_opt/solar_engine/src/dense/shared.rs:1-3 (`shared_router`):
+ *   logits[t, e] = h2_t . Wr[e, :]   fp32 accumulate, fp32 out.  Wr: [E, H] bf16 row-major.
+ */
+void or_router_logits(int T, int E, int H, const uint16_t* h2, const uint16_t* wr, float* logits) {
+    #pragma omp parallel for schedule(static)
+    for (int e = 0; e < E; e++)
+        for (int t = 0; t < T; t++) logits[(size_t)t * E + e] = dot_bf16(wr + (size_t)e * H, h2 + (size_t)t * H, H);
+}
+
+/*
+ * Shared expert + residual of shared.rs:1-3:  y = bf16(x2 + Wsd @ (silu(Wsg h2) * (Wsu h2))), fp32 add
+ * before the one rounding.  device_rounding = 0: the expert in cpu_moe's rounding points (g, u fp32,
+ * act bf16; cpu_moe.cpp:63-93), the form the B200 kernels compute.  device_rounding = 1: the
+ * reference's own host checker of its device kernels, expert_ref (solar_engine/src/host_util.rs:35-46:
+ * g and u rounded to bf16 before SwiGLU).  gu: [2F, H] (gate rows, then up rows); d: [H, F].
+ * shared_out (optional) receives the fp32 expert output before the residual.
+ */
+void or_shared_expert(int T, int H, int F, const uint16_t* h2, const uint16_t* x2, const uint16_t* gu,
+                      const uint16_t* d, int device_rounding, float* shared_out, uint16_t* y) {
+    uint16_t* act = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(T > 0 ? T : 1) * F);
+    float* s = (float*)malloc(sizeof(float) * (size_t)(T > 0 ? T : 1) * H);
+    #pragma omp parallel for schedule(static)
+    for (int f = 0; f < F; f++)
+        for (int t = 0; t < T; t++) {
+            const uint16_t* xt = h2 + (size_t)t * H;
+            float g = dot_bf16(gu + (size_t)f * H, xt, H), u = dot_bf16(gu + (size_t)(F + f) * H, xt, H);
+            if (device_rounding) {
+                g = bf2f(f2bf(g));
+                u = bf2f(f2bf(u));
+            }
+            act[(size_t)t * F + f] = swiglu_bf16(g, u);
+        }
+    #pragma omp parallel for schedule(static)
+    for (int h = 0; h < H; h++)
+        for (int t = 0; t < T; t++) s[(size_t)t * H + h] = dot_bf16(d + (size_t)h * F, act + (size_t)t * F, F);
+    for (size_t i = 0; i < (size_t)T * H; i++) {
+        if (shared_out) shared_out[i] = s[i];
+        if (y) y[i] = f2bf(bf2f(x2[i]) + s[i]);
+    }
+    free(act);
+    free(s);
+}
+
+/*
+ * Residual combine into the next layer's input, solar_engine/src/dense/combine.rs:1 and
+ * layer.rs:4:  x_next = bf16((y + extra) + moe), fp32 math, one rounding.  moe is the combined
+ * routed-expert sum (sum_k g_k e_k); extra may be NULL (then x_next = bf16(y + moe)).
+ */
+void or_combine_residual(long n, const uint16_t* y, const float* extra, const float* moe, uint16_t* x_next) {
+    for (long i = 0; i < n; i++) {
+        const float s = extra ? bf2f(y[i]) + extra[i] : bf2f(y[i]);
+        x_next[i] = f2bf(s + moe[i]);
+    }
+}

@@ -73,6 +73,13 @@ class Port:
             lib.or_place_expert_q8.restype = None
             lib.or_moe_layer.argtypes = [ctypes.c_int] * 6 + [_c_u16p, _c_f32p, _c_f32p] + [ctypes.c_void_p] * 4 + \
                 [_c_f32p, _c_i32p, _c_f32p]
+            lib.or_router_logits.argtypes = [ctypes.c_int] * 3 + [_c_u16p, _c_u16p, _c_f32p]
+            lib.or_router_logits.restype = None
+            lib.or_shared_expert.argtypes = [ctypes.c_int] * 3 + [_c_u16p] * 4 + [ctypes.c_int, ctypes.c_void_p,
+                                                                                  ctypes.c_void_p]
+            lib.or_shared_expert.restype = None
+            lib.or_combine_residual.argtypes = [ctypes.c_long, _c_u16p, ctypes.c_void_p, _c_f32p, _c_u16p]
+            lib.or_combine_residual.restype = None
             lib.or_set_threads.argtypes = [ctypes.c_int]
             lib.or_set_threads.restype = None
             lib.or_max_threads.restype = ctypes.c_int
@@ -185,6 +192,43 @@ class Port:
                                     _ptr_array(qs) if any(q is not None for q in qs) else None, _ptr_array(scs),
                                     _p(out, _c_f32p), _p(idx, _c_i32p), _p(w, _c_f32p))
         return out, idx[:T], w[:T], st
+
+
+    @classmethod
+    def router_logits(cls, h2, wr):
+        """logits [T, E] = h2 . wr^T in fp32 (solar_engine/src/dense/shared.rs:3)."""
+        h2, wr = np.ascontiguousarray(h2, np.uint16), np.ascontiguousarray(wr, np.uint16)
+        T, H = h2.shape
+        E = wr.shape[0]
+        out = np.zeros((T, E), np.float32)
+        cls.lib().or_router_logits(T, E, H, _p(h2, _c_u16p), _p(wr, _c_u16p), _p(out, _c_f32p))
+        return out
+
+    @classmethod
+    def shared_expert(cls, h2, x2, g, u, d, device_rounding=False):
+        """(y bf16 [T,H], shared fp32 [T,H]): y = bf16(x2 + down . SwiGLU(gate . h2, up . h2)) (shared.rs:1-3).
+        device_rounding follows the reference's host checker expert_ref (host_util.rs:35-46)."""
+        h2, x2 = np.ascontiguousarray(h2, np.uint16), np.ascontiguousarray(x2, np.uint16)
+        gu = np.ascontiguousarray(np.concatenate([g, u], 0), np.uint16)
+        d = np.ascontiguousarray(d, np.uint16)
+        T, H = h2.shape
+        F = d.shape[1]
+        y = np.zeros((T, H), np.uint16)
+        s = np.zeros((T, H), np.float32)
+        cls.lib().or_shared_expert(T, H, F, _p(h2, _c_u16p), _p(x2, _c_u16p), _p(gu, _c_u16p), _p(d, _c_u16p),
+                                   int(bool(device_rounding)), s.ctypes.data, y.ctypes.data)
+        return y, s
+
+    @classmethod
+    def combine_residual(cls, y, extra, moe):
+        """x_next = bf16((y + extra) + moe) (combine.rs:1, layer.rs:4); extra may be None."""
+        y = np.ascontiguousarray(y, np.uint16)
+        moe = np.ascontiguousarray(moe, np.float32)
+        ex = None if extra is None else np.ascontiguousarray(extra, np.float32)
+        out = np.zeros(y.shape, np.uint16)
+        cls.lib().or_combine_residual(y.size, _p(y, _c_u16p), None if ex is None else ex.ctypes.data,
+                                      _p(moe, _c_f32p), _p(out, _c_u16p))
+        return out
 
 
 def cpu_flags():

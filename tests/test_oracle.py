@@ -168,3 +168,58 @@ def test_oracle_matches_compiled_reference_live():
     for a, b in zip(Port.place_expert_q8(g0, u0, d0), Reference.place_expert_q8(g0, u0, d0)):
         np.testing.assert_array_equal(a, b)
     _ = rng
+
+
+# ---- the steps either side of the path: router-logit producer, shared expert, residual combine ----
+
+def _bf(a):
+    from oracle.oracle import f2bf
+    return f2bf(np.asarray(a, np.float32))
+
+
+def test_router_logits_restatement():
+    """logits = h2 . Wr^T in fp32 (solar_engine/src/dense/shared.rs:3) against a float64 product."""
+    from oracle.oracle import bf2f
+    rng = np.random.default_rng(7)
+    h2, wr = _bf(rng.standard_normal((5, 512))), _bf(rng.standard_normal((24, 512)) * 0.02)
+    got = Port.router_logits(h2, wr)
+    ref = bf2f(h2).astype(np.float64) @ bf2f(wr).astype(np.float64).T
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_shared_expert_restatement_rounding_points():
+    """y = bf16(x2 + shared) with the shared expert in cpu_moe's rounding points: its fp32 output is
+    exactly the restated cpu_moe with weight 1 for every token; device_rounding (the reference's
+    expert_ref, host_util.rs:35-46) differs only by the bf16 rounding of g and u."""
+    from oracle.oracle import bf2f
+    H, F, T = 256, 128, 3
+    g, u, d = synth.expert_weights(5, 0, 0, H, F)
+    h2, x2 = synth.hidden(11, T, H), synth.hidden(12, T, H)
+    y, s = Port.shared_expert(h2, x2, g, u, d)
+    ref = Port.cpu_moe(h2, [("bf16", np.concatenate([g, u], 0), d)], [np.arange(T)], [np.ones(T, np.float32)])
+    np.testing.assert_array_equal(s, ref)
+    np.testing.assert_array_equal(y, _bf(bf2f(x2) + s))
+    y2, s2 = Port.shared_expert(h2, x2, g, u, d, device_rounding=True)
+    assert_close(s2, s, max_abs=2e-3, min_cos=0.9999, what="device rounding")
+
+
+def test_combine_residual_restatement():
+    """x_next = bf16((y + extra) + moe) (combine.rs:1): one rounding of the fp32 sum, exactly."""
+    from oracle.oracle import bf2f
+    rng = np.random.default_rng(3)
+    y = _bf(rng.standard_normal(1000))
+    ex = rng.standard_normal(1000).astype(np.float32)
+    moe = rng.standard_normal(1000).astype(np.float32)
+    np.testing.assert_array_equal(Port.combine_residual(y, ex, moe), _bf((bf2f(y) + ex) + moe))
+    np.testing.assert_array_equal(Port.combine_residual(y, None, moe), _bf(bf2f(y) + moe))
+
+
+@pytest.mark.skipif(not Reference.available(), reason="compiled reference unavailable: " + Reference.why_unavailable())
+def test_shared_expert_matches_compiled_reference():
+    """The shared expert in cpu_moe semantics against the compiled reference cpu_moe (weight 1)."""
+    H, F, T = 512, 256, 4
+    g, u, d = synth.expert_weights(21, 0, 0, H, F)
+    h2, x2 = synth.hidden(31, T, H), synth.hidden(32, T, H)
+    _, s = Port.shared_expert(h2, x2, g, u, d)
+    ref = Reference.cpu_moe(h2, [np.concatenate([g, u], 0)], [d], [np.arange(T)], [np.ones(T, np.float32)])
+    assert_close(s, ref, max_abs=1e-5, min_cos=0.9999999, what="shared vs cpu_moe")
