@@ -673,6 +673,48 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         snapshot_err();
         return;
     }
+    if (a.block) {  // MoE block: residual and combine into the next layer's input (combine.rs:1)
+        const int sp0 = min(max(c.sh.sp0, 0), np - a.T);
+        for (int f = tid; f < a.T * nq; f += kCThreads) {
+            const int t = f / nq, q = f % nq;
+            const size_t e0 = (size_t)t * H + 4 * (size_t)(q0 + q);  // first of the quad's 4 elements
+            float r[4] = {0.f, 0.f, 0.f, 0.f};
+            const int npt = min(c.sh.tpn[t], kMaxTopK);
+            for (int m = 0; m < npt; m++) {
+                const int p = min(max(c.sh.tpair[t][m], 0), np - 1);
+                const float w = c.sh.pw[p];
+                const float4 v = R[(size_t)p * nq + q];
+                r[0] = fmaf(w, v.x, r[0]);
+                r[1] = fmaf(w, v.y, r[1]);
+                r[2] = fmaf(w, v.z, r[2]);
+                r[3] = fmaf(w, v.w, r[3]);
+            }
+            const float4 sv = R[(size_t)(sp0 + t) * nq + q];
+            const float sh[4] = {sv.x, sv.y, sv.z, sv.w};
+            const uint2 xv = *reinterpret_cast<const uint2*>(a.x2 + e0);
+            const float x2v[4] = {bf_lo(xv.x), bf_hi(xv.x), bf_lo(xv.y), bf_hi(xv.y)};
+            float ex[4] = {0.f, 0.f, 0.f, 0.f};
+            if (a.extra) {
+                const float4 ev = *reinterpret_cast<const float4*>(a.extra + e0);
+                ex[0] = ev.x, ex[1] = ev.y, ex[2] = ev.z, ex[3] = ev.w;
+            }
+            uint16_t yb[4], xb[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                yb[k] = f2bf(x2v[k] + sh[k]);  // y = bf16(x2 + shared): shared.rs:2
+                const float y = bf_lo(yb[k]);
+                xb[k] = f2bf((a.extra ? y + ex[k] : y) + r[k]);
+            }
+            *reinterpret_cast<uint2*>(a.x_next + e0) =
+                make_uint2((uint32_t)xb[0] | ((uint32_t)xb[1] << 16), (uint32_t)xb[2] | ((uint32_t)xb[3] << 16));
+            if (a.y_out)
+                *reinterpret_cast<uint2*>(a.y_out + e0) =
+                    make_uint2((uint32_t)yb[0] | ((uint32_t)yb[1] << 16), (uint32_t)yb[2] | ((uint32_t)yb[3] << 16));
+        }
+        if (tl && tid == 0) tl[5] = globaltimer_ns();
+        snapshot_err();
+        return;
+    }
     for (int f = tid; f < a.T * nq; f += kCThreads) {
         const int t = f / nq, q = f % nq;
         float4* o = reinterpret_cast<float4*>(a.out + (size_t)t * H) + q0 + q;

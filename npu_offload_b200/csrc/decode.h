@@ -34,6 +34,7 @@ struct __align__(16) PlanCta {
 // Routing result and reduction tables of one call, read by every CTA after its segments.
 struct __align__(16) PlanShared {
     int T, np, ngrp, nsegtot;
+    int sp0, pad_[3];                        // block calls: first pair of the shared expert (pair sp0 + t = token t)
     int gvs0[kMaxGroups], gvs1[kMaxGroups];  // segment range [gvs0, gvs1) of each token group
     int pgrp[kDecodeMaxPairs];               // token group of pair p (pairs job-major)
     int prow[kDecodeMaxPairs];               // row of pair p inside its group
@@ -88,6 +89,8 @@ struct PlanArgs {
     uint64_t* timeline;    // optional kTimelineSlots phase stamps of the plan kernel, else null
     const uint16_t* x_src; // optional: hidden states in device-accessible pinned host memory, copied
     uint16_t* x_dst;       //   by the plan kernel to x_dst ([T, H] bf16) before it publishes the plan
+    const ExpDesc* shared; // block calls: the layer's shared expert, appended as one more job whose
+                           //   pairs are every token with weight 1 (kept out of the routed sum)
 };
 
 struct DecodeArgs {
@@ -115,6 +118,13 @@ struct DecodeArgs {
     int ns_cap;            // tuning: cap on ring stages (0 = as many as shared memory allows)
     uint32_t stage_target; // tuning: target bytes per ring stage (0 = default)
     EpExchange ep;         // cross-rank combine (ep.world > 1 with peers attached), else world = 0
+    // block calls (plan with a shared expert): instead of out, x_next = bf16((y + extra) + routed)
+    // with y = bf16(x2 + shared); y_out (optional) receives y; extra may be null
+    int block;
+    const uint16_t* x2;
+    const float* extra;
+    uint16_t* x_next;
+    uint16_t* y_out;
 };
 
 // Host-side planning: shared-memory size and stage geometry for (T, H, F) on `grid` CTAs.

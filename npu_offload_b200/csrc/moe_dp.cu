@@ -338,7 +338,7 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
 
 // Launches plan_kernel + decode_kernel for one layer (da prepared by prepare_fused, x / out set).
 int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t dsmem, cudaStream_t st,
-                 cudaEvent_t* marks, const uint16_t* x_host = nullptr) {
+                 cudaEvent_t* marks, const uint16_t* x_host = nullptr, const ExpDesc* shared = nullptr) {
     const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
     da.ep = next_ep(c);
     const uint32_t epoch = c->epoch++;
@@ -363,6 +363,7 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     pa.ups_bf16 = da.ups_bf16;
     pa.ups_q8 = da.ups_q8;
     pa.timeline = c->d_timeline ? c->d_timeline + (size_t)(c->sm_count - 1) * kTimelineSlots : nullptr;
+    pa.shared = shared;
     if (x_host) {  // the plan kernel moves the hidden states: da.x is the device copy it writes
         pa.x_src = x_host;
         pa.x_dst = const_cast<uint16_t*>(da.x);
@@ -1430,14 +1431,32 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
     }
     float* lg = (logits_out && !host) ? logits_out : c->d_blk_logits;
     uint16_t* y = (y_out && !host) ? y_out : c->d_blk_y;
-    // router-logit producer, routed experts (their plan runs as soon as the logits exist), shared
-    // expert (its plan overlaps the routed stream), then one element-wise pass for y and x_next
-    CUDA_TRY(launch_router_gemv(c->d_router[layer], dh, T, E, H, lg, s));
+    const int K = c->cfg.top_k;
+    CUDA_TRY(launch_router_gemv(c->d_router[layer], dh, T, E, H, lg, s));  // router-logit producer
     c->launches++;
-    if ((st = moe_forward(c, layer, T, dh, lg, c->d_blk_moe, nullptr, nullptr, 0, s))) return st;
-    if ((st = moe_forward(c->shared, layer, T, dh, c->d_blk_zero, c->d_blk_shared, nullptr, nullptr, 0, s))) return st;
-    CUDA_TRY(launch_residual(nullptr, dx, c->d_blk_shared, de, c->d_blk_moe, (long)n, y, dn, c->sm_count, s));
-    c->launches++;
+    DecodeArgs da{};
+    size_t dsmem = 0;
+    // fused: the shared expert is one more job of the routed unit stream, and the decode kernel's
+    // reduction writes y and x_next (one plan, one decode grid)
+    const bool fused = c->cfg.ep_world == 1 && !c->prof_on && T * (K + 1) <= kDecodeMaxPairs &&
+                       c->sm_count - 1 + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
+    if (fused) {
+        da.x = dh;
+        da.out = c->d_blk_moe;
+        da.block = 1;
+        da.x2 = dx;
+        da.extra = de;
+        da.x_next = dn;
+        da.y_out = y;
+        if ((st = launch_fused(c, layer, lg, da, dsmem, s, nullptr, nullptr, c->shared->d_desc + layer))) return st;
+    } else {
+        // routed experts (their plan runs as soon as the logits exist), shared expert (its plan
+        // overlaps the routed stream), then one element-wise pass for y and x_next
+        if ((st = moe_forward(c, layer, T, dh, lg, c->d_blk_moe, nullptr, nullptr, 0, s))) return st;
+        if ((st = moe_forward(c->shared, layer, T, dh, c->d_blk_zero, c->d_blk_shared, nullptr, nullptr, 0, s))) return st;
+        CUDA_TRY(launch_residual(nullptr, dx, c->d_blk_shared, de, c->d_blk_moe, (long)n, y, dn, c->sm_count, s));
+        c->launches++;
+    }
     if (host) {
         CUDA_TRY(cudaMemcpyAsync(x_next, dn, n * 2, cudaMemcpyDeviceToHost, s));
         if (y_out) CUDA_TRY(cudaMemcpyAsync(y_out, y, n * 2, cudaMemcpyDeviceToHost, s));

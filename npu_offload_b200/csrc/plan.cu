@@ -205,6 +205,20 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
             ng += __shfl_sync(0xffffffffu, gincl, 31);
         }
         if (lane == 0) {
+            m.sh.sp0 = -1;
+            if (a.shared) {  // block call: the shared expert is one more job, every token at weight 1
+                const ExpDesc d = *a.shared;
+                m.jkind[nj] = d.kind;
+                m.jw1[nj] = static_cast<const unsigned char*>(d.w1);
+                m.jsc[nj] = d.sc;
+                m.jp0[nj] = np;
+                m.jg0[nj] = ng;
+                m.sh.sp0 = np;
+                if (d.kind != kKindBF16 && d.kind != kKindQ8) atomicOr(a.err, kErrBadExpert);
+                nj++;
+                np += T;
+                ng += (T + GM - 1) / GM;
+            }
             m.nj = nj;
             m.np = np;
             m.ngrp = ng;
@@ -237,7 +251,15 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(const PlanArgs a)
     for (int t = tid; t < T; t += kPlanThreads) {
         int n = 0;
         for (int k = 0; k < K; k++) n += m.jmap[m.idx[t][k]] >= 0;
-        m.sh.tpn[t] = n;
+        m.sh.tpn[t] = n;  // routed pairs only: the shared expert's pair is added apart
+        const int sp0 = m.sh.sp0;
+        if (sp0 >= 0) {
+            const int p = sp0 + t, j = nj - 1;
+            m.ptok[p] = t;
+            m.sh.pgrp[p] = m.jg0[j] + t / GM;
+            m.sh.prow[p] = t % GM;
+            m.sh.pw[p] = 1.f;
+        }
     }
     for (int j = tid; j < nj; j += kPlanThreads)
         for (int g = m.jg0[j]; g < m.jg0[j + 1]; g++) m.gjob[g] = j;

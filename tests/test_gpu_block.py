@@ -88,14 +88,20 @@ def test_shared_router_and_block_small(T):
         y_dev, _ = Port.shared_expert(h2, x2, sg, su, sd, device_rounding=True)
         d = np.abs(bf2f(bf16_np(y)) - bf2f(y_dev))
         assert np.mean(d > 0.02 * np.abs(bf2f(y_dev)) + 0.01 + 1e-3) < 0.01
-        # routed experts on the produced logits, then the residual combine: bit-identical to the fused call
+        # routed experts on the produced logits, then the residual combine
         moe = p.forward(layer, _dev(h2), torch.from_numpy(lg).cuda(), sync=True)
         xn = p.combine_residual(y, moe, extra=torch.from_numpy(extra).cuda(), sync=True)
         xb, yb, lb = p.block_forward(layer, _dev(h2), _dev(x2), extra=torch.from_numpy(extra).cuda(),
                                      return_parts=True, sync=True)
         np.testing.assert_array_equal(lb.cpu().numpy(), lg)
-        np.testing.assert_array_equal(bf16_np(yb), bf16_np(y))
-        np.testing.assert_array_equal(bf16_np(xb), bf16_np(xn))
+        if T <= 16:
+            # one fused decode grid streams the shared expert with the routed ones: its share
+            # boundaries, hence the partial-sum order, differ from the separate calls'
+            assert_bf16_close(bf16_np(yb), bf16_np(y), f"fused y T={T}")
+            assert_bf16_close(bf16_np(xb), bf16_np(xn), f"fused x_next T={T}", slack=_ulp_bf16(bf2f(bf16_np(y))))
+        else:  # the composition of the separate calls, bit for bit
+            np.testing.assert_array_equal(bf16_np(yb), bf16_np(y))
+            np.testing.assert_array_equal(bf16_np(xb), bf16_np(xn))
         # against the oracle: routed layer on the same logits, residual combine restated
         moe_ref, idx, _, st = Port.moe_layer(h2, lg, ex, K)
         assert st == 0
@@ -108,9 +114,14 @@ def test_shared_router_and_block_small(T):
         xh = p.block_forward_host(layer, torch.from_numpy(h2.view(np.int16)).view(torch.bfloat16),
                                   torch.from_numpy(x2.view(np.int16)).view(torch.bfloat16), extra=torch.from_numpy(extra))
         np.testing.assert_array_equal(bf16_np(xh), bf16_np(xb))
-        # no extra: x_next = bf16(y + moe)
+        # no extra: x_next = bf16(y + moe); repeated calls give the same bits
         xb0 = p.block_forward(layer, _dev(h2), _dev(x2), sync=True)
-        np.testing.assert_array_equal(bf16_np(xb0), Port.combine_residual(bf16_np(y), None, moe.cpu().numpy()))
+        np.testing.assert_array_equal(bf16_np(p.block_forward(layer, _dev(h2), _dev(x2), sync=True)), bf16_np(xb0))
+        ref0 = Port.combine_residual(bf16_np(y), None, moe.cpu().numpy())
+        if T <= 16:
+            assert_bf16_close(bf16_np(xb0), ref0, f"fused x_next, no extra, T={T}", slack=_ulp_bf16(bf2f(bf16_np(y))))
+        else:
+            np.testing.assert_array_equal(bf16_np(xb0), ref0)
     finally:
         p.close()
 
