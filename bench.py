@@ -7,9 +7,11 @@ permutation + expert FFN (GEMV path) + combine, through the library's hot path (
 
   N = 1: configs[1] -- 8 Solar-shaped MoE layers (H 4096, 128 experts, F 1280, top-8), 32.2 GB of
          bf16 expert weights resident, decode batch --batch (default 1; --sweep adds 4 and 16).
-  N > 1: configs[2] pro-rated -- 6*N layers (48 at N = 8), experts sharded expert-parallel with the
-         popularity-striped shard map (16 experts per GPU per layer at N = 8), one NCCL all-reduce
-         of the fp32 partial outputs per layer.  Weak scaling: per-GPU expert bytes stay fixed.
+  N > 1: configs[2] pro-rated -- 6*N layers (48 at N = 8), expert-parallel with every GPU holding the
+         same slice of the intermediate units of every expert (--ep-shard units, the default;
+         --ep-shard experts deals whole experts by popularity stripe instead), combined per layer
+         inside the decode kernel over NVLink peer memory (--ep nccl: one NCCL all-reduce).  Weak
+         scaling: per-GPU expert bytes stay fixed.
 
 value = MoE-layer tokens/s = batch * layers / step time (max over ranks, CUDA events).
 Synthetic seeded inputs (no checkpoint exists here): weights N(0, 0.02) bf16, hidden N(0,1) bf16,
@@ -62,6 +64,8 @@ def parse():
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="configs[3] prefill measurement at N=1 (0 to skip)")
     ap.add_argument("--no-block", action="store_true", help="skip the moe_block_forward measurement")
+    ap.add_argument("--ep-shard", choices=["units", "experts"], default="units",
+                    help="N>1 split: every rank a slice of every expert's units, or whole experts per rank")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="N>1 combine: in-kernel NVLink peer exchange (p2p) or an NCCL all-reduce per layer")
     return ap.parse_args()
@@ -163,8 +167,10 @@ def popularity_counts(seed, L):
     return out
 
 
-def load_weights(plane, layers, owner, rank, seed, device):
+def load_weights(plane, layers, owner, rank, seed, device, units=None):
+    """This rank's experts (owner[l, e] == rank); with units = (f0, f1) only those units of each."""
     import torch
+    from npu_offload_b200.parallel import unit_slice
     gen = torch.Generator(device=device)
     FH = F * H
     for l in range(layers):
@@ -173,7 +179,10 @@ def load_weights(plane, layers, owner, rank, seed, device):
                 continue
             gen.manual_seed(seed * 1_000_003 + 1009 * l + e)
             buf = (torch.randn(3 * FH, generator=gen, device=device) * 0.02).to(torch.bfloat16)
-            plane.load_expert(l, e, buf[:FH].view(F, H), buf[FH:2 * FH].view(F, H), buf[2 * FH:].view(H, F))
+            g, u, d = buf[:FH].view(F, H), buf[FH:2 * FH].view(F, H), buf[2 * FH:].view(H, F)
+            if units is not None:
+                g, u, d = unit_slice(g, u, d, *units)
+            plane.load_expert(l, e, g, u, d)
     torch.cuda.synchronize(device)
 
 
@@ -184,12 +193,21 @@ class Stack:
         import torch
         from npu_offload_b200.moe import MoEDataPlane
         from npu_offload_b200.parallel import shard_map
+        from npu_offload_b200.parallel import unit_ranges
         self.T, self.L, self.ws, self.rank, self.device = T, L, ws, rank, device
-        self.owner = shard_map(popularity_counts(args.seed, L), ws) if ws > 1 else np.zeros((L, E), np.int32)
-        self.plane = MoEDataPlane(H, F, E, K, n_layers=L, max_tokens=max(T, 16, getattr(args, "prefill_tokens", 0)),
-                                  device=device.index,
+        self.units = None
+        self.shard = getattr(args, "ep_shard", "units") if ws > 1 else None
+        if ws > 1 and self.shard == "units":  # every rank owns its slice of the units of every expert
+            self.units = unit_ranges(F, ws)[rank]
+            self.owner = np.full((L, E), rank, np.int32)
+        else:
+            self.owner = shard_map(popularity_counts(args.seed, L), ws) if ws > 1 else np.zeros((L, E), np.int32)
+        F_local = F if self.units is None else self.units[1] - self.units[0]
+        self.ebytes = 3 * H * F_local * 2  # streamed bytes of one routed expert on this rank
+        self.plane = MoEDataPlane(H, F_local, E, K, n_layers=L,
+                                  max_tokens=max(T, 16, getattr(args, "prefill_tokens", 0)), device=device.index,
                                   ep_rank=rank, ep_world=ws, shard_map=self.owner if ws > 1 else None)
-        load_weights(self.plane, L, self.owner, rank, args.seed, device)
+        load_weights(self.plane, L, self.owner, rank, args.seed, device, self.units)
         if ws > 1 and getattr(args, "ep", "p2p") == "p2p":
             from npu_offload_b200.parallel import attach_peers
             attach_peers(self.plane)  # the decode kernel combines over NVLink peer memory
@@ -213,7 +231,7 @@ class Stack:
                 ids = set(idx.cpu().numpy().ravel().tolist())
                 loc = [e for e in ids if self.owner[l, e] == self.rank]
                 self.ucount[r, l] = len(loc)
-                self.ubytes[r, l] = len(loc) * EXPERT_BYTES
+                self.ubytes[r, l] = len(loc) * self.ebytes
         torch.cuda.synchronize(self.device)
 
     def step(self, s):
@@ -535,7 +553,7 @@ def our_arm(args):
     R = stack.R
     reps = [(args.warmup + s) % R for s in range(args.steps)]
     n_dec = args.steps * L
-    all_bytes = sum(stack.ucount[r].sum() for r in reps) * EXPERT_BYTES
+    all_bytes = sum(stack.ucount[r].sum() for r in reps) * stack.ebytes
     bpl = all_bytes / n_dec
     dur_s = ms / 1e3 / n_dec
     achieved = bpl / dur_s / 1e9
@@ -561,7 +579,7 @@ def our_arm(args):
         sms, _, _ = timed(stack, ks, min(args.warmup, 3), ws, profile=False)
         sms = max_over_ranks(sms, ws)
         reps = [(min(args.warmup, 3) + s) % R for s in range(ks)]
-        ub = sum(stack.ucount[r].sum() for r in reps) * EXPERT_BYTES
+        ub = sum(stack.ucount[r].sum() for r in reps) * stack.ebytes
         sweep.append({"batch": tb, "value": tb * L * ks / (sms / 1e3), "layer_gbs": ub / (sms / 1e3) / 1e9,
                       "experts_per_layer": float(np.mean([stack.ucount[r].mean() for r in reps]))})
     launches_all = int(sum_over_ranks(launches, ws))
@@ -601,6 +619,9 @@ def our_arm(args):
                            "parallelism": f"ep{ws}" if ws > 1 else "single",
                            "combine": ("in-kernel NVLink peer exchange" if args.ep == "p2p" else "NCCL all-reduce")
                                       if ws > 1 else None,
+                           "ep_shard": (f"units: each GPU {stack.units[1] - stack.units[0]} of {F} units of every "
+                                        "expert" if stack.shard == "units" else "experts: popularity stripe")
+                                       if ws > 1 else None,
                            "l2": "no flush: each step streams its routed experts (~%.1f GB/step/GPU) >> 126 MB L2"
                                  % (ubytes_main.mean() * L / 1e9),
                            "experts_per_layer": float(ucount_main.mean())},

@@ -1,5 +1,9 @@
 """Expert parallelism across the GPUs of one box (one process per GPU, torch.distributed).
 
+Two ways to split the experts: by expert (``shard_map``: each rank owns whole experts) or by unit
+(``unit_ranges``: each rank owns the same slice of the intermediate units of every expert; the
+context of rank r is then created with ``inter = f1 - f0`` and owns all experts).
+
 The shard map is npu-offload's placement plan turned into ownership: experts are ranked by
 popularity (profile counts, moe_offload/placement.py:15-16 ``ranks``) and dealt round-robin to the
 ranks (the alternating assignment of solar_hybrid/runtime.py:522-533), so every rank gets a
@@ -35,6 +39,29 @@ def shard_map(counts_per_layer, world, policy="stripe"):
         for r, e in enumerate(order):
             out[l, e] = r % world if policy == "stripe" else min(r // per, world - 1)
     return out
+
+
+def unit_ranges(F, world, align=64):
+    """Unit sharding: rank r owns units [f0, f1) of EVERY expert (gate rows, up rows and down columns
+    f0..f1), contiguous multiples of `align`, as even as possible.  A unit's activation needs only
+    its own gate and up rows, and its down column adds into all H outputs, so the per-rank partial
+    sums add up to the full expert output.  Every rank then streams the same share of each routed
+    expert, however the router skews the expert choice."""
+    chunks = F // align
+    if F % align or chunks < world:
+        raise ValueError(f"F={F} does not split into {world} shares of {align}-unit multiples")
+    base, extra = divmod(chunks, world)
+    out, f = [], 0
+    for r in range(world):
+        n = (base + (1 if r < extra else 0)) * align
+        out.append((f, f + n))
+        f += n
+    return out
+
+
+def unit_slice(gate, up, down, f0, f1):
+    """This rank's part of one expert under unit sharding: gate/up rows and down columns f0..f1."""
+    return gate[f0:f1], up[f0:f1], down[:, f0:f1]
 
 
 def local_experts(smap, layer, rank):

@@ -1,5 +1,6 @@
 """Expert parallelism across two GPUs with the in-kernel NVLink peer exchange: one process per GPU,
-each owning half of the experts (popularity stripe), both mapping each other's exchange buffers.
+each owning half of the experts (popularity stripe) or half of every expert's units, both mapping
+each other's exchange buffers.
 Every rank must return the same full layer output, bit for bit, and it must match the oracle.
 Needs two GPUs (skipped otherwise): kernels that wait on each other must never share one GPU."""
 import os
@@ -30,25 +31,30 @@ def _inputs(T, seed):
     return f2bf(rng.standard_normal((T, H), np.float32)), rng.standard_normal((T, E)).astype(np.float32)
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, mode):
     try:
         import datetime
         import torch.distributed as dist
         from npu_offload_b200.moe import MoEDataPlane
-        from npu_offload_b200.parallel import attach_peers, shard_map
+        from npu_offload_b200.parallel import attach_peers, shard_map, unit_ranges, unit_slice
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         torch.cuda.set_device(rank)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
-        counts = np.arange(E)[None, :][::-1].copy()
-        smap = shard_map(counts, world)
-        p = MoEDataPlane(H, F, E, K, n_layers=L, max_tokens=64, device=rank, ep_rank=rank, ep_world=world,
+        if mode == "units":  # this rank: its slice of the units of every expert
+            f0, f1 = unit_ranges(F, world)[rank]
+            smap = np.full((L, E), rank, np.int32)
+        else:
+            f0, f1 = 0, F
+            smap = shard_map(np.arange(E)[None, :][::-1].copy(), world)
+        p = MoEDataPlane(H, f1 - f0, E, K, n_layers=L, max_tokens=64, device=rank, ep_rank=rank, ep_world=world,
                          shard_map=smap)
         for e, (g, u, d) in enumerate(_weights(5)):
             if smap[0, e] == rank:
-                p.load_expert(0, e, torch.from_numpy(g.view(np.int16)).view(torch.bfloat16).cuda(),
-                              torch.from_numpy(u.view(np.int16)).view(torch.bfloat16).cuda(),
-                              torch.from_numpy(d.view(np.int16)).view(torch.bfloat16).cuda())
+                g, u, d = unit_slice(g, u, d, f0, f1)
+                p.load_expert(0, e, torch.from_numpy(np.ascontiguousarray(g).view(np.int16)).view(torch.bfloat16).cuda(),
+                              torch.from_numpy(np.ascontiguousarray(u).view(np.int16)).view(torch.bfloat16).cuda(),
+                              torch.from_numpy(np.ascontiguousarray(d).view(np.int16)).view(torch.bfloat16).cuda())
         attach_peers(p)
         res = {}
         for T in TS:
@@ -80,7 +86,10 @@ def _port():
     return p
 
 
-def test_peer_exchange_two_gpus_matches_single_rank():
+@pytest.mark.parametrize("mode", ["experts", "units"])
+def test_peer_exchange_two_gpus_matches_single_rank(mode):
+    """experts: each rank owns half of the experts (popularity stripe); units: each rank owns half of
+    the intermediate units of every expert."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import multiprocessing as mp
@@ -88,7 +97,7 @@ def test_peer_exchange_two_gpus_matches_single_rank():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in ps:
         p.start()
     got = dict(q.get(timeout=300) for _ in ps)
@@ -105,7 +114,7 @@ def test_peer_exchange_two_gpus_matches_single_rank():
         x, lg = _inputs(T, 100 + T)
         ref, _, _, st = Port.moe_layer(x, lg, ex, K)
         assert st == 0
-        assert_close(got[0][T], ref, what=f"ep2 peer exchange T={T}")
+        assert_close(got[0][T], ref, what=f"ep2 {mode} peer exchange T={T}")
     np.testing.assert_array_equal(got[0]["host_acc"], got[1]["host_acc"])
     x, lg = _inputs(3, 103)
     ref, _, _, _ = Port.moe_layer(x, lg, ex, K)
