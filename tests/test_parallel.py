@@ -115,3 +115,32 @@ def test_expert_parallel_partials_allreduce_to_the_full_layer_gloo():
     assert st == 0
     np.testing.assert_array_equal(res[0], res[1])  # every rank holds the same combined output
     assert_close(res[0], full, max_abs=1e-5, min_cos=0.9999999, what="ep2 gloo vs single rank")
+
+
+def test_unit_ranges_partition_every_expert():
+    from npu_offload_b200.parallel import unit_ranges
+    for F, world in ((1280, 8), (1280, 2), (1280, 4), (256, 2), (640, 3)):
+        r = unit_ranges(F, world)
+        assert r[0][0] == 0 and r[-1][1] == F and len(r) == world
+        assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+        sizes = [b - a for a, b in r]
+        assert all(s % 64 == 0 and s > 0 for s in sizes) and max(sizes) - min(sizes) <= 64
+    with pytest.raises(ValueError):
+        unit_ranges(1280, 32)  # 20 chunks of 64 units cannot feed 32 ranks
+
+
+def test_unit_sharding_partials_sum_to_the_expert():
+    """The ranks' partial outputs over their unit slices add up to the whole expert (restated cpu_moe)."""
+    from npu_offload_b200 import synth
+    from npu_offload_b200.parallel import unit_ranges, unit_slice
+    H, F, T = 256, 256, 3
+    g, u, d = synth.expert_weights(9, 0, 0, H, F)
+    x = synth.hidden(19, T, H)
+    w = np.array([0.7, 0.2, 1.0], np.float32)
+    full = Port.cpu_moe(x, [("bf16", np.concatenate([g, u], 0), d)], [np.arange(T)], [w])
+    parts = []
+    for f0, f1 in unit_ranges(F, 4):
+        gs, us, ds = unit_slice(g, u, d, f0, f1)
+        parts.append(Port.cpu_moe(x, [("bf16", np.concatenate([gs, us], 0), np.ascontiguousarray(ds))],
+                                  [np.arange(T)], [w]))
+    assert_close(np.sum(parts, axis=0), full, max_abs=1e-5, min_cos=0.9999999, what="unit shards")
