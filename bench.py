@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="configs[3] prefill measurement at N=1 (0 to skip)")
     ap.add_argument("--no-block", action="store_true", help="skip the moe_block_forward measurement")
+    ap.add_argument("--cold-slots", type=int, default=0,
+                    help="HBM slots per layer for the host-cold tier measurement (0: skip)")
     ap.add_argument("--ep-shard", choices=["units", "experts"], default="units",
                     help="N>1 split: every rank a slice of every expert's units, or whole experts per rank")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
@@ -431,6 +433,50 @@ def block_run(stack, steps, warmup, T=1):
             "gpu_launches_per_layer": (stack.plane.launch_count - l0) / (steps * L)}
 
 
+def cold_run(args, device, L=2, steps=256, warmup=32):
+    """HBM-hot / host-cold tier: `--cold-slots` HBM slots per layer, the other
+    experts in pinned host memory, batch-1 decode with Zipf routing through ExpertCache (swap on miss
+    plus the LFU-decay follow rule).  MoE-layer tokens/s over `steps` layer calls, wall clock (misses
+    synchronise), with the hit rate and the swaps."""
+    import torch
+    from npu_offload_b200 import synth
+    from npu_offload_b200.cache import ExpertCache
+    from npu_offload_b200.moe import MoEDataPlane
+    S = args.cold_slots
+    gen = torch.Generator(device=device)
+    host = []
+    for l in range(L):
+        row = []
+        for e in range(E):
+            gen.manual_seed(args.seed * 1_000_003 + 1009 * l + e)
+            buf = (torch.randn(3 * F * H, generator=gen, device=device) * 0.02).to(torch.bfloat16).cpu().pin_memory()
+            row.append((buf[:F * H].view(F, H), buf[F * H:2 * F * H].view(F, H), buf[2 * F * H:].view(H, F)))
+        host.append(row)
+    plane = MoEDataPlane(H, F, E, K, n_layers=L, max_tokens=16, device=device.index)
+    prior = popularity_counts(args.seed, L)
+    cache = ExpertCache(plane, host, S, prior=prior, swap_per_tok=1)
+    x = torch.from_numpy(np.stack([synth.hidden(700 + i, 1, H) for i in range(64)]).view(np.int16)).view(
+        torch.bfloat16).to(device)
+    lg = torch.from_numpy(np.stack([synth.logits(700 + i, 1, E, zipf=False) + synth.zipf_bias(args.seed + 31 * (i % L), E)
+                                    for i in range(64)]).astype(np.float32)).to(device)
+    out = torch.empty(1, H, dtype=torch.float32, device=device)
+    for i in range(warmup):
+        cache.forward(i % L, x[i % 64], lg[i % 64], out=out)
+    torch.cuda.synchronize(device)
+    st0 = dict(cache.stats)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        cache.forward(i % L, x[i % 64], lg[i % 64], out=out)
+    torch.cuda.synchronize(device)
+    dt = time.perf_counter() - t0
+    d = {k: cache.stats[k] - st0[k] for k in st0}
+    n = d["hits"] + d["misses"]
+    plane.close()
+    return {"workload": f"{L} layers x {E} experts, {S} HBM slots per layer, the rest in pinned host memory; "
+                        "batch 1, Zipf routing", "tokens_per_s": steps / dt, "us_per_layer": dt / steps * 1e6,
+            "hit_rate": d["hits"] / n if n else None, "swaps_per_layer": (d["swaps"] + d["follow_swaps"]) / steps}
+
+
 # ---------------------------------------------------------------- CPU baseline (reference / port)
 def cpu_threads():
     try:
@@ -589,6 +635,9 @@ def our_arm(args):
     block = None
     if ws == 1 and not args.no_block:
         block = block_run(stack, max(1, args.steps // 4), min(args.warmup, 3))
+    cold = None
+    if ws == 1 and args.cold_slots > 0:
+        cold = cold_run(args, device)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -627,7 +676,7 @@ def our_arm(args):
                            "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
                 "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep, "prefill": prefill,
-                "block": block}
+                "block": block, "cold": cold}
         print(json.dumps(line), flush=True)
     if ws > 1:
         barrier(ws)  # no rank frees its exchange buffer while a peer may still use it

@@ -115,6 +115,16 @@ MOE_API int moe_quantize_expert_q8(moe_ctx* ctx, int layer, int expert);
 /* Kind (MOE_KIND_*) of a stored expert, or -1 on bad arguments. */
 MOE_API int moe_expert_kind(moe_ctx* ctx, int layer, int expert);
 
+/* HBM-hot / host-cold expert tier (the reference's swap of a device table slot,
+ * track2_opt/solar_engine/src/experts_b.rs:162-186, driven by the LFU-decay `follow` of
+ * solar_hybrid/runtime.py:287-311).  With MOE_OPT_LAYER_SLOTS = S set before a layer's first load,
+ * that layer's HBM table holds S experts; a load takes a free slot, and moe_evict_expert frees one
+ * (the expert then reads as MOE_KIND_NONE and routing a token to it makes moe_forward report
+ * MOE_ESTATE).  Evicting or loading must not overlap a forward call of the same layer on the GPU:
+ * loads run on the legacy default stream; callers on other streams synchronise first.
+ * npu_offload_b200.cache.ExpertCache keeps the host copies and makes the choices. */
+MOE_API int moe_evict_expert(moe_ctx* ctx, int layer, int expert);
+
 /* Sigmoid-scoring correction bias for a layer ([E] fp32; e_score_correction_bias, host.rs:120). */
 MOE_API int moe_set_bias(moe_ctx* ctx, int layer, const float* bias, int flags);
 
@@ -230,6 +240,8 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *   MOE_OPT_PREFILL_TC          1 (default): the prefill gate/up and down GEMMs run on the library's
  *                               persistent tcgen05 kernels (SwiGLU fused, g / u / y kept in fp32);
  *                               0: cuBLAS grouped GEMMs with bf16 outputs and a SwiGLU kernel.
+ *   MOE_OPT_LAYER_SLOTS         HBM expert slots per layer for layers not yet loaded (0, the default:
+ *                               one per local expert); see moe_evict_expert.
  *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
  *                               globaltimer / cycle slots (0 start, 1 plan share loaded, 2 all stages
  *                               issued, 3 all segments done, 4 grid-wide arrival seen, 5 reduction
@@ -244,6 +256,7 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 #define MOE_OPT_STAGE_BYTES 6
 #define MOE_OPT_PREFILL_MIN_T 7
 #define MOE_OPT_PREFILL_TC 8
+#define MOE_OPT_LAYER_SLOTS 9
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
 /* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see

@@ -97,6 +97,10 @@ struct moe_ctx {
     std::vector<int32_t> owner;           // [L*E] owning rank
     std::vector<int32_t> slot;            // [L*E] local slot, -1 if remote
     std::vector<int32_t> n_local;         // [L]
+    std::vector<int32_t> res;             // [L*E] arena slot of a resident local expert, -1 if not resident
+    std::vector<int32_t> arena_slots;     // [L] slots of each layer's arena
+    int slot_budget = 0;                  // MOE_OPT_LAYER_SLOTS: slots per layer (0: every local expert)
+    void* d_down_stage = nullptr;         // [F*H] bf16: host down matrices on their way to the unit tables
     std::vector<void*> arena;             // [L] lazily allocated expert storage
     size_t stride = 0;                    // bytes per expert slot
     std::vector<ExpDesc> h_desc;          // [L*E]
@@ -240,7 +244,14 @@ int check_layer_expert(moe_ctx* c, int layer, int expert) {
 
 int ensure_arena(moe_ctx* c, int layer) {
     if (c->arena[layer]) return MOE_OK;
-    size_t bytes = c->stride * (size_t)std::max(1, c->n_local[layer]);
+    int n = std::max(1, c->n_local[layer]);
+    if (c->slot_budget > 0 && c->slot_budget < n) {  // fewer slots than experts: residency set at load
+        n = c->slot_budget;
+        const int E = c->cfg.n_experts;
+        for (int e = 0; e < E; e++) c->res[(size_t)layer * E + e] = -1;
+    }
+    c->arena_slots[layer] = n;
+    size_t bytes = c->stride * (size_t)n;
     if (cudaMalloc(&c->arena[layer], bytes) != cudaSuccess) {
         cudaGetLastError();
         return fail(MOE_ENOMEM, "expert table of layer %d (%zu bytes)", layer, bytes);
@@ -249,7 +260,24 @@ int ensure_arena(moe_ctx* c, int layer) {
 }
 
 char* slot_ptr(moe_ctx* c, int layer, int expert) {
-    return (char*)c->arena[layer] + c->stride * (size_t)c->slot[(size_t)layer * c->cfg.n_experts + expert];
+    return (char*)c->arena[layer] + c->stride * (size_t)c->res[(size_t)layer * c->cfg.n_experts + expert];
+}
+
+// Gives a local expert an arena slot for loading: its own if resident, else a free one.
+int acquire_slot(moe_ctx* c, int layer, int expert) {
+    const int E = c->cfg.n_experts;
+    int32_t* r = &c->res[(size_t)layer * E];
+    if (r[expert] >= 0) return MOE_OK;
+    std::vector<char> used(c->arena_slots[layer], 0);
+    for (int e = 0; e < E; e++)
+        if (r[e] >= 0) used[r[e]] = 1;
+    for (int s = 0; s < c->arena_slots[layer]; s++)
+        if (!used[s]) {
+            r[expert] = s;
+            return MOE_OK;
+        }
+    return fail(MOE_ESTATE, "layer %d: all %d expert slots are in use; evict an expert first", layer,
+                c->arena_slots[layer]);
 }
 
 int upload_desc(moe_ctx* c, int layer, int expert, const ExpDesc& d) {
@@ -269,24 +297,22 @@ size_t q8_scale_off(const moe_ctx* c) {
 // device buffer.
 int load_down_columns(moe_ctx* c, void* dst, const void* src, size_t pitch, int esize, bool host) {
     const size_t H = c->cfg.hidden, F = c->cfg.inter, bytes = F * H * esize;
-    void* tmp = nullptr;
-    if (host) {
-        if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(MOE_ENOMEM, "down-matrix staging (%zu bytes)", bytes);
+    if (host) {  // staged in a context buffer kept for later loads (expert swaps reload often)
+        if (!c->d_down_stage) {
+            if (cudaMalloc(&c->d_down_stage, F * H * 2) != cudaSuccess) {
+                cudaGetLastError();
+                c->d_down_stage = nullptr;
+                return fail(MOE_ENOMEM, "down-matrix staging (%zu bytes)", F * H * 2);
+            }
         }
-        cudaError_t e = cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, 0);
-        if (e != cudaSuccess) {
-            cudaFree(tmp);
-            return fail(MOE_ECUDA, "down-matrix copy: %s", cudaGetErrorString(e));
-        }
-        src = tmp;
+        cudaError_t e = cudaMemcpyAsync(c->d_down_stage, src, bytes, cudaMemcpyHostToDevice, 0);
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "down-matrix copy: %s", cudaGetErrorString(e));
+        src = c->d_down_stage;
     }
     int n = 0;
     cudaError_t e = launch_scatter_down(src, dst, pitch, (int)H, (int)F, esize, 0, &n);
     c->launches += n;
     if (e == cudaSuccess) e = cudaStreamSynchronize(0);
-    if (tmp) cudaFree(tmp);
     if (e != cudaSuccess) return fail(MOE_ECUDA, "down-matrix scatter: %s", cudaGetErrorString(e));
     return MOE_OK;
 }
@@ -451,7 +477,7 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         }
         // pageable source: the copy has completed when the call returns, so items may go out of scope
         CUDA_TRY(cudaMemcpyAsync(c->d_tc_items, items.data(), sizeof(TcItem) * items.size(), cudaMemcpyHostToDevice, st));
-        const int n_slots = std::max(1, c->n_local[layer]);
+        const int n_slots = c->arena_slots[layer];
         CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
         CUDA_TRY(launch_gateup_tc(c->d_pf_x, np, c->arena[layer], n_slots, c->stride, c->d_tc_items, n_gu, H, F, c->d_act,
                                   c->d_tc_sched, c->d_err, c->timeout_ns, c->sm_count, st));
@@ -620,6 +646,8 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
             c->owner[(size_t)l * E + e] = r;
             if (r == k.ep_rank) c->slot[(size_t)l * E + e] = c->n_local[l]++;
         }
+    c->res = c->slot;
+    c->arena_slots.assign(c->n_local.begin(), c->n_local.end());
     c->arena.assign(L, nullptr);
     c->stride = align_up((size_t)3 * k.inter * k.hidden * 2, 256);
     c->h_desc.assign((size_t)L * E, ExpDesc{nullptr, nullptr, nullptr, kKindNone, 0});
@@ -697,6 +725,7 @@ int moe_destroy(moe_ctx* c) {
     DeviceGuard dg(c->dev);
     cudaDeviceSynchronize();
     if (c->shared) moe_destroy(c->shared);
+    if (c->d_down_stage) cudaFree(c->d_down_stage);
     for (uint16_t* r : c->d_router) cudaFree(r);
     for (void* q : {(void*)c->d_blk_zero, (void*)c->d_blk_logits, (void*)c->d_blk_shared, (void*)c->d_blk_moe,
                     (void*)c->d_blk_y, (void*)c->d_blk_io, (void*)c->d_blk_extra})
@@ -733,6 +762,7 @@ int moe_load_expert_bf16(moe_ctx* c, int layer, int expert, const uint16_t* gate
     if (!gate || !up || !down) return fail(MOE_EINVAL, "null weight pointer");
     DeviceGuard dg(c->dev);
     if ((st = ensure_arena(c, layer))) return st;
+    if ((st = acquire_slot(c, layer, expert))) return st;
     const size_t H = c->cfg.hidden, F = c->cfg.inter, P = unit_pitch(kKindBF16, (int)H);
     char* base = slot_ptr(c, layer, expert);
     const bool host = flags & MOE_F_HOST;
@@ -750,6 +780,7 @@ int moe_load_expert_q8(moe_ctx* c, int layer, int expert, const int8_t* q, const
     if (!q || !scales) return fail(MOE_EINVAL, "null weight pointer");
     DeviceGuard dg(c->dev);
     if ((st = ensure_arena(c, layer))) return st;
+    if ((st = acquire_slot(c, layer, expert))) return st;
     const size_t H = c->cfg.hidden, F = c->cfg.inter, P = unit_pitch(kKindQ8, (int)H);
     char* base = slot_ptr(c, layer, expert);
     const bool host = flags & MOE_F_HOST;
@@ -791,6 +822,16 @@ int moe_quantize_expert_q8(moe_ctx* c, int layer, int expert) {
     if (e != cudaSuccess) return fail(MOE_ECUDA, "quantise: %s", cudaGetErrorString(e));
     return upload_desc(c, layer, expert,
                        ExpDesc{base, base + 2 * H, (const float*)(base + q8_scale_off(c)), kKindQ8, kLayoutUnit});
+}
+
+int moe_evict_expert(moe_ctx* c, int layer, int expert) {
+    int st = check_layer_expert(c, layer, expert);
+    if (st) return st;
+    const size_t i = (size_t)layer * c->cfg.n_experts + expert;
+    if (c->res[i] < 0) return MOE_OK;
+    DeviceGuard dg(c->dev);
+    c->res[i] = -1;  // the slot is free for the next load; routing to this expert now reports MOE_ESTATE
+    return upload_desc(c, layer, expert, ExpDesc{nullptr, nullptr, nullptr, kKindNone, 0});
 }
 
 int moe_expert_kind(moe_ctx* c, int layer, int expert) {
@@ -1507,6 +1548,11 @@ static int set_option_one(moe_ctx* c, int option, int64_t value) {
             return MOE_OK;
         case MOE_OPT_PREFILL_TC:
             c->prefill_tc = value != 0;
+            return MOE_OK;
+        case MOE_OPT_LAYER_SLOTS:
+            if (value < 0 || value > c->cfg.n_experts)
+                return fail(MOE_EINVAL, "layer slots %lld not in [0,%d]", (long long)value, c->cfg.n_experts);
+            c->slot_budget = (int)value;
             return MOE_OK;
         case MOE_OPT_STAGE_BYTES:
             if (value < 0 || value > 196608) return fail(MOE_EINVAL, "stage bytes %lld not in [0,196608]", (long long)value);

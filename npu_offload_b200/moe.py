@@ -145,6 +145,10 @@ class MoEDataPlane:
     def quantize_expert_q8(self, layer, expert):
         check(lib().moe_quantize_expert_q8(self._h, layer, expert))
 
+    def evict_expert(self, layer, expert):
+        """Frees the expert's HBM slot (MOE_OPT_LAYER_SLOTS tables); it reads as not loaded afterwards."""
+        check(lib().moe_evict_expert(self._h, layer, expert))
+
     def expert_kind(self, layer, expert):
         return lib().moe_expert_kind(self._h, layer, expert)
 
