@@ -148,9 +148,9 @@ struct moe_ctx {
     float* d_pf_yf = nullptr;           // [NP, H] down . act (tensor-core path, fp32)
     void** d_pf_ptr = nullptr;          // [9 * E] grouped-GEMM operand pointers
     bool prefill_tc = true;             // gate/up and down on the tcgen05 kernels; else cuBLAS
-    TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels
+    TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels (gate/up, then down)
+    int* d_tc_cnt = nullptr;            // [4] device-built counts: gate/up items, down items, local pairs
     uint32_t* d_tc_sched = nullptr;     // [4] tile-schedule counters (gate/up, down), left zero by each launch
-    int tc_items_cap = 0;
     // MoE-block calls (moe_load_shared, moe_shared_router, moe_block_forward)
     moe_ctx* shared = nullptr;          // one-expert context holding each layer's shared expert
     std::vector<uint16_t*> d_router;    // [L] router weights [E, H] bf16 (null until loaded)
@@ -423,6 +423,39 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
     const int H = c->cfg.hidden, F = c->cfg.inter, E = c->cfg.n_experts;
     const size_t NP = (size_t)c->cfg.max_tokens * c->cfg.top_k;
     int s;
+    const bool tc = c->prefill_tc && tc_available() && F % 128 == 0 && H % 256 == 0 && E <= kMaxExperts;
+    if (tc) {  // tile lists built on the device from the permutation's job list: no host round trip
+        for (int e = 0; e < E; e++)
+            if (c->h_desc[(size_t)layer * E + e].kind == kKindQ8) return MOE_OK;  // int8 tables: CUDA cores
+        const int mt_max = (int)(NP / 256) + E;  // 256-pair tiles: every job adds at most one partial tile
+        const int cap_gu = mt_max * (F / 128), cap_dn = mt_max * (H / 256);
+        if (!c->d_pf_x) {
+            int st2 = dalloc(&c->d_pf_x, NP * H);
+            if (!st2) st2 = dalloc(&c->d_pf_yf, NP * H);
+            if (!st2) st2 = dalloc(&c->d_tc_sched, 4);
+            if (!st2 && cudaMemset(c->d_tc_sched, 0, 4 * sizeof(uint32_t)) != cudaSuccess) st2 = fail(MOE_ECUDA, "memset");
+            if (st2) return st2;
+        }
+        if (!c->d_tc_items) {
+            int st2 = dalloc(&c->d_tc_items, (size_t)cap_gu + cap_dn);
+            if (!st2) st2 = dalloc(&c->d_tc_cnt, 4);
+            if (st2) return st2;
+        }
+        TcItem* items_dn = c->d_tc_items + cap_gu;
+        const int n_slots = c->arena_slots[layer];
+        CUDA_TRY(launch_tc_items(c->d_jobs, c->d_nlj, E, c->arena[layer], c->stride, F, H, c->d_tc_items, cap_gu, items_dn,
+                                 cap_dn, c->d_tc_cnt, c->d_err, st));
+        CUDA_TRY(launch_gather_rows(x, c->d_ptok, (int)NP, H, c->d_pf_x, c->sm_count, st, c->d_tc_cnt + 2));
+        CUDA_TRY(launch_gateup_tc(c->d_pf_x, (int)NP, c->arena[layer], n_slots, c->stride, c->d_tc_items, 0, c->d_tc_cnt,
+                                  H, F, c->d_act, c->d_tc_sched, c->d_err, c->timeout_ns, c->sm_count, st));
+        CUDA_TRY(launch_down_tc(c->d_act, (int)NP, c->arena[layer], n_slots, c->stride, items_dn, 0, c->d_tc_cnt + 1, H, F,
+                                c->d_pf_yf, c->d_tc_sched + 2, c->d_err, c->timeout_ns, c->sm_count, st));
+        CUDA_TRY(launch_combine_rows(c->d_pf_yf, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
+        c->launches += 5;
+        *done = true;
+        return MOE_OK;
+    }
+    // library path (MOE_OPT_PREFILL_TC = 0): operand pointer arrays built on the host from the job list
     if ((s = c->job_stage.reserve(sizeof(int32_t) + sizeof(Job) * E + 64))) return s;
     char* hp = (char*)c->job_stage.host;
     CUDA_TRY(cudaMemcpyAsync(hp, c->d_nlj, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
@@ -435,58 +468,19 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         if (j.ex.kind != kKindBF16 || j.ex.layout != kLayoutUnit) return MOE_OK;  // int8 experts: CUDA cores
         np = std::max(np, j.p0 + j.n);
     }
-    const bool tc = c->prefill_tc && tc_available() && F % 128 == 0 && H % 256 == 0;
-    if (!tc && !c->blas) {
+    if (!c->blas) {
         if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "cublasCreate failed");
     }
-    if (!c->d_pf_x) {
-        int st2 = dalloc(&c->d_pf_x, NP * H);
+    if (!c->d_pf_g) {
+        int st2 = c->d_pf_x ? MOE_OK : dalloc(&c->d_pf_x, NP * H);
         if (!st2) st2 = dalloc(&c->d_pf_g, NP * F);
         if (!st2) st2 = dalloc(&c->d_pf_u, NP * F);
         if (!st2) st2 = dalloc(&c->d_pf_y, NP * H);
-        if (!st2) st2 = dalloc(&c->d_pf_yf, NP * H);
         if (!st2) st2 = dalloc(&c->d_pf_ptr, (size_t)9 * E);
-        if (!st2) st2 = dalloc(&c->d_tc_sched, 4);
-        if (!st2 && cudaMemset(c->d_tc_sched, 0, 4 * sizeof(uint32_t)) != cudaSuccess) st2 = fail(MOE_ECUDA, "memset");
         if (st2) return st2;
     }
     int launches = 0;
-    if (nj > 0 && tc) {
-        // tile lists: gate/up tiles (TcItem.f0 = first f), then down tiles (TcItem.f0 = first output h)
-        // jobs with the most pairs first (their tiles carry both halves), so the schedule ends on light tiles
-        std::vector<int> order(nj);
-        for (int j = 0; j < nj; j++) order[j] = j;
-        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return jobs[a].n > jobs[b].n; });
-        std::vector<TcItem> items;
-        int n_gu = 0;
-        for (int pass = 0; pass < 2; pass++) {
-            for (int j : order) {
-                const long slot = ((const char*)jobs[j].ex.w1 - (const char*)c->arena[layer]) / (long)c->stride;
-                for (int m0 = 0; m0 < jobs[j].n; m0 += 256)
-                    for (int n0 = 0; n0 < (pass ? H : F); n0 += (pass ? 256 : 128))
-                        items.push_back(TcItem{jobs[j].p0 + m0, std::min(256, jobs[j].n - m0), (int)slot, n0});
-            }
-            if (!pass) n_gu = (int)items.size();
-        }
-        if ((int)items.size() > c->tc_items_cap) {
-            if (c->d_tc_items) cudaFree(c->d_tc_items);
-            c->d_tc_items = nullptr;
-            c->tc_items_cap = 0;
-            if ((s = dalloc(&c->d_tc_items, items.size()))) return s;
-            c->tc_items_cap = (int)items.size();
-        }
-        // pageable source: the copy has completed when the call returns, so items may go out of scope
-        CUDA_TRY(cudaMemcpyAsync(c->d_tc_items, items.data(), sizeof(TcItem) * items.size(), cudaMemcpyHostToDevice, st));
-        const int n_slots = c->arena_slots[layer];
-        CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
-        CUDA_TRY(launch_gateup_tc(c->d_pf_x, np, c->arena[layer], n_slots, c->stride, c->d_tc_items, n_gu, H, F, c->d_act,
-                                  c->d_tc_sched, c->d_err, c->timeout_ns, c->sm_count, st));
-        CUDA_TRY(launch_down_tc(c->d_act, np, c->arena[layer], n_slots, c->stride, c->d_tc_items + n_gu,
-                                (int)items.size() - n_gu, H, F, c->d_pf_yf, c->d_tc_sched + 2, c->d_err, c->timeout_ns,
-                                c->sm_count, st));
-        CUDA_TRY(launch_combine_rows(c->d_pf_yf, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
-        launches += 4;
-    } else {
+    {
         if (nj > 0) {
             CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
             launches++;
@@ -739,7 +733,7 @@ int moe_destroy(moe_ctx* c) {
     for (void* p : ps) cudaFree(p);
     if (c->blas) cublasDestroy(c->blas);
     for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_yf, (void*)c->d_pf_ptr, (void*)c->d_tc_sched,
-                    (void*)c->d_tc_items})
+                    (void*)c->d_tc_items, (void*)c->d_tc_cnt})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
     for (void* q : {(void*)c->d_xbuf, (void*)c->d_xflag, (void*)c->d_peer_x, (void*)c->d_peer_flag, (void*)c->d_xpart})

@@ -14,9 +14,11 @@
 
 namespace moe {
 
-// xg[p, :] = x[ptok[p], :] for the n pairs of the local jobs (job-major): 16-byte vectors.
-__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, const int32_t* ptok, int n, int H,
-                                                          uint16_t* xg) {
+// xg[p, :] = x[ptok[p], :] for the n pairs of the local jobs (job-major): 16-byte vectors.  n_dev
+// (nullable) holds n in device memory (job list built on the device).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, const int32_t* ptok, int n,
+                                                          const int* n_dev, int H, uint16_t* xg) {
+    if (n_dev) n = min(n, *n_dev);
     const int per = H / 8;
     const long total = (long)n * per;
     for (long i = blockIdx.x * 256L + threadIdx.x; i < total; i += (long)gridDim.x * 256) {
@@ -98,11 +100,11 @@ cudaError_t launch_combine_rows(const float* y, const float* w, const int32_t* c
 }
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* ptok, int n, int H, uint16_t* xg, int sm_count,
-                               cudaStream_t st) {
+                               cudaStream_t st, const int* n_dev) {
     if (n <= 0) return cudaSuccess;
     const long total = (long)n * (H / 8);
     const int grid = (int)std::min<long>((total + 255) / 256, (long)sm_count * 16);
-    gather_rows_kernel<<<grid, 256, 0, st>>>(x, ptok, n, H, xg);
+    gather_rows_kernel<<<grid, 256, 0, st>>>(x, ptok, n, n_dev, H, xg);
     return cudaGetLastError();
 }
 

@@ -141,8 +141,9 @@ __device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr) {
 template <bool DOWN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                   const TcItem* __restrict__ items, int n_items, int H, int F, void* __restrict__ out, uint32_t* sched,
-                   uint32_t* err, uint64_t timeout_ns) {
+                   const TcItem* __restrict__ items, int n_items, const int* __restrict__ n_items_dev, int H, int F,
+                   void* __restrict__ out, uint32_t* sched, uint32_t* err, uint64_t timeout_ns) {
+    if (n_items_dev) n_items = *n_items_dev;  // tile list built on the device (every CTA reads it)
     extern __shared__ __align__(1024) unsigned char tsm[];
     unsigned char* ring = reinterpret_cast<unsigned char*>(((uintptr_t)tsm + 1023) & ~(uintptr_t)1023);
     TcCtrl& c = *reinterpret_cast<TcCtrl*>(ring + (size_t)kTcStages * kTcStage);
@@ -338,6 +339,64 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
+// ---- tile lists from the permutation's job list, on the device (no host round trip) ----
+// Jobs heaviest first (stable), each job's 256-pair m-tiles in order, then the tile's n-blocks:
+// gate/up items (f0 = first of 128 f) into gu, down items (f0 = first of 256 h) into dn.
+// cnt[0] = gate/up items, cnt[1] = down items, cnt[2] = local pairs (rows of the gathered x).
+__global__ void __launch_bounds__(256) tc_items_kernel(const Job* __restrict__ jobs, const int* __restrict__ n_jobs, int E,
+                                                       const char* arena, size_t stride, int F, int H, TcItem* gu,
+                                                       int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err) {
+    __shared__ int n_s[kMaxExperts], order_s[kMaxExperts], off_s[kMaxExperts + 1];
+    __shared__ int np_s;
+    const int tid = threadIdx.x;
+    const int nj = min(max(*n_jobs, 0), E);
+    if (tid == 0) np_s = 0;
+    for (int j = tid; j < nj; j += blockDim.x) n_s[j] = jobs[j].n;
+    __syncthreads();
+    for (int j = tid; j < nj; j += blockDim.x) {
+        int r = 0;
+        for (int i = 0; i < nj; i++) r += n_s[i] > n_s[j] || (n_s[i] == n_s[j] && i < j);
+        order_s[r] = j;
+        atomicMax(&np_s, jobs[j].p0 + n_s[j]);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int r = 0; r < nj; r++) {
+            off_s[r] = acc;
+            acc += (n_s[order_s[r]] + 255) / 256;
+        }
+        off_s[nj] = acc;
+    }
+    __syncthreads();
+    const int nf = F / 128, nh = H / 256, mt = off_s[nj];
+    const bool fits = mt * nf <= cap_gu && mt * nh <= cap_dn;
+    if (fits)
+        for (int r = tid; r < nj; r += blockDim.x) {
+            const Job jb = jobs[order_s[r]];
+            const int slot = (int)(((const char*)jb.ex.w1 - arena) / (long)stride);
+            for (int t = 0; t * 256 < jb.n; t++) {
+                const int row0 = jb.p0 + t * 256, rows = min(256, jb.n - t * 256), m = off_s[r] + t;
+                for (int f = 0; f < nf; f++) gu[(size_t)m * nf + f] = TcItem{row0, rows, slot, f * 128};
+                for (int h = 0; h < nh; h++) dn[(size_t)m * nh + h] = TcItem{row0, rows, slot, h * 256};
+            }
+        }
+    if (tid == 0) {
+        if (!fits) atomicOr(err, kErrBadIndex);  // sized by the host for max_tokens: never expected
+        cnt[0] = fits ? mt * nf : 0;
+        cnt[1] = fits ? mt * nh : 0;
+        cnt[2] = np_s;
+    }
+}
+
+cudaError_t launch_tc_items(const Job* jobs, const int* n_jobs, int E, const void* arena, size_t stride, int F, int H,
+                            TcItem* gu, int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err, cudaStream_t st) {
+    if (E > kMaxExperts) return cudaErrorInvalidValue;
+    tc_items_kernel<<<1, 256, 0, st>>>(jobs, n_jobs, E, static_cast<const char*>(arena), stride, F, H, gu, cap_gu, dn,
+                                       cap_dn, cnt, err);
+    return cudaGetLastError();
+}
+
 // ---- host side ----
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -391,8 +450,8 @@ static bool encode_units(EncodeTiledFn enc, CUtensorMap* m, const void* arena, i
 }
 
 cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, int n_slots, size_t slot_bytes,
-                           const TcItem* items, int n_items, int H, int F, float* y, uint32_t* sched, uint32_t* err,
-                           uint64_t timeout_ns, int grid_max, cudaStream_t st) {
+                           const TcItem* items, int n_items, const int* n_items_dev, int H, int F, float* y,
+                           uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     if (H % 256 || F % kTcBK || slot_bytes % 16 || ((uintptr_t)act | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
@@ -400,15 +459,16 @@ cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, in
     // activation rows [arows][F]; down columns at element 2H of each unit, boxes of 64 outputs x 64 f
     if (!encode_rows(enc, &ma, act, F, arows) || !encode_units(enc, &md, arena, H, F, n_slots, slot_bytes, 64, kTcBK))
         return cudaErrorInvalidValue;
-    if (n_items <= 0) return cudaSuccess;
-    tc_gemm_kernel<true><<<std::min(n_items, grid_max), kTcThreads, kTcSmem, st>>>(ma, md, items, n_items, H, F, y, sched,
-                                                                                  err, timeout_ns);
+    if (!n_items_dev && n_items <= 0) return cudaSuccess;
+    const int grid = n_items_dev ? grid_max : std::min(n_items, grid_max);
+    tc_gemm_kernel<true><<<grid, kTcThreads, kTcSmem, st>>>(ma, md, items, n_items, n_items_dev, H, F, y, sched, err,
+                                                           timeout_ns);
     return cudaGetLastError();
 }
 
 cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, int n_slots, size_t slot_bytes,
-                             const TcItem* items, int n_items, int H, int F, uint16_t* act, uint32_t* sched,
-                             uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st) {
+                             const TcItem* items, int n_items, const int* n_items_dev, int H, int F, uint16_t* act,
+                             uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     if (H % kTcBK || F % 128 || slot_bytes % 16 || ((uintptr_t)xg | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
@@ -416,9 +476,10 @@ cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, i
     // gathered token rows [xrows][H]; gate row f at element 0 of unit f, up row at element H
     if (!encode_rows(enc, &mx, xg, H, xrows) || !encode_units(enc, &mw, arena, H, F, n_slots, slot_bytes, kTcBK, 128))
         return cudaErrorInvalidValue;
-    if (n_items <= 0) return cudaSuccess;
-    tc_gemm_kernel<false><<<std::min(n_items, grid_max), kTcThreads, kTcSmem, st>>>(mx, mw, items, n_items, H, F, act,
-                                                                                   sched, err, timeout_ns);
+    if (!n_items_dev && n_items <= 0) return cudaSuccess;
+    const int grid = n_items_dev ? grid_max : std::min(n_items, grid_max);
+    tc_gemm_kernel<false><<<grid, kTcThreads, kTcSmem, st>>>(mx, mw, items, n_items, n_items_dev, H, F, act, sched, err,
+                                                            timeout_ns);
     return cudaGetLastError();
 }
 
