@@ -111,6 +111,7 @@ struct moe_ctx {
     int32_t *d_idx = nullptr, *d_counts = nullptr, *d_offsets = nullptr, *d_perm = nullptr, *d_jobord = nullptr;
     int32_t *d_nj = nullptr, *d_nlj = nullptr, *d_ptok = nullptr, *d_pairpos = nullptr, *d_comb_off = nullptr;
     int32_t* d_comb_p = nullptr;
+    int32_t* d_route_scratch = nullptr;  // permutation scratch (route_scratch_ints(max_tokens, E))
     float *d_w = nullptr, *d_pw = nullptr;
     Job* d_jobs = nullptr;
     uint16_t* d_act = nullptr;
@@ -651,6 +652,7 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     const size_t NP = (size_t)k.max_tokens * k.top_k;
     int st = MOE_OK;
     if (!st) st = dalloc(&c->d_desc, (size_t)L * E);
+    if (!st) st = dalloc(&c->d_route_scratch, route_scratch_ints(k.max_tokens, E));
     if (!st) st = dalloc(&c->d_bias, (size_t)L * E);
     if (!st) st = dalloc(&c->d_idx, NP);
     if (!st) st = dalloc(&c->d_w, NP);
@@ -729,7 +731,7 @@ int moe_destroy(moe_ctx* c) {
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
                   c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
                   c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
-                  c->d_plan_flag, c->d_part};
+                  c->d_plan_flag, c->d_part, c->d_route_scratch};
     for (void* p : ps) cudaFree(p);
     if (c->blas) cublasDestroy(c->blas);
     for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_yf, (void*)c->d_pf_ptr, (void*)c->d_tc_sched,
@@ -871,6 +873,7 @@ static RouteArgs route_args(moe_ctx* c, int T, const float* logits, const float*
     a.jobs = c->d_jobs;
     a.n_ljobs = c->d_nlj;
     a.err = c->d_err;
+    a.scratch = c->d_route_scratch;
     return a;
 }
 

@@ -85,10 +85,18 @@ __device__ __forceinline__ void permute_count_tile(const RouteArgs& a, PermShare
 // Placement pass over one tile: grouped position = expert offset + tile base + rank in the tile
 // (tokens ascending, cpu_moe's per-expert token lists); the token's combine list is its positions
 // ordered by job rank (the order the reference accumulates, cpu_moe.cpp:81-93), pairs owned by
-// another rank marked -1.
-template <int KM>
-__device__ __forceinline__ void permute_place_tile(const RouteArgs& a, const PermShared& ps, uint32_t* wmask,
-                                                   const uint16_t* tcnt, const unsigned char* idx8, int tile) {
+// another rank marked -1.  idx: the 8-bit copy (shared) or the router's int32 output (global, an
+// out-of-range id read as 0 as in the count pass); tb: the tile's bases [E].
+__device__ __forceinline__ int perm_id(const unsigned char* idx, size_t q, int) { return idx[q]; }
+__device__ __forceinline__ int perm_id(const int32_t* idx, size_t q, int E) {
+    const int e = idx[q];
+    return e < 0 || e >= E ? 0 : e;
+}
+
+template <int KM, typename IX, typename TB>
+__device__ __forceinline__ void permute_place_tile(const RouteArgs& a, const int* offs, const int* jrank,
+                                                   const unsigned char* remote, uint32_t* wmask, const TB* tb,
+                                                   const IX* idx, int tile) {
     const int lane = threadIdx.x & 31, K = a.K, E = a.E;
     const int t = tile * 32 + lane;
     const bool on = t < a.T;
@@ -97,7 +105,7 @@ __device__ __forceinline__ void permute_place_tile(const RouteArgs& a, const Per
     float wk[KM];
 #pragma unroll
     for (int k = 0; k < KM; k++) {
-        ek[k] = (on && k < K) ? idx8[t * K + k] : 0;
+        ek[k] = (on && k < K) ? perm_id(idx, (size_t)t * K + k, E) : 0;
         wk[k] = (on && k < K && a.pw) ? a.w[(size_t)t * K + k] : 0.f;
     }
 #pragma unroll
@@ -111,14 +119,14 @@ __device__ __forceinline__ void permute_place_tile(const RouteArgs& a, const Per
         pp[k] = -1;
         if (on && k < K) {
             const int e = ek[k];
-            const int pos = ps.offs[e] + tcnt[tile * E + e] + __popc(wmask[e] & lt);
+            const int pos = offs[e] + (int)tb[e] + __popc(wmask[e] & lt);
             const int q = t * K + k;
             if (a.perm) a.perm[pos] = q;
             if (a.ptok) a.ptok[pos] = t;
             if (a.pw) a.pw[pos] = wk[k];
             if (a.pairpos) a.pairpos[q] = pos;
-            rk[k] = ps.jrank[e];
-            pp[k] = ps.remote[e] ? -1 : pos;
+            rk[k] = jrank[e];
+            pp[k] = remote[e] ? -1 : pos;
         }
     }
     __syncwarp();
@@ -144,7 +152,13 @@ __device__ __forceinline__ void permute_place_tile(const RouteArgs& a, const Per
     }
 }
 
-__device__ void permute_block(const RouteArgs& a, unsigned char* dyn) {
+// Permutation scratch in global memory (RouteArgs::scratch, route_scratch_ints) between the counting
+// block and the many-CTA placement: tile bases [ceil(T/32)][E], then offsets [E], job ranks [E],
+// remote flags [E].
+
+// place = false: the placement is left to permute_place_kernel (many CTAs: a single SM's scattered
+// stores of every pair were the bottleneck); the block publishes what it needs in a.scratch.
+__device__ void permute_block(const RouteArgs& a, unsigned char* dyn, bool place) {
     __shared__ PermShared ps;
     const int E = a.E, K = a.K, T = a.T;
     const int tid = threadIdx.x, nth = blockDim.x;
@@ -249,18 +263,56 @@ __device__ void permute_block(const RouteArgs& a, unsigned char* dyn) {
         }
     }
     if (tid == 0 && a.offsets) a.offsets[E] = ps.offs[E];
+    if (!place) {
+        int32_t* tb = a.scratch;
+        int32_t* meta = a.scratch + (size_t)ntiles * E;
+        for (int i = tid; i < ntiles * E; i += nth) tb[i] = tcnt[i];
+        for (int e = tid; e < E; e += nth) {
+            meta[e] = ps.offs[e];
+            meta[E + e] = ps.jrank[e];
+            meta[2 * E + e] = ps.remote[e];
+        }
+        return;
+    }
     for (int tile = warp; tile < ntiles; tile += nwarps) {
         if (K <= 8)
-            permute_place_tile<8>(a, ps, wmask, tcnt, idx8, tile);
+            permute_place_tile<8>(a, ps.offs, ps.jrank, ps.remote, wmask, tcnt + (size_t)tile * E, idx8, tile);
         else
-            permute_place_tile<kMaxTopK>(a, ps, wmask, tcnt, idx8, tile);
+            permute_place_tile<kMaxTopK>(a, ps.offs, ps.jrank, ps.remote, wmask, tcnt + (size_t)tile * E, idx8, tile);
     }
     if (a.comb_p && tid == 0) a.comb_off[T] = T * K;
 }
 
+// Placement over many CTAs (a warp per 32-token tile) from the counting block's scratch.
+constexpr int kPlaceWarps = 8;
+__global__ void __launch_bounds__(kPlaceWarps * 32) permute_place_kernel(RouteArgs a) {
+    __shared__ uint32_t wm[kPlaceWarps][kMaxExperts];
+    __shared__ int offs[kMaxExperts], jrank[kMaxExperts];
+    __shared__ unsigned char remote[kMaxExperts];
+    const int E = a.E, K = a.K, T = a.T, ntiles = (T + 31) / 32;
+    const int warp = threadIdx.x >> 5;
+    const int32_t* meta = a.scratch + (size_t)ntiles * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        offs[e] = meta[e];
+        jrank[e] = meta[E + e];
+        remote[e] = (unsigned char)meta[2 * E + e];
+    }
+    for (int i = threadIdx.x; i < kPlaceWarps * kMaxExperts; i += blockDim.x) (&wm[0][0])[i] = 0;
+    __syncthreads();
+    const int tile = blockIdx.x * kPlaceWarps + warp;
+    if (tile < ntiles) {
+        const int32_t* tb = a.scratch + (size_t)tile * E;
+        if (K <= 8)
+            permute_place_tile<8>(a, offs, jrank, remote, wm[warp], tb, a.idx, tile);
+        else
+            permute_place_tile<kMaxTopK>(a, offs, jrank, remote, wm[warp], tb, a.idx, tile);
+    }
+    if (a.comb_p && blockIdx.x == 0 && threadIdx.x == 0) a.comb_off[T] = T * K;
+}
+
 __global__ void __launch_bounds__(1024) permute_kernel(RouteArgs a) {
     extern __shared__ __align__(16) unsigned char pdyn[];
-    permute_block(a, pdyn);
+    permute_block(a, pdyn, a.scratch == nullptr);
 }
 
 // Small batches: routing and permutation in one launch.
@@ -270,7 +322,7 @@ __global__ void __launch_bounds__(1024) route_fused_kernel(RouteArgs a) {
     const int warp = threadIdx.x >> 5;
     for (int t = warp; t < a.T; t += 32) route_token_warp(a, t, scr + warp * 2 * kMaxExperts);
     __syncthreads();
-    permute_block(a, dyn + 32 * 2 * kMaxExperts * sizeof(float));
+    permute_block(a, dyn + 32 * 2 * kMaxExperts * sizeof(float), true);
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
@@ -284,6 +336,10 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
     size_t sm = permute_smem_bytes(a.T, a.K, a.E);
     permute_kernel<<<1, 1024, sm, st>>>(a);
     if (launches) *launches += a.T > 0 ? 2 : 1;
+    if (a.scratch && a.T > 0) {
+        permute_place_kernel<<<((a.T + 31) / 32 + kPlaceWarps - 1) / kPlaceWarps, kPlaceWarps * 32, 0, st>>>(a);
+        if (launches) *launches += 1;
+    }
     return cudaGetLastError();
 }
 

@@ -24,7 +24,12 @@ struct RouteArgs {
     int32_t* n_ljobs;     // [1] out, optional
     const ExpDesc* desc;  // [E] expert table of the layer, or null
     uint32_t* err;        // latched error bits
+    int32_t* scratch;     // optional [permute_scratch_ints(T, E)]: batches above 64 tokens then place
+                          // their pairs over many CTAs (null: one block does everything)
 };
+
+// Ints of RouteArgs::scratch for T tokens and E experts.
+constexpr size_t route_scratch_ints(int T, int E) { return (size_t)(T + 31) / 32 * E + 3 * (size_t)E; }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches);
 cudaError_t route_set_smem_limits();
