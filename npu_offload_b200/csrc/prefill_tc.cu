@@ -360,13 +360,22 @@ __global__ void __launch_bounds__(256) tc_items_kernel(const Job* __restrict__ j
         atomicMax(&np_s, jobs[j].p0 + n_s[j]);
     }
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0;
-        for (int r = 0; r < nj; r++) {
+    if (tid < 32) {  // exclusive scan of the m-tile counts in job order: one warp, 8 jobs per lane
+        const int per = (nj + 31) / 32, r0 = tid * per;
+        int sum = 0;
+        for (int r = r0; r < r0 + per && r < nj; r++) sum += (n_s[order_s[r]] + 255) / 256;
+        int inc = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (tid >= o) inc += y;
+        }
+        int acc = inc - sum;
+        for (int r = r0; r < r0 + per && r < nj; r++) {
             off_s[r] = acc;
             acc += (n_s[order_s[r]] + 255) / 256;
         }
-        off_s[nj] = acc;
+        if (tid == 31) off_s[nj] = inc;
     }
     __syncthreads();
     const int nf = F / 128, nh = H / 256, mt = off_s[nj];
