@@ -379,7 +379,8 @@ def prefill_run(stack, T, reps=5, warmup=2):
 
 
 def block_run(stack, steps, warmup, T=1):
-    """The whole MoE block around the path: router GEMV producing the logits,
+    """The whole MoE block around the path (the steps either side of the routed experts, layer.rs:1-6):
+    router GEMV producing the logits,
     routed experts, the shared expert and the residual combine into the next layer's input
     (moe_block_forward), per layer of the stack, device-resident inputs, CUDA events."""
     import torch
@@ -434,7 +435,7 @@ def block_run(stack, steps, warmup, T=1):
 
 
 def cold_run(args, device, L=2, steps=256, warmup=32):
-    """HBM-hot / host-cold tier: `--cold-slots` HBM slots per layer, the other
+    """HBM-hot / host-cold tier (solar_hybrid/runtime.py:287-311): `--cold-slots` HBM slots per layer, the other
     experts in pinned host memory, batch-1 decode with Zipf routing through ExpertCache (swap on miss
     plus the LFU-decay follow rule).  MoE-layer tokens/s over `steps` layer calls, wall clock (misses
     synchronise), with the hit rate and the swaps."""

@@ -172,8 +172,9 @@ MOE_API int moe_place_expert_q8(moe_ctx* ctx, const uint16_t* g, const uint16_t*
 /* ---- The steps either side of the routed experts in one Solar MoE block
  * (track2_opt/solar_engine/src/layer.rs:1-6: combine -> attention -> shared expert + router). ----
  *
- * moe_load_shared: layer `layer`'s shared expert (gate [F*H], up [F*H] rows, down [H*F] row-major,
- * the routed experts' layout) and router weights Wr [E*H] row-major, bf16.  Either part may be NULL
+ * moe_load_shared: layer `layer`'s shared expert (gate [Fs*H], up [Fs*H] rows, down [H*Fs] row-major,
+ * the routed experts' layout; Fs = MOE_OPT_SHARED_INTER, by default the context's F) and router
+ * weights Wr [E*H] row-major, bf16.  Either part may be NULL
  * (then left as loaded before).  Copied; host pointers with MOE_F_HOST.  Replaces the host-side
  * placement of dense/shared.rs's WG / WD / WR tables (shared.rs:5-31).
  *
@@ -216,6 +217,13 @@ MOE_API int moe_block_forward(moe_ctx* ctx, int layer, int T, const uint16_t* h2
 MOE_API int moe_ep_export(moe_ctx* ctx, void* buf, int cap);
 MOE_API int moe_ep_import(moe_ctx* ctx, const void* records, int world);
 
+/* The router's exponential, y[i] = exp(x[i]) rounded once to fp32 (correctly rounded), on the
+ * calling thread's current device, asynchronously on `stream`; x and y are device pointers.  It is
+ * the exp of the softmax numerators (host.rs.tpl:249, `(v - m).exp()`) and of the sigmoid
+ * denominators (track2_opt/solar_engine/src/host.rs:121) as every router kernel evaluates it,
+ * exported so a caller (and the tests) can compare it with a host libm over the whole domain. */
+MOE_API int moe_router_exp(const float* x, float* y, int64_t n, void* stream);
+
 /* Synchronise `stream`, then return (and clear) the latched device-side status. */
 MOE_API int moe_status(moe_ctx* ctx, void* stream);
 
@@ -237,9 +245,9 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 128) run the expert
  *                               FFN as grouped tensor-core GEMMs when every routed local expert is
  *                               bf16; 0 keeps every batch on the CUDA-core paths.
- *   MOE_OPT_PREFILL_TC          1 (default): the prefill gate/up and down GEMMs run on the library's
- *                               persistent tcgen05 kernels (SwiGLU fused, g / u / y kept in fp32);
- *                               0: cuBLAS grouped GEMMs with bf16 outputs and a SwiGLU kernel.
+ *   MOE_OPT_PREFILL_TC          1 (default): prefill batches run the gate/up and down GEMMs on the
+ *                               library's persistent tcgen05 kernels (SwiGLU fused, g / u / y kept in
+ *                               fp32); 0: they stay on the CUDA-core multi-kernel path.
  *   MOE_OPT_LAYER_SLOTS         HBM expert slots per layer for layers not yet loaded (0, the default:
  *                               one per local expert); see moe_evict_expert.
  *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
@@ -247,7 +255,11 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               issued, 3 all segments done, 4 grid-wide arrival seen, 5 reduction
  *                               done; for consumer warp 0, SM cycles (8) waiting for ring stages,
  *                               (9) working on them, (10) of which in the cross-warp exchange) and
- *                               CTA 0's per-stage stamps; read them with moe_timeline_read. */
+ *                               CTA 0's per-stage stamps; read them with moe_timeline_read.
+ *   MOE_OPT_SHARED_INTER        intermediate size of the shared expert (moe_load_shared), set before its
+ *                               first load; 0 (the default) = the context's inter.  A context holding a
+ *                               slice of every routed expert's units (inter = the slice) still loads the
+ *                               whole shared expert: set this to its full width. */
 #define MOE_OPT_FUSED_DECODE 1
 #define MOE_OPT_WAIT_TIMEOUT_US 2
 #define MOE_OPT_INJECT_WAIT_TIMEOUT 3
@@ -257,6 +269,7 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 #define MOE_OPT_PREFILL_MIN_T 7
 #define MOE_OPT_PREFILL_TC 8
 #define MOE_OPT_LAYER_SLOTS 9
+#define MOE_OPT_SHARED_INTER 10
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
 /* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see

@@ -74,7 +74,7 @@ def build(force=False, verbose=False, extra=(), out=None):
     failed = [obj for obj, p in jobs if p.wait() != 0]
     if failed:
         raise subprocess.CalledProcessError(1, "nvcc " + " ".join(failed))
-    link = [NVCC, *ARCH, "-shared", "-o", lib + ".tmp", *[obj for obj, _ in jobs], "-lcudart", "-lcublas"]
+    link = [NVCC, *ARCH, "-shared", "-o", lib + ".tmp", *[obj for obj, _ in jobs], "-lcudart"]
     subprocess.check_call(link)
     os.replace(lib + ".tmp", lib)
     return lib

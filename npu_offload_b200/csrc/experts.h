@@ -30,13 +30,9 @@ struct ExpertArgs {
 // y[p, :] (times comb_w[p] when set).
 cudaError_t launch_combine(const ExpertArgs& a, cudaStream_t st, int* launches);
 
-// Prefill helpers (prefill.cu): token-row gather and the SwiGLU epilogue between the grouped GEMMs.
+// Prefill helpers (prefill.cu): token-row gather before the grouped GEMMs, weighted combine after.
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* ptok, int n, int H, uint16_t* xg, int sm_count,
                                cudaStream_t st, const int* n_dev = nullptr);
-cudaError_t launch_swiglu_rows(const uint16_t* g, const uint16_t* u, long count, uint16_t* act, int sm_count,
-                               cudaStream_t st);
-cudaError_t launch_combine_bf16(const uint16_t* y, const float* w, const int32_t* comb_off, const int32_t* comb_p,
-                                int T, int H, int accumulate, float* out, cudaStream_t st);
 cudaError_t launch_combine_rows(const float* y, const float* w, const int32_t* comb_off, const int32_t* comb_p, int T,
                                 int H, int accumulate, float* out, cudaStream_t st);
 

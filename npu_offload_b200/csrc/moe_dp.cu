@@ -1,5 +1,4 @@
 // libmoe_dp: context, expert tables and the C ABI declared in include/moe_dp.h.
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -138,22 +137,18 @@ struct moe_ctx {
     std::vector<void*> ipc_opened;      // peer mappings to close
     bool ep_attached = false;
     uint32_t xepoch = 0;
-    // prefill: grouped GEMMs on the tensor cores (cuBLAS) between our gather / SwiGLU / combine
+    // prefill: grouped GEMMs on the tcgen05 tensor cores between the gather and the combine
     bool prefill = true;
     int prefill_min_t = 128;            // smallest batch that takes the prefill path
-    cublasHandle_t blas = nullptr;
     uint16_t* d_pf_x = nullptr;         // [NP, H] gathered token rows (job-major pairs)
-    uint16_t* d_pf_g = nullptr;         // [NP, F] gate . x (bf16 GEMM output)
-    uint16_t* d_pf_u = nullptr;         // [NP, F] up . x
-    uint16_t* d_pf_y = nullptr;         // [NP, H] down . act (library path, bf16)
-    float* d_pf_yf = nullptr;           // [NP, H] down . act (tensor-core path, fp32)
-    void** d_pf_ptr = nullptr;          // [9 * E] grouped-GEMM operand pointers
-    bool prefill_tc = true;             // gate/up and down on the tcgen05 kernels; else cuBLAS
+    float* d_pf_yf = nullptr;           // [NP, H] down . act (fp32)
+    bool prefill_tc = true;             // prefill batches on the tcgen05 kernels; else the CUDA-core path
     TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels (gate/up, then down)
     int* d_tc_cnt = nullptr;            // [4] device-built counts: gate/up items, down items, local pairs
     uint32_t* d_tc_sched = nullptr;     // [4] tile-schedule counters (gate/up, down), left zero by each launch
     // MoE-block calls (moe_load_shared, moe_shared_router, moe_block_forward)
     moe_ctx* shared = nullptr;          // one-expert context holding each layer's shared expert
+    int shared_inter = 0;               // its intermediate size (MOE_OPT_SHARED_INTER; 0 = cfg.inter)
     std::vector<uint16_t*> d_router;    // [L] router weights [E, H] bf16 (null until loaded)
     float* d_blk_zero = nullptr;        // [max_tokens] zero logits: the shared context routes with weight 1
     float* d_blk_logits = nullptr;      // [max_tokens, E]
@@ -411,19 +406,16 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
 }
 
 // Prefill: after the router has grouped the pairs (d_jobs, d_ptok, d_pw, combine lists), the expert
-// FFN runs as two grouped GEMMs over the context's unit tables, read in place.
-// Tensor-core path (tcgen05 kernels, fp32 accumulation, g / u / y kept in fp32 like the decode paths):
+// FFN runs as two grouped GEMMs on the tcgen05 tensor cores over the context's unit tables, read in
+// place (fp32 accumulation; g, u and y kept in fp32 like the decode paths):
 //   gate/up  tiles of 256 pairs x 128 f: act = SwiGLU(gate . x, up . x) fused in the epilogue
 //   down     tiles of 256 pairs x 256 h: y = down . act, the down columns as an MN-major operand
-// Library path (cuBLAS grouped GEMM, column-major view, bf16 outputs):
-//   gate/up  C^T[F x n] = W^T(op T) . X^T   A = gate (or up) rows, lda = unit pitch 3H; B = gathered x
-//   down     Y^T[H x n] = W2 . act^T        A = the down columns, which are W2 column-major (lda 3H)
-// Sets *done when it ran (every local job bf16); the caller runs the CUDA-core path otherwise.
+// Sets *done when it ran (every local job bf16, shape supported); the caller runs the CUDA-core path
+// otherwise.
 int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int accumulate, cudaStream_t st, bool* done) {
     *done = false;
     const int H = c->cfg.hidden, F = c->cfg.inter, E = c->cfg.n_experts;
     const size_t NP = (size_t)c->cfg.max_tokens * c->cfg.top_k;
-    int s;
     const bool tc = c->prefill_tc && tc_available() && F % 128 == 0 && H % 256 == 0 && E <= kMaxExperts;
     if (tc) {  // tile lists built on the device from the permutation's job list: no host round trip
         for (int e = 0; e < E; e++)
@@ -456,90 +448,7 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         *done = true;
         return MOE_OK;
     }
-    // library path (MOE_OPT_PREFILL_TC = 0): operand pointer arrays built on the host from the job list
-    if ((s = c->job_stage.reserve(sizeof(int32_t) + sizeof(Job) * E + 64))) return s;
-    char* hp = (char*)c->job_stage.host;
-    CUDA_TRY(cudaMemcpyAsync(hp, c->d_nlj, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
-    CUDA_TRY(cudaMemcpyAsync(hp + 16, c->d_jobs, sizeof(Job) * E, cudaMemcpyDeviceToHost, st));
-    CUDA_TRY(cudaStreamSynchronize(st));
-    const int nj = std::min(*(int32_t*)hp, E);
-    std::vector<Job> jobs((Job*)(hp + 16), (Job*)(hp + 16) + nj);
-    int np = 0;
-    for (const Job& j : jobs) {
-        if (j.ex.kind != kKindBF16 || j.ex.layout != kLayoutUnit) return MOE_OK;  // int8 experts: CUDA cores
-        np = std::max(np, j.p0 + j.n);
-    }
-    if (!c->blas) {
-        if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "cublasCreate failed");
-    }
-    if (!c->d_pf_g) {
-        int st2 = c->d_pf_x ? MOE_OK : dalloc(&c->d_pf_x, NP * H);
-        if (!st2) st2 = dalloc(&c->d_pf_g, NP * F);
-        if (!st2) st2 = dalloc(&c->d_pf_u, NP * F);
-        if (!st2) st2 = dalloc(&c->d_pf_y, NP * H);
-        if (!st2) st2 = dalloc(&c->d_pf_ptr, (size_t)9 * E);
-        if (st2) return st2;
-    }
-    int launches = 0;
-    {
-        if (nj > 0) {
-            CUDA_TRY(launch_gather_rows(x, c->d_ptok, np, H, c->d_pf_x, c->sm_count, st));
-            launches++;
-            // problem arrays: [gate_0..gate_nj-1, up_0..up_nj-1] then [down_0..down_nj-1]
-            const int P1 = 2 * nj;
-            std::vector<cublasOperation_t> ta(P1, CUBLAS_OP_T), tb(P1, CUBLAS_OP_N), ta2(nj, CUBLAS_OP_N), tb2(nj, CUBLAS_OP_N);
-            std::vector<int> m1(P1, F), n1(P1), k1(P1, H), lda1(P1, 3 * H), ldb1(P1, H), ldc1(P1, F), gs1(P1, 1);
-            std::vector<int> m2(nj, H), n2(nj), k2(nj, F), lda2(nj, 3 * H), ldb2(nj, F), ldc2(nj, H), gs2(nj, 1);
-            std::vector<float> one1(P1, 1.f), zero1(P1, 0.f), one2(nj, 1.f), zero2(nj, 0.f);
-            std::vector<void*> ptr((size_t)9 * E, nullptr);
-            void** A1 = ptr.data();
-            void** B1 = A1 + P1;
-            void** C1 = B1 + P1;
-            void** A2 = C1 + P1;
-            void** B2 = A2 + nj;
-            void** C2 = B2 + nj;
-            for (int j = 0; j < nj; j++) {
-                const uint16_t* w = static_cast<const uint16_t*>(jobs[j].ex.w1);
-                const int p0 = jobs[j].p0, n = jobs[j].n;
-                n1[j] = n1[nj + j] = n2[j] = n;
-                A1[j] = (void*)w;                      // gate rows
-                A1[nj + j] = (void*)(w + H);           // up rows
-                B1[j] = B1[nj + j] = c->d_pf_x + (size_t)p0 * H;
-                C1[j] = c->d_pf_g + (size_t)p0 * F;
-                C1[nj + j] = c->d_pf_u + (size_t)p0 * F;
-                A2[j] = (void*)(w + 2 * (size_t)H);    // down columns = W2 column-major
-                B2[j] = c->d_act + (size_t)p0 * F;
-                C2[j] = c->d_pf_y + (size_t)p0 * H;
-            }
-            void** dA1 = c->d_pf_ptr;
-            void** dB1 = dA1 + P1;
-            void** dC1 = dB1 + P1;
-            void** dA2 = dC1 + P1;
-            void** dB2 = dA2 + nj;
-            void** dC2 = dB2 + nj;
-            CUDA_TRY(cudaMemcpyAsync(c->d_pf_ptr, ptr.data(), sizeof(void*) * (3 * P1 + 3 * nj), cudaMemcpyHostToDevice, st));
-            CUDA_TRY(cudaStreamSynchronize(st));  // the host arrays above are read at launch
-            cublasSetStream(c->blas, st);
-            cublasStatus_t bs =
-                cublasGemmGroupedBatchedEx(c->blas, ta.data(), tb.data(), m1.data(), n1.data(), k1.data(), one1.data(),
-                                           (const void* const*)dA1, CUDA_R_16BF, lda1.data(), (const void* const*)dB1,
-                                           CUDA_R_16BF, ldb1.data(), zero1.data(), dC1, CUDA_R_16BF, ldc1.data(), P1,
-                                           gs1.data(), CUBLAS_COMPUTE_32F);
-            if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped gate/up GEMM: cuBLAS status %d", (int)bs);
-            CUDA_TRY(launch_swiglu_rows(c->d_pf_g, c->d_pf_u, (long)np * F, c->d_act, c->sm_count, st));
-            launches++;
-            bs = cublasGemmGroupedBatchedEx(c->blas, ta2.data(), tb2.data(), m2.data(), n2.data(), k2.data(), one2.data(),
-                                            (const void* const*)dA2, CUDA_R_16BF, lda2.data(), (const void* const*)dB2,
-                                            CUDA_R_16BF, ldb2.data(), zero2.data(), dC2, CUDA_R_16BF, ldc2.data(), nj,
-                                            gs2.data(), CUBLAS_COMPUTE_32F);
-            if (bs != CUBLAS_STATUS_SUCCESS) return fail(MOE_ECUDA, "grouped down GEMM: cuBLAS status %d", (int)bs);
-        }
-        CUDA_TRY(launch_combine_bf16(c->d_pf_y, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
-        launches++;
-    }
-    c->launches += launches;
-    *done = true;
-    return MOE_OK;
+    return MOE_OK;  // tcgen05 kernels unavailable for this shape: the CUDA-core path runs
 }
 
 // Host buffers on the fused path.  Pinned host memory is device-accessible under unified addressing,
@@ -733,8 +642,7 @@ int moe_destroy(moe_ctx* c) {
                   c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
                   c->d_plan_flag, c->d_part, c->d_route_scratch};
     for (void* p : ps) cudaFree(p);
-    if (c->blas) cublasDestroy(c->blas);
-    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_g, (void*)c->d_pf_u, (void*)c->d_pf_y, (void*)c->d_pf_yf, (void*)c->d_pf_ptr, (void*)c->d_tc_sched,
+    for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_yf, (void*)c->d_tc_sched,
                     (void*)c->d_tc_items, (void*)c->d_tc_cnt})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
@@ -1330,6 +1238,7 @@ int moe_ep_import(moe_ctx* c, const void* blobs, int world) {
 static int ensure_shared(moe_ctx* c) {
     if (c->shared) return MOE_OK;
     moe_config k = c->cfg;
+    if (c->shared_inter > 0) k.inter = c->shared_inter;  // a unit-sharded context still holds the whole shared expert
     k.n_experts = 1;  // softmax over one zero logit: weight exactly 1 for every token
     k.top_k = 1;
     k.scoring = MOE_SCORING_SOFTMAX;
@@ -1476,7 +1385,8 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
     size_t dsmem = 0;
     // fused: the shared expert is one more job of the routed unit stream, and the decode kernel's
     // reduction writes y and x_next (one plan, one decode grid)
-    const bool fused = c->cfg.ep_world == 1 && !c->prof_on && T * (K + 1) <= kDecodeMaxPairs &&
+    const bool fused = c->cfg.ep_world == 1 && !c->prof_on && c->shared->cfg.inter == c->cfg.inter &&
+                       T * (K + 1) <= kDecodeMaxPairs &&
                        c->sm_count - 1 + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
     if (fused) {
         da.x = dh;
@@ -1503,6 +1413,17 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
     return (host || (flags & MOE_F_SYNC)) ? block_sync(c, s) : MOE_OK;
 }
 
+int moe_router_exp(const float* x, float* y, int64_t n, void* stream) {
+    if (n < 0) return fail(MOE_EINVAL, "negative n");
+    if (n == 0) return MOE_OK;
+    if (!x || !y) return fail(MOE_EINVAL, "null x / y");
+    int dev = 0, sms = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CUDA_TRY(launch_router_exp(x, y, (long long)n, sms, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
 int moe_status(moe_ctx* c, void* stream) {
     if (!c) return fail(MOE_EINVAL, "null context");
     DeviceGuard dg(c->dev);
@@ -1517,7 +1438,8 @@ int moe_set_option(moe_ctx* c, int option, int64_t value) {
     if (!c) return fail(MOE_EINVAL, "null context");
     const int st = set_option_one(c, option, value);
     // the shared-expert context follows the path options (not the test hook, not instrumentation)
-    if (st == MOE_OK && c->shared && option != MOE_OPT_INJECT_WAIT_TIMEOUT && option != MOE_OPT_TIMELINE)
+    if (st == MOE_OK && c->shared && option != MOE_OPT_INJECT_WAIT_TIMEOUT && option != MOE_OPT_TIMELINE &&
+        option != MOE_OPT_SHARED_INTER)
         return set_option_one(c->shared, option, value);
     return st;
 }
@@ -1551,6 +1473,14 @@ static int set_option_one(moe_ctx* c, int option, int64_t value) {
                 return fail(MOE_EINVAL, "layer slots %lld not in [0,%d]", (long long)value, c->cfg.n_experts);
             c->slot_budget = (int)value;
             return MOE_OK;
+        case MOE_OPT_SHARED_INTER: {
+            const int64_t v = value ? value : c->cfg.inter;
+            if (v < 64 || v % 64 || v > 2048) return fail(MOE_EINVAL, "shared inter %lld must be a multiple of 64 in [64, 2048]", (long long)v);
+            if (c->shared && c->shared->cfg.inter != v)
+                return fail(MOE_ESTATE, "the shared expert is already loaded with inter %d", c->shared->cfg.inter);
+            c->shared_inter = (int)v;
+            return MOE_OK;
+        }
         case MOE_OPT_STAGE_BYTES:
             if (value < 0 || value > 196608) return fail(MOE_EINVAL, "stage bytes %lld not in [0,196608]", (long long)value);
             c->stage_target = (uint32_t)value;

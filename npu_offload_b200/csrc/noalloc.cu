@@ -38,7 +38,9 @@ constexpr int kMaxDevices = 64;
 // The call's working memory: job table, pair lists, SwiGLU activations and per-expert outputs.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// Per device: the array's device address and the SM count (looked up once, with that device current).
 void* g_scratch_addr[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
 // Scratch layout inside g_noalloc_scratch (offsets in bytes, each 256-aligned).
@@ -91,7 +93,8 @@ __global__ void noalloc_setup_kernel(NoAllocTable t, const float* w, unsigned ch
     }
 }
 
-int scratch_address(void** out) {
+// The calling thread's current device, the scratch array's address on it and its SM count.
+int scratch_address(void** out, int* sms) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
@@ -101,14 +104,22 @@ int scratch_address(void** out) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (!g_scratch_addr[dev]) {
         void* p = nullptr;
+        int n = 0;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
             cudaGetLastError();
             return internal_fail(MOE_ECUDA, "moe_ck_moe3_noalloc: cudaGetSymbolAddress of the scratch array failed");
         }
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            return internal_fail(MOE_ECUDA, "moe_ck_moe3_noalloc: SM count query failed");
+        }
+        g_sm_count[dev] = n;
         g_scratch_addr[dev] = p;
     }
     *out = g_scratch_addr[dev];
+    *sms = g_sm_count[dev];
     return MOE_OK;
 }
 
@@ -138,11 +149,14 @@ extern "C" int moe_ck_moe3_noalloc(int E, const uint16_t* const* base, const flo
         t.base[e] = base[e];
     }
     void* sp = nullptr;
-    int st = scratch_address(&sp);
+    int sms = 0;
+    int st = scratch_address(&sp, &sms);
     if (st != MOE_OK) return st;
     unsigned char* s = static_cast<unsigned char*>(sp);
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     noalloc_setup_kernel<<<1, 32, 0, cs>>>(t, w, s, L);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return internal_fail(MOE_ECUDA, cudaGetErrorString(e));
     ExpertArgs a{};
     a.x = x;
     a.T = 1;
@@ -162,11 +176,8 @@ extern "C" int moe_ck_moe3_noalloc(int E, const uint16_t* const* base, const flo
     a.out = out;
     a.accumulate = 1;
     a.err = nullptr;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     int launches = 0;
-    cudaError_t e = launch_experts(a, sms, cs, &launches, nullptr);
+    e = launch_experts(a, sms, cs, &launches, nullptr);
     if (e != cudaSuccess) return internal_fail(MOE_ECUDA, cudaGetErrorString(e));
     return MOE_OK;
 }

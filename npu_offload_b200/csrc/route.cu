@@ -3,6 +3,8 @@
 //
 // Permutation semantics: solar_hybrid/runtime.py:343-354 -- pairs (t, k) grouped per expert with
 // tokens ascending; experts listed in first-appearance order of the t-major, k-minor scan.
+#include <algorithm>
+
 #include "common.cuh"
 #include "route.h"
 #include "route_core.cuh"
@@ -340,6 +342,19 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches) {
         permute_place_kernel<<<((a.T + 31) / 32 + kPlaceWarps - 1) / kPlaceWarps, kPlaceWarps * 32, 0, st>>>(a);
         if (launches) *launches += 1;
     }
+    return cudaGetLastError();
+}
+
+// The router's exponential over an array (tests compare it with the CPU oracle over every float of
+// the domain the softmax sees).
+__global__ void __launch_bounds__(256) router_exp_kernel(const float* x, float* y, long long n) {
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256) y[i] = router_exp(x[i]);
+}
+
+cudaError_t launch_router_exp(const float* x, float* y, long long n, int sms, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const long long blocks = std::min<long long>((n + 255) / 256, (long long)sms * 8);
+    router_exp_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, y, n);
     return cudaGetLastError();
 }
 

@@ -33,5 +33,7 @@ constexpr size_t route_scratch_ints(int T, int E) { return (size_t)(T + 31) / 32
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, int* launches);
 cudaError_t route_set_smem_limits();
+// y[i] = router_exp(x[i]) for i < n (device pointers).
+cudaError_t launch_router_exp(const float* x, float* y, long long n, int sms, cudaStream_t st);
 
 }  // namespace moe

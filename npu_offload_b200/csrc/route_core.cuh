@@ -6,8 +6,12 @@
 //   softmax: m = max v; e_i = exp(v_i - m); z = sum_i e_i in index order; p_i = e_i / z;
 //            top-k by p, ties -> lower index; w_k = p_k / sum_k p_k in k order (no epsilon)
 //   sigmoid: s_i = 1 / (1 + exp(-v_i)); key_i = s_i + bias_i; top-k by key; w_k = s_k / (sum s + 1e-20)
-// exp is evaluated in double and rounded once (a correctly rounded expf), so the fp32 probabilities
-// -- and the top-k order including rounding ties -- match a host with a correctly rounded expf.
+// exp is evaluated in double and rounded once (router_exp: a correctly rounded expf), so the fp32
+// probabilities -- and the top-k order including rounding ties -- are those of a correctly rounded
+// expf.  The reference's f32::exp goes to the platform libm, which need not be correctly rounded
+// (glibc 2.39's expf differs from it by one ulp on 97,052 of the 1,120,927,745 floats in [-104, 0]);
+// the CPU oracle uses the same correctly rounded evaluation, and a test compares the two over every
+// float of that domain.
 // Both sums run sequentially in the reference's order: every lane performs the same chain of fp32
 // additions on values read back (broadcast) from the warp's shared scratch, so all lanes agree.
 // Top-k is a rank count over 64-bit composite keys (ordered fp32 bits, then the complemented index),
@@ -16,6 +20,10 @@
 #include "common.cuh"
 
 namespace moe {
+
+// The router's exponential: exp in double, rounded once to fp32 (host.rs.tpl:249 softmax numerator,
+// host.rs:121 sigmoid denominator).
+__device__ __forceinline__ float router_exp(float x) { return (float)exp((double)x); }
 
 // Order-preserving map of a float to uint32 (NaN excluded by the caller).
 __device__ __forceinline__ uint32_t ordered_bits(float f) {
@@ -51,7 +59,7 @@ __device__ __forceinline__ bool route_keys_s(const float* v, const float* bias, 
 #pragma unroll
         for (int s = 0; s < S; s++) {
             const int i = lane + 32 * s;
-            val[s] = i < E ? (float)exp((double)(key[s] - m)) : 0.f;
+            val[s] = i < E ? router_exp(key[s] - m) : 0.f;
             if (i < E) scr[i] = val[s];
         }
         __syncwarp();
@@ -81,7 +89,7 @@ __device__ __forceinline__ bool route_keys_s(const float* v, const float* bias, 
             key[s] = -INFINITY;
             val[s] = 0.f;
             if (i < E) {
-                const float sg = __fdiv_rn(1.0f, 1.0f + (float)exp(-(double)v[i]));
+                const float sg = __fdiv_rn(1.0f, 1.0f + router_exp(-v[i]));
                 const float k = sg + (bias ? bias[i] : 0.f);
                 key[s] = k;
                 val[s] = sg;

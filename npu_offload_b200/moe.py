@@ -181,13 +181,20 @@ class MoEDataPlane:
 
     # ---- the steps either side of the routed experts (one Solar MoE block, solar_engine/src/layer.rs:1-6) ----
     def load_shared(self, layer, gate=None, up=None, down=None, router=None):
-        """Shared expert gate/up [F,H], down [H,F] and router weights [E,H] (bf16) of one layer."""
+        """Shared expert gate/up [Fs,H], down [H,Fs] and router weights [E,H] (bf16) of one layer.
+        Fs may differ from the routed F (a context holding a slice of every routed expert's units
+        still holds the whole shared expert); it is fixed by the first load."""
+        from ._lib import MOE_OPT_SHARED_INTER
         ws = [None if a is None else as_bf16(a) for a in (gate, up, down, router)]
         on_dev = [w.is_cuda for w in ws if w is not None]
         dev = bool(on_dev) and on_dev[0]
         ws = [None if w is None else (w.to(self.device) if dev else w.cpu()) for w in ws]
         if ws[0] is not None:
-            assert ws[0].shape == (self.F, self.H) and ws[1].shape == (self.F, self.H) and ws[2].shape == (self.H, self.F)
+            fs = ws[0].shape[0]
+            assert ws[0].shape == (fs, self.H) and ws[1].shape == (fs, self.H) and ws[2].shape == (self.H, fs)
+            if getattr(self, "_shared_inter", None) != fs:
+                self.set_option(MOE_OPT_SHARED_INTER, fs)
+                self._shared_inter = fs
         if ws[3] is not None:
             assert ws[3].shape == (self.E, self.H)
         check(lib().moe_load_shared(self._h, layer, *[_vp(w) for w in ws], 0 if dev else MOE_F_HOST))
@@ -366,7 +373,55 @@ def _cpu(t):
 
 # ---------------- cpu_moe_ext drop-in ----------------
 _planes = {}
-_wcache = {}
+
+
+class _WeightCache:
+    """Device copies of CPU weight tensors for gpu_moe, keyed on the tensor object itself.
+
+    An entry holds a weak reference to the host tensor and the tensor's version counter
+    (``Tensor._version``, bumped by every in-place write), so a tensor that is freed (its storage
+    possibly reused at the same address) or overwritten in place (the reference's expert swap,
+    runtime.py:287-311) is copied again instead of returning stale weights.  Entries die with their
+    host tensor, and the cache keeps at most ``limit_bytes`` of device copies, evicting the least
+    recently used first.
+    """
+
+    def __init__(self, limit_bytes):
+        import collections
+        self.limit = int(limit_bytes)
+        self.bytes = 0
+        self.entries = collections.OrderedDict()  # id(t) -> (weakref, version, device, copy)
+
+    def _drop(self, key):
+        e = self.entries.pop(key, None)
+        if e is not None:
+            self.bytes -= e[3].numel() * e[3].element_size()
+
+    def get(self, t, device):
+        import weakref
+        key = id(t)
+        e = self.entries.get(key)
+        if e is not None and e[0]() is t and e[1] == t._version and e[2] == device:
+            self.entries.move_to_end(key)
+            return e[3]
+        self._drop(key)
+        d = as_bf16(t, device)
+        nb = d.numel() * d.element_size()
+        while self.entries and self.bytes + nb > self.limit:
+            self._drop(next(iter(self.entries)))
+        if nb <= self.limit:
+            ref = weakref.ref(t, lambda _r, k=key, c=self: c._drop(k) if k in c.entries and c.entries[k][0] is _r else None)
+            self.entries[key] = (ref, t._version, device, d)
+            self.bytes += nb
+        return d
+
+    def clear(self):
+        self.entries.clear()
+        self.bytes = 0
+
+
+# device copies of CPU weights: 8 GiB by default (NPU_OFFLOAD_GPU_MOE_CACHE_GB overrides)
+_wcache = _WeightCache(float(__import__("os").environ.get("NPU_OFFLOAD_GPU_MOE_CACHE_GB", "8")) * (1 << 30))
 
 
 def _plane_for(device, H, F, pairs, T, n_jobs):
@@ -392,12 +447,7 @@ def _plane_for(device, H, F, pairs, T, n_jobs):
 def _device_weight(t, device):
     if t.is_cuda:
         return as_bf16(t)
-    key = (t.data_ptr(), t.numel(), str(device))
-    d = _wcache.get(key)
-    if d is None:
-        d = as_bf16(t, device)
-        _wcache[key] = d
-    return d
+    return _wcache.get(t, device)
 
 
 def gpu_moe(x, gus, ds, toks, ws):
@@ -406,7 +456,8 @@ def gpu_moe(x, gus, ds, toks, ws):
     x [T,H] bf16; gus[e] [2F,H] bf16 (gate rows then up rows); ds[e] [H,F] bf16; toks[e] int64 token
     rows; ws[e] fp32 routing weights.  Returns out [T,H] fp32 = sum_e ws[e] * expert_e(x[toks[e]]),
     on x's device (a CPU x gives a CPU result, as the reference does).  CPU weight tensors are copied
-    to the GPU once and cached by storage address; pass CUDA tensors to avoid the cache.
+    to the GPU and cached per tensor object and version (a bounded cache: see _WeightCache); pass
+    CUDA tensors to avoid the cache.
     """
     T, H = x.shape
     E = len(gus)

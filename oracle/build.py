@@ -19,7 +19,8 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("NPU_OFFLOAD_REF", "/root/reference")
+# The reference tree: $NPU_OFFLOAD_REF, else a directory named "reference" beside this repository.
+REF_ROOT = os.environ.get("NPU_OFFLOAD_REF") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 REF_DIR = os.path.join(HERE, "_ref")
 ORACLE_SO = os.path.join(HERE, "libmoe_oracle.so")
 CPU_KERN_SO = os.path.join(REF_DIR, "libcpu_kern.so")

@@ -60,6 +60,64 @@ int or_max_threads(void) {
 #endif
 }
 
+/* The routers' exponential: exp evaluated in double and rounded once to fp32, i.e. a correctly
+ * rounded expf.  The reference calls f32::exp (host.rs.tpl:249, host.rs:121), which goes to the
+ * platform libm; glibc 2.39's expf is not correctly rounded -- it is one ulp off on 97,052 of the
+ * 1,120,927,745 floats in [-104, 0], the domain of the softmax's exp(v - max).  The GPU routers and
+ * this oracle both use the correctly rounded value (tests compare them over that whole domain), so
+ * top-k ties and weights agree bit for bit between them. */
+static inline float router_exp(float x) { return (float)exp((double)x); }
+
+/* router_exp over n consecutive float bit patterns starting at first_bits (test support). */
+void or_router_exp_range(uint32_t first_bits, int64_t n, float* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        const uint32_t b = first_bits + (uint32_t)i;
+        float x;
+        memcpy(&x, &b, 4);
+        out[i] = router_exp(x);
+    }
+}
+
+/* Count of floats among bit patterns first_bits, first_bits + stride, ... (n of them) where router_exp
+ * differs from the long-double exp rounded to fp32 (a correctly-rounded check; test support). */
+int64_t or_router_exp_vs_long_double(uint32_t first_bits, int64_t n, int32_t stride) {
+    int64_t bad = 0;
+#pragma omp parallel for schedule(static) reduction(+ : bad)
+    for (int64_t i = 0; i < n; i++) {
+        const uint32_t b = first_bits + (uint32_t)(i * stride);
+        float x;
+        memcpy(&x, &b, 4);
+        const float a = (float)expl((long double)x), c = router_exp(x);
+        if (memcmp(&a, &c, 4) != 0) bad++;
+    }
+    return bad;
+}
+
+/* Count of floats (bit patterns first_bits .. first_bits + n - 1) where the host libm's expf differs
+ * from router_exp, and the largest difference in ulps (test support). */
+int64_t or_libm_expf_mismatches(uint32_t first_bits, int64_t n, int32_t* max_ulp) {
+    int64_t bad = 0;
+    int32_t worst = 0;
+#pragma omp parallel for schedule(static) reduction(+ : bad) reduction(max : worst)
+    for (int64_t i = 0; i < n; i++) {
+        const uint32_t b = first_bits + (uint32_t)i;
+        float x;
+        memcpy(&x, &b, 4);
+        const float a = expf(x), c = router_exp(x);
+        int32_t ua, uc;
+        memcpy(&ua, &a, 4);
+        memcpy(&uc, &c, 4);
+        if (ua != uc) {
+            bad++;
+            const int32_t d = ua > uc ? ua - uc : uc - ua;
+            if (d > worst) worst = d;
+        }
+    }
+    if (max_ulp) *max_ulp = worst;
+    return bad;
+}
+
 /* Top-k selection shared by both scoring modes: repeatedly take the largest key, ties to the lower
  * index.  Equivalent to the first k entries of the reference's stable descending sort
  * (npu-kernels/npu_kernels/rngd/layer_template/src/host.rs.tpl:256-260; Rust sort_by is stable, so
@@ -80,7 +138,7 @@ static void topk_desc(const float* key, int E, int K, int32_t* out) {
 
 /*
  * Softmax router, npu-kernels/npu_kernels/rngd/layer_template/src/host.rs.tpl:247-268:
- *   m = max(logits); e_i = expf(v_i - m); z = sum_i e_i (sequential, index order); p_i = e_i / z;
+ *   m = max(logits); e_i = exp(v_i - m) (router_exp); z = sum_i e_i (sequential, index order); p_i = e_i / z;
  *   order p descending, ties -> lower index; take K; w_k = p_k / sum_k p_k (sequential, no epsilon).
  * Returns OR_ENONFINITE where the reference would panic (a NaN reaching partial_cmp().unwrap()).
  */
@@ -94,7 +152,7 @@ int or_route_softmax(int T, int E, int K, const float* logits, int32_t* idx, flo
         for (int i = 0; i < E; i++) m = (v[i] > m || m != m) ? v[i] : m; /* f32::max fold */
         float z = 0.f;
         for (int i = 0; i < E; i++) {
-            p[i] = expf(v[i] - m);
+            p[i] = router_exp(v[i] - m);
             z += p[i];
         }
         int bad = 0;
@@ -116,7 +174,7 @@ int or_route_softmax(int T, int E, int K, const float* logits, int32_t* idx, flo
 /*
  * Sigmoid + correction-bias router, track2_opt/solar_engine/src/host.rs:119-128 (also the template's
  * non-softmax branch, host.rs.tpl:254-265):
- *   s_i = 1/(1+expf(-v_i)); key_i = s_i + bias_i; top K by key (ties -> lower index);
+ *   s_i = 1/(1+exp(-v_i)) (router_exp); key_i = s_i + bias_i; top K by key (ties -> lower index);
  *   w_k = s_k / (sum_k s_k + 1e-20).   bias may be NULL (all zero).
  */
 int or_route_sigmoid(int T, int E, int K, const float* logits, const float* bias, int32_t* idx, float* w) {
@@ -127,7 +185,7 @@ int or_route_sigmoid(int T, int E, int K, const float* logits, const float* bias
         const float* v = logits + (size_t)t * E;
         int bad = 0;
         for (int i = 0; i < E; i++) {
-            s[i] = 1.0f / (1.0f + expf(-v[i]));
+            s[i] = 1.0f / (1.0f + router_exp(-v[i]));
             key[i] = s[i] + (bias ? bias[i] : 0.0f);
             if (key[i] != key[i]) bad = 1;
         }

@@ -80,6 +80,12 @@ class Port:
             lib.or_shared_expert.restype = None
             lib.or_combine_residual.argtypes = [ctypes.c_long, _c_u16p, ctypes.c_void_p, _c_f32p, _c_u16p]
             lib.or_combine_residual.restype = None
+            lib.or_router_exp_range.argtypes = [ctypes.c_uint32, ctypes.c_int64, _c_f32p]
+            lib.or_router_exp_range.restype = None
+            lib.or_router_exp_vs_long_double.argtypes = [ctypes.c_uint32, ctypes.c_int64, ctypes.c_int32]
+            lib.or_router_exp_vs_long_double.restype = ctypes.c_int64
+            lib.or_libm_expf_mismatches.argtypes = [ctypes.c_uint32, ctypes.c_int64, _c_i32p]
+            lib.or_libm_expf_mismatches.restype = ctypes.c_int64
             lib.or_set_threads.argtypes = [ctypes.c_int]
             lib.or_set_threads.restype = None
             lib.or_max_threads.restype = ctypes.c_int
@@ -89,6 +95,24 @@ class Port:
     @classmethod
     def set_threads(cls, n):
         cls.lib().or_set_threads(int(n))
+
+    @classmethod
+    def router_exp_range(cls, first_bits, n):
+        """The routers' exp (double exp rounded once) of the n floats whose bit patterns follow first_bits."""
+        out = np.empty(int(n), np.float32)
+        cls.lib().or_router_exp_range(int(first_bits), int(n), _p(out, _c_f32p))
+        return out
+
+    @classmethod
+    def router_exp_vs_long_double(cls, first_bits, n, stride):
+        return int(cls.lib().or_router_exp_vs_long_double(int(first_bits), int(n), int(stride)))
+
+    @classmethod
+    def libm_expf_mismatches(cls, first_bits, n):
+        """(count, max ulp) of floats in the range where the host libm's expf differs from the routers' exp."""
+        worst = np.zeros(1, np.int32)
+        bad = cls.lib().or_libm_expf_mismatches(int(first_bits), int(n), _p(worst, _c_i32p))
+        return int(bad), int(worst[0])
 
     @classmethod
     def route_softmax(cls, logits, K):

@@ -31,7 +31,8 @@ from npu_offload_b200 import synth  # noqa: E402
 from oracle.oracle import Port, Reference  # noqa: E402
 
 OUT = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("NPU_OFFLOAD_REF", "/root/reference")
+# The reference tree: $NPU_OFFLOAD_REF, else a directory named "reference" beside this repository.
+REF_ROOT = os.environ.get("NPU_OFFLOAD_REF") or os.path.join(os.path.dirname(ROOT), "reference")
 
 
 def sha(*arrs):

@@ -240,3 +240,61 @@ def test_mixed_bf16_int8_layer(solar):
         np.testing.assert_array_equal(gi.cpu().numpy(), idx)
         assert any(e in cold for e in idx.ravel()), "case must route to an int8 expert"
         assert_close(out.cpu().numpy(), ref, what=f"mixed layer vs {kind}")
+
+
+@pytest.mark.parametrize("seed", [2, 5])
+def test_configs4_int8_cold_experts_t1_matches_reference(solar, seed):
+    """configs[4] exactly: a Solar-shaped layer whose 96 least popular experts (by the Zipf rank of the
+    routing bias) are stored int8 weight-only, quantised on the GPU with the reference's quant_row
+    rule, and the top 32 stay bf16; decode batch 1, top-8 Zipf routing.  The routed int8 experts'
+    tables must equal the reference's ck_place_expert_q8 tables (cpu_kern.c:227-241) bit for bit;
+    the layer output is checked against the reference itself: ck_moe_q8w (cpu_kern.c:306-333) for
+    the int8 jobs plus cpu_moe (cpu_moe.cpp:38-96) for the bf16 jobs (the C restatement where this
+    host cannot run the reference).  The seeds route at least one token pair to an int8 expert."""
+    from npu_offload_b200.moe import MoEDataPlane
+    _, W = solar
+    order = synth.popularity_order(seed, E)
+    cold = set(order[32:].tolist())
+    x = synth.hidden(seed, 1, H)
+    lg = synth.logits(seed, 1, E)
+    with MoEDataPlane(H, F, E, K, max_tokens=1) as p:
+        for e in range(E):
+            p.load_expert(0, e, *W[e])
+            if e in cold:
+                p.quantize_expert_q8(0, e)
+        assert sum(p.expert_kind(0, e) == 2 for e in range(E)) == 96
+        out, gi, gw = p.forward(0, torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda(),
+                                torch.from_numpy(lg).cuda(), return_topk=True, sync=True)
+        idx, w, st = Port.route_softmax(lg, K)
+        assert st == 0
+        np.testing.assert_array_equal(gi.cpu().numpy(), idx)
+        ids, ws = idx[0].tolist(), w[0].tolist()
+        assert any(e in cold for e in ids) and any(e not in cold for e in ids)
+        use_ref = Reference.available()
+        hot_gu, hot_d, hot_w, qs, scs, q_w = [], [], [], [], [], []
+        for e, we in zip(ids, ws):
+            gate, up, down = bf16_np(W[e][0]), bf16_np(W[e][1]), bf16_np(W[e][2])
+            if e in cold:
+                q, sc, _ = (Reference if use_ref else Port).place_expert_q8(gate, up, down)
+                gq, gsc, _ = p.place_expert_q8(W[e][0], W[e][1], W[e][2])
+                np.testing.assert_array_equal(gq.cpu().numpy(), q)
+                np.testing.assert_array_equal(gsc.cpu().numpy(), sc)
+                qs.append(q)
+                scs.append(sc)
+                q_w.append(we)
+            else:
+                hot_gu.append(np.concatenate([gate, up], 0))
+                hot_d.append(down)
+                hot_w.append(we)
+        if use_ref:
+            ref = Reference.cpu_moe(x, hot_gu, hot_d, [np.zeros(1, np.int64)] * len(hot_gu),
+                                    [np.array([v], np.float32) for v in hot_w]).copy()
+            Reference.ck_moe_q8w(qs, scs, np.array(q_w, np.float32), x[0], ref[0])
+            kind = "reference cpu_moe + ck_moe_q8w"
+        else:
+            jobs = [("bf16", a, b) for a, b in zip(hot_gu, hot_d)] + [("q8", a, b) for a, b in zip(qs, scs)]
+            ref = Port.cpu_moe(x, jobs, [[0]] * len(jobs), [[v] for v in hot_w + q_w])
+            kind = "oracle restatement"
+        d, c = assert_close(out.cpu().numpy(), ref, what=f"configs[4] seed {seed} vs {kind}")
+        print(f"configs[4] seed {seed}: {len(qs)} int8 + {len(hot_w)} bf16 experts vs {kind}: "
+              f"max-abs {d:.3g}, cosine {c:.8f}")

@@ -1,5 +1,6 @@
 """Router + permutation on the GPU, through the C ABI, against the oracle: bit-exact indices,
-permutation and job order (SURVEY parity bar), weights within 1e-6 relative."""
+permutation and job order (the north-star parity bar), weights within 1e-6 relative; the routers'
+exp bit-exact against the oracle's over every float of its domain."""
 import json
 import os
 
@@ -124,3 +125,35 @@ def test_route_empty_batch(planes):
     p = planes(128, 8)
     r = p.route(np.zeros((0, 128), np.float32))
     assert r["status"] == 0 and int(r["n_jobs"][0]) == 0 and r["counts"].sum() == 0
+
+
+def test_router_exp_matches_oracle_over_the_whole_domain():
+    """Every float x in [-104, 0] (the softmax's exp(v - max)) and in [0, 88.72] (the sigmoid's
+    exp(-v)): the GPU routers' exp (moe_router_exp, the device function every router kernel calls)
+    gives the same fp32 bits as the oracle's.  Outside that range both give 0 / +inf."""
+    import ctypes
+    import torch
+    from npu_offload_b200._lib import MOE_OK, lib
+    neg0, neg104 = 0x80000000, int(np.float32(-104.0).view(np.uint32))
+    pos8872 = int(np.float32(88.72).view(np.uint32))
+    chunk = 1 << 26
+    x = torch.empty(chunk, dtype=torch.int64, device="cuda")
+    y = torch.empty(chunk, dtype=torch.float32, device="cuda")
+    yh = torch.empty(chunk, dtype=torch.float32).pin_memory()
+    total = bad = 0
+    for lo, hi in ((neg0, neg104), (0, pos8872)):
+        for b0 in range(lo, hi + 1, chunk):
+            n = min(chunk, hi + 1 - b0)
+            torch.arange(b0, b0 + n, dtype=torch.int64, device="cuda", out=x[:n])
+            xb = torch.where(x[:n] >= 2 ** 31, x[:n] - 2 ** 32, x[:n]).to(torch.int32).view(torch.float32)
+            st = lib().moe_router_exp(ctypes.c_void_p(xb.data_ptr()), ctypes.c_void_p(y.data_ptr()), n,
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            assert st == MOE_OK
+            yh[:n].copy_(y[:n])
+            ref = Port.router_exp_range(b0, n)
+            got = yh[:n].numpy()
+            bad += int(np.count_nonzero(got.view(np.uint32) != ref.view(np.uint32)))
+            total += n
+    print(f"router exp: {bad} mismatches over {total} floats")
+    assert total == (neg104 - neg0 + 1) + (pos8872 + 1)
+    assert bad == 0

@@ -36,6 +36,28 @@ def test_softmax_router_known_answers(case):
         np.testing.assert_allclose(w[0], case["w"], rtol=2e-6)
 
 
+# The routers' exp domain: the softmax evaluates exp(v - max) <= 0 (below -104 it is 0 in fp32);
+# the sigmoid evaluates exp(-v) for any v (above 88.72 it is +inf).
+NEG_ZERO, NEG_104, POS_8872 = 0x80000000, int(np.float32(-104.0).view(np.uint32)), int(np.float32(88.72).view(np.uint32))
+N_SOFTMAX = NEG_104 - NEG_ZERO + 1
+
+
+def test_router_exp_is_correctly_rounded():
+    """The routers' exp (double exp rounded once) equals the long-double exp rounded to fp32 on every
+    61st float of [-104, 0] and every 61st float of [0, 88.72]."""
+    assert Port.router_exp_vs_long_double(NEG_ZERO, N_SOFTMAX // 61, 61) == 0
+    assert Port.router_exp_vs_long_double(0, (POS_8872 + 1) // 61, 61) == 0
+
+
+def test_libm_expf_differs_from_router_exp_by_at_most_one_ulp():
+    """The reference evaluates f32::exp through the platform libm (host.rs.tpl:249).  On this host's
+    libm some of the 1.12e9 softmax-domain results are one ulp away from the correctly rounded value
+    the routers use; none is further off."""
+    bad, worst = Port.libm_expf_mismatches(NEG_ZERO, N_SOFTMAX)
+    print(f"host libm expf differs from the correctly rounded exp on {bad} of {N_SOFTMAX} floats in [-104, 0]")
+    assert worst <= 1, worst
+
+
 def test_sigmoid_router_matches_reference_python(golden):
     g = golden("route_sigmoid.npz")
     idx, w, st = Port.route_sigmoid(g["logits"], g["bias"], int(g["K"]))

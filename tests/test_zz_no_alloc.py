@@ -5,9 +5,11 @@ all of HBM (expert tables plus KV cache), or a framework that forbids allocation
 pool -- so they cannot create a moe_ctx, whose creation allocates.  This entry point needs no
 context: the caller passes inputs and outputs, and the working memory is a 1 MiB file-scope device
 array inside libmoe_dp.so.  These tests call it through the C ABI and compare it with the existing
-context-based moe_ck_moe3 on two calls in a row (different experts, tokens and weights, so stale
-scratch from the first call cannot leak into the second), within the parity tolerance used
-everywhere else (max-abs 2e-2, cosine 0.9999).  The file name makes pytest collect it last.
+context-based moe_ck_moe3 and with the reference's own ck_moe3 (track2_opt/solar_engine/csrc/
+cpu_kern.c:141-172, compiled from the reference sources; the C restatement where this host cannot
+run it) on two calls in a row (different experts, tokens and weights, so stale scratch from the
+first call cannot leak into the second), within the parity tolerance used everywhere else (max-abs
+2e-2, cosine 0.9999).  The file name makes pytest collect it last.
 """
 import ctypes
 
@@ -34,6 +36,20 @@ def _noalloc(bases, w, x, out):
     return lib().moe_ck_moe3_noalloc(len(bases), arr, ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(x.data_ptr()),
                                      ctypes.c_void_p(out.data_ptr()), H, F,
                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+
+def _reference_ck_moe3(bases, w, x, init):
+    """out = init + sum_e w[e] * expert_e(x) on the CPU: the reference's ck_moe3 when it runs here."""
+    from oracle.oracle import Port, Reference
+    from tests.gpu_util import bf16_np
+    b = [bf16_np(t) for t in bases]
+    wn, xn, out = w.cpu().numpy().astype(np.float32), bf16_np(x), init.cpu().numpy().astype(np.float32).copy()
+    if Reference.available():
+        return Reference.ck_moe3(b, wn, xn, out), "reference ck_moe3"
+    jobs = [("bf16", a[:2 * F * H].reshape(2 * F, H), a[2 * F * H:].reshape(H, F)) for a in b]
+    acc = out[None].copy()
+    Port.cpu_moe(xn[None], jobs, [[0]] * len(b), [[v] for v in wn], out=acc, accumulate=True)
+    return acc[0], "oracle ck_moe3 restatement"
 
 
 def test_noalloc_matches_ck_moe3_on_two_calls():
@@ -63,7 +79,11 @@ def test_noalloc_matches_ck_moe3_on_two_calls():
         torch.cuda.synchronize()
         if i == 1:  # the first call may trigger the lazy module load; later calls must not allocate
             assert torch.cuda.mem_get_info()[0] == free_before
-        assert_close(outs[i].cpu().numpy(), refs[i].cpu().numpy(), what=f"noalloc call {i + 1} vs moe_ck_moe3")
+        got = outs[i].cpu().numpy()
+        assert_close(got, refs[i].cpu().numpy(), what=f"noalloc call {i + 1} vs moe_ck_moe3")
+        ref, kind = _reference_ck_moe3(bases, w, x, cases[i][3])
+        d, c = assert_close(got, ref, what=f"noalloc call {i + 1} vs {kind}")
+        print(f"noalloc call {i + 1} vs {kind}: max-abs {d:.3g}, cosine {c:.7f}")
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
