@@ -64,6 +64,7 @@ def parse():
     ap.add_argument("--prefill-tokens", type=int, default=2048,
                     help="configs[3] prefill measurement at N=1 (0 to skip)")
     ap.add_argument("--no-block", action="store_true", help="skip the moe_block_forward measurement")
+    ap.add_argument("--no-int8", action="store_true", help="skip the configs[4] int8 measurement")
     ap.add_argument("--cold-slots", type=int, default=0,
                     help="HBM slots per layer for the host-cold tier measurement (0: skip)")
     ap.add_argument("--ep-shard", choices=["units", "experts"], default="units",
@@ -224,6 +225,11 @@ class Stack:
         self.x = torch.from_numpy(xs.view(np.int16)).view(torch.bfloat16).to(self.device)
         self.lg = torch.from_numpy(lgs).to(self.device)
         self.out = torch.empty(self.L, T, H, dtype=torch.float32, device=self.device)
+        # per (rotation, layer) ctypes arguments of moe_forward, so the timed loop is one C call per layer
+        vp = ctypes.c_void_p
+        self.args = [[(l, T, vp(self.x[r, l].data_ptr()), vp(self.lg[r, l].data_ptr()), vp(self.out[l].data_ptr()))
+                      for l in range(self.L)] for r in range(self.R)]
+        self.sp = vp(torch.cuda.current_stream(self.device).cuda_stream)
         # algorithmic bytes per (rotation, layer): this rank's distinct routed experts
         self.ubytes = np.zeros((self.R, self.L))
         self.ucount = np.zeros((self.R, self.L))
@@ -237,9 +243,10 @@ class Stack:
         torch.cuda.synchronize(self.device)
 
     def step(self, s):
-        r = s % self.R
-        for l in range(self.L):
-            self.plane.forward(l, self.x[r, l], self.lg[r, l], out=self.out[l])
+        from npu_offload_b200._lib import check, lib
+        fn, h, sp = lib().moe_forward, self.plane.handle, self.sp
+        for l, T, x, lg, out in self.args[s % self.R]:
+            check(fn(h, l, T, x, lg, out, None, None, 0, sp))
             if self.ws > 1 and not self.plane.ep_attached:
                 from npu_offload_b200.parallel import allreduce_partial
                 allreduce_partial(self.out[l])
@@ -407,31 +414,108 @@ def block_run(stack, steps, warmup, T=1):
     fn, h = lib().moe_block_forward, stack.plane.handle
     sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
-    def one(s):
-        r = s % R
-        for l in range(L):
-            check(fn(h, l, T, ctypes.c_void_p(h2[r, l].data_ptr()), ctypes.c_void_p(x2[r, l].data_ptr()), None,
-                     ctypes.c_void_p(xn[l].data_ptr()), None, None, 0, sp))
+    vp = ctypes.c_void_p
+    ind = [[(l, vp(h2[r, l].data_ptr()), vp(x2[r, l].data_ptr()), vp(xn[l].data_ptr())) for l in range(L)]
+           for r in range(R)]
 
-    for s in range(warmup):
-        one(s)
-    torch.cuda.synchronize(dev)
-    l0 = stack.plane.launch_count
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for s in range(steps):
-        one(warmup + s)
-    ev1.record()
-    torch.cuda.synchronize(dev)
-    ms = ev0.elapsed_time(ev1)
+    def one(s):
+        for l, a, b, o in ind[s % R]:
+            check(fn(h, l, T, a, b, None, o, None, None, 0, sp))
+
+    # dependent chain: block l's x_next is block l+1's h2 and x2, as in the engine's layer loop
+    # (main.rs:267-289, with attention left out), so the router logits of a layer exist only once
+    # the previous layer is done
+    xc = torch.empty(L + 1, T, H, dtype=torch.bfloat16, device=dev)
+    chain = [(l, vp(xc[l].data_ptr()), vp(xc[l + 1].data_ptr())) for l in range(L)]
+
+    def one_chain(s):
+        xc[0].copy_(h2[s % R, 0])
+        for l, a, o in chain:
+            check(fn(h, l, T, a, a, None, o, None, None, 0, sp))
+
+    def run(f):
+        for s in range(warmup):
+            f(s)
+        torch.cuda.synchronize(dev)
+        l0 = stack.plane.launch_count
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for s in range(steps):
+            f(warmup + s)
+        ev1.record()
+        torch.cuda.synchronize(dev)
+        return ev0.elapsed_time(ev1), stack.plane.launch_count - l0
+
+    ms, nl = run(one)
     reps = [(warmup + s) % R for s in range(steps)]
     nbytes = sum(routed[r].sum() for r in reps) * EXPERT_BYTES + steps * L * (EXPERT_BYTES + E * H * 2)
     us_layer = ms * 1e3 / (steps * L)
+    # the chain's routed experts are only known on the device: count them from one untimed pass
+    routed_chain = []
+    one_chain(0)
+    torch.cuda.synchronize(dev)
+    for l in range(L):
+        lg = torch.empty(T, E, dtype=torch.float32, device=dev)
+        check(lib().moe_shared_router(h, l, T, vp(xc[l].data_ptr()), None, None, vp(lg.data_ptr()), 0, sp))
+        torch.cuda.synchronize(dev)
+        top = np.argsort(-lg.cpu().numpy(), axis=1, kind="stable")[:, :K]
+        routed_chain.append(len(set(top.ravel().tolist())))
+    cms, cnl = run(one_chain)
+    cbytes = steps * (sum(routed_chain) * EXPERT_BYTES + L * (EXPERT_BYTES + E * H * 2))
     return {"workload": f"moe_block_forward: router GEMV + routed experts + shared expert + residual combine, "
                         f"batch {T}, {L} layers",
             "us_per_layer": us_layer, "tokens_per_s": T * L * steps / (ms / 1e3),
             "bytes_per_layer": nbytes / (steps * L), "gbs": nbytes / (ms / 1e3) / 1e9,
-            "gpu_launches_per_layer": (stack.plane.launch_count - l0) / (steps * L)}
+            "gpu_launches_per_layer": nl / (steps * L),
+            "chain": {"workload": "dependent chain: each block's x_next is the next block's h2 and x2 (its "
+                                  "router logits exist only after the previous block)",
+                      "us_per_layer": cms * 1e3 / (steps * L), "tokens_per_s": T * L * steps / (cms / 1e3),
+                      "bytes_per_layer": cbytes / (steps * L), "gbs": cbytes / (cms / 1e3) / 1e9,
+                      "frac": cbytes / (cms / 1e3) / 1e9 / peaks()[0],
+                      "gpu_launches_per_layer": cnl / (steps * L)}}
+
+
+Q8_BYTES = 3 * H * F + (2 * F + H) * 4  # one int8 weight-only expert: q tables + fp32 scales
+
+
+def int8_run(stack, args, steps, warmup):
+    """the stack's 96 least popular experts of every layer (by the Zipf rank of the layer's
+    routing bias) re-stored int8 weight-only (quantised on the GPU with the reference's quant_row
+    rule), the top 32 kept bf16; decode batch 1, the same Zipf-routed inputs.  Roofline bytes: the
+    routed experts' stored bytes (bf16 31,457,280 B; int8 15,728,640 B of tables + 26,624 B of scales)."""
+    import torch
+    from npu_offload_b200 import synth
+    L = stack.L
+    cold = []
+    for l in range(L):
+        order = np.argsort(-synth.zipf_bias(args.seed + 31 * l, E), kind="stable")  # most popular first
+        c = set(order[32:].tolist())
+        for e in sorted(c):
+            stack.plane.quantize_expert_q8(l, e)
+        cold.append(c)
+    stack.set_batch(1, args.seed)
+    R = stack.R
+    nbytes = np.zeros((R, L))
+    n8 = np.zeros((R, L))
+    for r in range(R):
+        for l in range(L):
+            _, idx, _ = stack.plane.forward(l, stack.x[r, l], stack.lg[r, l], out=stack.out[l], return_topk=True)
+            ids = set(idx.cpu().numpy().ravel().tolist())
+            n8[r, l] = sum(e in cold[l] for e in ids)
+            nbytes[r, l] = n8[r, l] * Q8_BYTES + (len(ids) - n8[r, l]) * EXPERT_BYTES
+    torch.cuda.synchronize(stack.device)
+    ms, launches, _ = timed(stack, steps, warmup, 1)
+    reps = [(warmup + s) % R for s in range(steps)]
+    tot = sum(nbytes[r].sum() for r in reps)
+    gbs = tot / (ms / 1e3) / 1e9
+    peak = peaks()[0]
+    return {"workload": f"configs[4]: {L}-layer stack, 96 least popular experts per layer int8 weight-only, "
+                        "top 32 bf16; decode batch 1, Zipf routing",
+            "tokens_per_s": L * steps / (ms / 1e3), "us_per_layer": ms * 1e3 / (steps * L),
+            "int8_experts_per_layer": float(n8.mean()), "bytes_per_layer": tot / (steps * L),
+            "roofline": {"bound": "hbm", "kernel": "decode_kernel", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak},
+            "gpu_launches": launches}
 
 
 def cold_run(args, device, L=2, steps=256, warmup=32):
@@ -595,8 +679,8 @@ def our_arm(args):
 
     # Roofline of the dominant kernel (decode_kernel, one launch per layer): algorithmic bytes per
     # launch = this rank's distinct routed experts x their gate/up/down bytes; launch duration = the
-    # timed region / decode launches (the plan kernel of the next layer runs on the SM the decode
-    # grid leaves free, overlapped; no events between launches, which would break that overlap).
+    # timed region / decode launches (back-to-back launches overlap their start-up with the previous
+    # grid's tail through programmatic dependent launch; events between launches would break that).
     R = stack.R
     reps = [(args.warmup + s) % R for s in range(args.steps)]
     n_dec = args.steps * L
@@ -639,6 +723,9 @@ def our_arm(args):
     cold = None
     if ws == 1 and args.cold_slots > 0:
         cold = cold_run(args, device)
+    int8 = None
+    if ws == 1 and not args.no_int8:  # last: it re-stores most of the stack's experts as int8
+        int8 = int8_run(stack, args, max(1, args.steps // 4), min(args.warmup, 3))
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -677,7 +764,7 @@ def our_arm(args):
                            "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
                 "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep, "prefill": prefill,
-                "block": block, "cold": cold}
+                "block": block, "cold": cold, "int8": int8}
         print(json.dumps(line), flush=True)
     if ws > 1:
         barrier(ws)  # no rank frees its exchange buffer while a peer may still use it

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libmoe_dp.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["moe_dp.cu", "route.cu", "experts.cu", "decode.cu", "plan.cu", "noalloc.cu", "prefill.cu", "prefill_tc.cu",
+SOURCES = ["moe_dp.cu", "route.cu", "experts.cu", "decode.cu", "noalloc.cu", "prefill.cu", "prefill_tc.cu",
            "block.cu"]
 
 

@@ -9,36 +9,44 @@
 
 #include "block.h"
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace moe {
 
-constexpr int kRtWarps = 8;   // experts per CTA (a warp per expert)
-constexpr int kRtTok = 16;    // tokens per CTA row of the grid
+constexpr int kRtThreads = 256;  // one CTA per (expert, tile of kRtTok tokens)
+constexpr int kRtTok = 16;
 
-// Warp per expert row of Wr (H bf16, read once per token block with 16-byte loads); lane-strided
-// 8-element chunks accumulated in fp32 in element order, then a fixed butterfly: the same bits on
-// every run.
-__global__ void __launch_bounds__(kRtWarps * 32) router_gemv_kernel(const uint16_t* __restrict__ wr,
-                                                                  const uint16_t* __restrict__ x, int T, int E, int H,
-                                                                  float* __restrict__ logits) {
-    const int lane = threadIdx.x & 31;
-    const int e = blockIdx.x * kRtWarps + (threadIdx.x >> 5);
-    const int t0 = blockIdx.y * kRtTok, nt = min(kRtTok, T - t0);
-    if (e >= E || nt <= 0) return;
+// logits[t, e] = x[t] . wr[e] in fp32.  Latency-bound (1 MB of router weights for the Solar shape),
+// so every thread issues all its loads at once: thread i covers 16-byte chunks i, i + 256, ... of
+// the row, then the CTA sums the per-thread dot products (warp shuffles, then the 8 warps in order).
+// Launched with programmatic dependent launch: the CTAs take SMs as the previous grid frees them and
+// wait for its completion (x may be its output) before reading; they never trigger their dependents
+// early, so a dependent kernel starts only once the logits are written.
+__global__ void __launch_bounds__(kRtThreads) router_gemv_kernel(const uint16_t* __restrict__ wr,
+                                                               const uint16_t* __restrict__ x, int T, int E, int H,
+                                                               float* __restrict__ logits) {
+    __shared__ float part[kRtThreads / 32][kRtTok];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int e = blockIdx.x, t0 = blockIdx.y * kRtTok, nt = min(kRtTok, T - t0);
+    griddep_wait();
     float acc[kRtTok];
 #pragma unroll
     for (int t = 0; t < kRtTok; t++) acc[t] = 0.f;
     const uint4* w4 = reinterpret_cast<const uint4*>(wr + (size_t)e * H);
     const uint4* x4 = reinterpret_cast<const uint4*>(x + (size_t)t0 * H);
     const int n8 = H / 8;
-    for (int c = lane; c < n8; c += 32) {
+#pragma unroll 2
+    for (int c = tid; c < n8; c += kRtThreads) {
         const uint4 wv = __ldg(w4 + c);
+        uint4 xv[kRtTok];
+#pragma unroll
+        for (int t = 0; t < kRtTok; t++)
+            if (t < nt) xv[t] = __ldg(x4 + (size_t)t * n8 + c);
         const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
         for (int t = 0; t < kRtTok; t++)
             if (t < nt) {
-                const uint4 xv = __ldg(x4 + (size_t)t * n8 + c);
-                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+                const uint32_t xw[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
                     acc[t] = fmaf(bf_lo(ww[k]), bf_lo(xw[k]), acc[t]);
@@ -47,13 +55,19 @@ __global__ void __launch_bounds__(kRtWarps * 32) router_gemv_kernel(const uint16
             }
     }
 #pragma unroll
-    for (int t = 0; t < kRtTok; t++)
+    for (int t = 0; t < kRtTok; t++) {
+        if (t < nt) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-    if (lane == 0) {
+            for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+            if (lane == 0) part[warp][t] = acc[t];
+        }
+    }
+    __syncthreads();
+    if (tid < nt) {
+        float v = 0.f;
 #pragma unroll
-        for (int t = 0; t < kRtTok; t++)
-            if (t < nt) logits[(size_t)(t0 + t) * E + e] = acc[t];
+        for (int w = 0; w < kRtThreads / 32; w++) v += part[w][tid];
+        logits[(size_t)(t0 + tid) * E + e] = v;
     }
 }
 
@@ -61,13 +75,18 @@ cudaError_t launch_router_gemv(const uint16_t* wr, const uint16_t* x, int T, int
                                cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (H % 8 || ((uintptr_t)wr | (uintptr_t)x) & 15) return cudaErrorInvalidValue;
-    dim3 g((E + kRtWarps - 1) / kRtWarps, (T + kRtTok - 1) / kRtTok);
-    router_gemv_kernel<<<g, kRtWarps * 32, 0, st>>>(wr, x, T, E, H, logits);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(E, (T + kRtTok - 1) / kRtTok);
+    cfg.blockDim = dim3(kRtThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, router_gemv_kernel, wr, x, T, E, H, logits);
 }
 
-// 8 elements per thread.  y = y_in, or bf16(x2 + shared) when y_in is null (stored to y_out when
-// set); x_next = bf16((y + extra) + moe) when x_next is set (extra may be null).
 __global__ void __launch_bounds__(256) residual_kernel(const uint16_t* __restrict__ y_in, const uint16_t* __restrict__ x2,
                                                        const float* __restrict__ shared, const float* __restrict__ extra,
                                                        const float* __restrict__ moe, long n, uint16_t* __restrict__ y_out,

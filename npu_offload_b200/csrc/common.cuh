@@ -124,6 +124,9 @@ __device__ __forceinline__ float sum_f32x2(f32x2 v) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
     return lo + hi;
 }
+__device__ __forceinline__ void unpack_f32x2(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
 // two bf16 (one 32-bit word) widened to an fp32 pair
 __device__ __forceinline__ f32x2 bf16x2_to_f32x2(uint32_t w) { return pack_f32x2(bf_lo(w), bf_hi(w)); }
 // d = a * b + c per element, round to nearest (two fmaf in one instruction)
@@ -203,8 +206,12 @@ __device__ __forceinline__ float warp_sum_multi(float (&v)[V]) {
     return v[0];
 }
 
-// int8 value k (0..3) of a 32-bit word, exactly as float.
-__device__ __forceinline__ float i8f(uint32_t v, int k) { return (float)(int8_t)(v >> (8 * k)); }
+// int8 value k (0..3) of a 32-bit word, exactly as float.  The byte plus 128 (the sign bit flipped)
+// is moved into the low mantissa bits of 2^23 by one byte permute, and 2^23 + 128 is subtracted:
+// exact for every int8, and it keeps the conversion off the slower integer-to-float pipe.
+__device__ __forceinline__ float i8f(uint32_t v, int k) {
+    return __uint_as_float(__byte_perm(v ^ 0x80808080u, 0x4B000000u, 0x7540 | k)) - 8388736.f;
+}
 
 // 4 int8 weights (one u32) dot 4 bf16 activations (two u32), fp32.
 __device__ __forceinline__ float dot4_i8(uint32_t w, uint32_t x01, uint32_t x23, float acc) {

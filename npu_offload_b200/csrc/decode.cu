@@ -36,6 +36,7 @@
 
 #include "common.cuh"
 #include "decode.h"
+#include "plan.cuh"
 #include "ptx.cuh"
 
 namespace moe {
@@ -63,12 +64,16 @@ struct __align__(16) Ctrl {
     uint64_t empty[kMaxNS];
     uint64_t xbar[kXB];     // slice-sum exchange of a batch (8 warp arrivals), batch % kXB
     int abort_flag;
-    int pad[3];
+    int ticket;             // this CTA's arrival order (-1: it gave up)
+    int pad[2];
     float red[kXB][kCW][32];  // slice sums of one batch, by batch % kXB
-    PlanCta me;             // this CTA's share (copied from the plan)
-    PlanShared sh;          // reduction tables (copied from the plan after the segments)
+    PlanCta me;             // this CTA's share
+    PlanShared sh;          // reduction tables
+    CallPlan P;             // the call's routing and job structure (plan.cuh)
 };
-static_assert(offsetof(Ctrl, me) % 16 == 0 && offsetof(Ctrl, sh) % 16 == 0, "int4 copies into Ctrl");
+static_assert(offsetof(Ctrl, me) % 16 == 0 && offsetof(Ctrl, sh) % 16 == 0 && offsetof(Ctrl, P) % 16 == 0,
+              "16-byte aligned plan structs");
+static_assert(kDecThreads == kPlanThr, "the planning steps use every thread of the CTA");
 
 __device__ __forceinline__ bool timed_out(Ctrl& c, uint32_t* err, uint64_t deadline) {
     if (*(volatile int*)&c.abort_flag) return true;
@@ -217,20 +222,24 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
                         fma_bf16x2(wu[q], xw[t][cc][q], au[t][k0], au[t][k0 + 1]);
                     }
             } else {
+                // packed f32x2 FMAs: (even, odd) element pairs, the same bits as two fmaf
                 float wg[8], wu[8];
                 load_q8_f32(U + eoff[cc], wg);
                 load_q8_f32(U + H + eoff[cc], wu);
 #pragma unroll
-                for (int q = 0; q < 4; q++)
+                for (int q = 0; q < 4; q++) {
+                    const f32x2 g2 = pack_f32x2(wg[2 * q], wg[2 * q + 1]), u2 = pack_f32x2(wu[2 * q], wu[2 * q + 1]);
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
-                        const float x0 = bf_lo(xw[t][cc][q]), x1 = bf_hi(xw[t][cc][q]);
+                        const f32x2 x2 = bf16x2_to_f32x2(xw[t][cc][q]);
                         const int k0 = NA == 4 ? (q & 1) * 2 : 0;
-                        ag[t][k0] = fmaf(wg[2 * q], x0, ag[t][k0]);
-                        ag[t][k0 + 1] = fmaf(wg[2 * q + 1], x1, ag[t][k0 + 1]);
-                        au[t][k0] = fmaf(wu[2 * q], x0, au[t][k0]);
-                        au[t][k0 + 1] = fmaf(wu[2 * q + 1], x1, au[t][k0 + 1]);
+                        f32x2 a2 = pack_f32x2(ag[t][k0], ag[t][k0 + 1]), b2 = pack_f32x2(au[t][k0], au[t][k0 + 1]);
+                        a2 = ffma2(g2, x2, a2);
+                        b2 = ffma2(u2, x2, b2);
+                        unpack_f32x2(a2, ag[t][k0], ag[t][k0 + 1]);
+                        unpack_f32x2(b2, au[t][k0], au[t][k0 + 1]);
                     }
+                }
             }
         }
 #pragma unroll
@@ -265,8 +274,12 @@ __device__ bool run_segment(const DecodeArgs& a, Ctrl& c, const unsigned char* r
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                     const float at = bf_lo(ab[t]);
+                    const f32x2 a2 = pack_f32x2(at, at);
 #pragma unroll
-                    for (int e = 0; e < 8; e++) y[t][cc][e] = fmaf(wd[e], at, y[t][cc][e]);
+                    for (int e = 0; e < 8; e += 2) {
+                        const f32x2 r = ffma2(pack_f32x2(wd[e], wd[e + 1]), a2, pack_f32x2(y[t][cc][e], y[t][cc][e + 1]));
+                        unpack_f32x2(r, y[t][cc][e], y[t][cc][e + 1]);
+                    }
                 }
             }
         }
@@ -483,8 +496,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
 
     uint64_t* tl = a.timeline ? a.timeline + (size_t)s * kTimelineSlots : nullptr;  // optional phase stamps
     if (tl && tid == 0) tl[0] = globaltimer_ns();
+    // CTA 0 leaves the call's error bits in host memory when asked to (host callers read it after
+    // their stream synchronisation instead of copying the device word back)
+    auto snapshot_err = [&]() {
+        if (a.err_host && s == 0 && tid == 0) *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+    };
 
-    // ---------------- prologue: barriers, then this CTA's share of the plan ----------------
+    // ---------------- prologue: barriers, inputs, the call's plan ----------------
     if (tid == 0) {
         for (int i = 0; i < NS; i++) {
             mbar_init(&c.full[i], 1);
@@ -493,33 +511,68 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         for (int b = 0; b < kXB; b++) mbar_init(&c.xbar[b], kCW);
         c.abort_flag = 0;
         fence_mbar_init();
-        // The plan kernel published the plan before this grid could start; the acquire makes it
-        // visible (bounded in case the launch order was violated).
-        const uint64_t dl = globaltimer_ns() + a.timeout_ns;
-        while (ld_acquire_gpu(a.flag) != a.stamp)
-            if (globaltimer_ns() > dl) {
-                c.abort_flag = 1;
-                atomicOr(a.err, kErrTimeout);
-                break;
-            }
+        // the next call's CTAs may take the SMs this grid frees; they wait below for its completion
+        griddep_launch_dependents();
     }
-    // CTA 0 leaves the call's error bits in host memory when asked to (host callers read it after
-    // their stream synchronisation instead of copying the device word back)
-    auto snapshot_err = [&]() {
-        if (a.err_host && s == 0 && tid == 0) *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
-    };
-    __syncthreads();
-    if (c.abort_flag) {  // no plan: write nothing, the call reports MOE_ETIMEOUT
+    // Routing reads only the router logits, the bias and the expert table, which no decode grid
+    // writes, so the plan is made while the previous grid of the stream still finishes.  Everything
+    // that grid may touch (hidden states, partial sums, counters, outputs) waits for its completion
+    // (griddepcontrol.wait) first: host calls here, the consumers before their first segment.
+    if (a.x_src) {  // host call: each CTA moves a slice of the pinned inputs to the device
+        griddep_wait();
+        if (s == 0 && tid == 0) a.hctr[par ^ 1] = 0;  // the previous call's counter, for the next call
+        const int nx = a.T * a.H / 8, nl = a.T * a.E;
+        const int x0 = (int)((long long)s * nx / G), x1 = (int)((long long)(s + 1) * nx / G);
+        const int l0 = (int)((long long)s * nl / G), l1 = (int)((long long)(s + 1) * nl / G);
+        uint4* xd = reinterpret_cast<uint4*>(const_cast<uint16_t*>(a.x));
+        const uint4* xs = reinterpret_cast<const uint4*>(a.x_src);
+        for (int i = x0 + tid; i < x1; i += kDecThreads) xd[i] = xs[i];
+        float* ld = const_cast<float*>(a.logits);
+        for (int i = l0 + tid; i < l1; i += kDecThreads) ld[i] = a.lg_src[i];
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            atomicAdd(&a.hctr[par], 1u);
+            const uint64_t dl = globaltimer_ns() + a.timeout_ns;
+            while (ld_acquire_gpu(&a.hctr[par]) < (uint32_t)G) {
+                if (globaltimer_ns() > dl) {
+                    c.abort_flag = 1;
+                    atomicOr(a.err, kErrTimeout);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+    }
+    __syncthreads();  // also makes the barrier initialisation visible
+    if (c.abort_flag) {  // the inputs never arrived: write nothing, the call reports MOE_ETIMEOUT
         snapshot_err();
         return;
     }
     {
-        const int4* src = reinterpret_cast<const int4*>(&a.plan->cta[s]);
-        int4* dst = reinterpret_cast<int4*>(&c.me);
-        for (int q = tid; q < (int)(sizeof(PlanCta) / 16); q += kDecThreads) dst[q] = __ldcg(src + q);
+        PlanIn pin;
+        pin.logits = a.logits;
+        pin.bias = a.bias;
+        pin.desc = a.desc;
+        pin.shared = a.shared;
+        pin.idx_out = a.idx_out;
+        pin.w_out = a.w_out;
+        pin.err = a.err;
+        pin.T = a.T;
+        pin.E = a.E;
+        pin.K = a.K;
+        pin.H = a.H;
+        pin.F = a.F;
+        pin.scoring = a.scoring;
+        pin.G = G;
+        pin.gmax = a.gmax;
+        pin.ups_bf16 = a.ups_bf16;
+        pin.ups_q8 = a.ups_q8;
+        // the planning scratch aliases the ring: no copy is issued before plan_call returns
+        plan_call(pin, c.P, *reinterpret_cast<PlanScratch*>(ring), c.sh, c.me, tl);
     }
+    fence_proxy_async_smem();  // generic accesses of the ring before the bulk copies overwrite it
     __syncthreads();
-    if (tid == 0) griddep_launch_dependents();
     if (tl && tid == 0) tl[1] = globaltimer_ns();
     const int nseg = c.me.nseg;
     // ---------------- producer warpgroup: bulk copies of this CTA's units ----------------
@@ -556,9 +609,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
 
     // ---------------- consumer warpgroups ----------------
     setmaxnreg_inc<kConsRegs>();
-    griddep_wait();  // the previous grid's partial / counter / output accesses are complete beyond this point
+    griddep_wait();  // the previous grid's x / partial / counter / output accesses are complete beyond this point
     const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
-    if (s == 0 && tid == 0) a.ctr[par ^ 1] = 0;  // the previous call's counter, for the next call
+    if (s == 0 && tid == 0) a.ctr[par ^ 1] = a.ctr[2 + (par ^ 1)] = 0;  // the previous call's counters
     LoopStat st, *ls = (tl && warp == 0) ? &st : nullptr;
     int stage = 0, batch = 0;
     bool ok = true;
@@ -576,57 +629,79 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         tl[13] = (uint64_t)st.act;
         tl[14] = (uint64_t)st.axpy;
     }
-    // ---------------- grid-wide arrival: every CTA's partials are written ----------------
+    // ---------------- arrival: a ticket per CTA; the last nred CTAs to arrive reduce ----------------
+    // A CTA whose partial sums are written takes a ticket and, unless it is among the last nred to
+    // arrive, exits at once: its SM is free for the next call (whose CTAs plan and start their weight
+    // stream while this call's reduction finishes).  Reducer r owns output quads [r*H/4/nred, ...).
     __threadfence();
     named_bar_sync(1, kCThreads);
-    if (tid == 0 && ok) atomicAdd(&a.ctr[par], 1u);
-    {  // reduction tables
-        const int4* src = reinterpret_cast<const int4*>(&a.plan->sh);
-        int4* dst = reinterpret_cast<int4*>(&c.sh);
-        for (int q = tid; q < (int)(sizeof(PlanShared) / 16); q += kCThreads) dst[q] = __ldcg(src + q);
+    if (tid == 0) c.ticket = ok ? (int)atomicAdd(&a.ctr[par], 1u) : -1;
+    named_bar_sync(1, kCThreads);
+    const int NR = a.nred, tk = c.ticket;
+    if (tk < 0) {  // gave up (its error is raised): leave the error bits for host callers
+        if (a.err_host && tid == 0) *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+        return;
     }
+    if (tk < G - NR) {
+        if (tl && tid == 0) tl[4] = tl[5] = globaltimer_ns();
+        return;
+    }
+    const int rr = tk - (G - NR);
+    // the last reducer to finish leaves the call's error bits for host callers
+    auto reducer_done = [&]() {
+        named_bar_sync(1, kCThreads);
+        if (tid == 0 && atomicAdd(&a.ctr[2 + par], 1u) == (uint32_t)(NR - 1) && a.err_host)
+            *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+    };
+    // the reduction's segment tables (the same in every CTA) while the last CTAs arrive
+    plan_tables(c.P, c.sh, G, a.F, a.H, a.gmax, tid, kCThreads, 1);
+    named_bar_sync(1, kCThreads);
     if (tid == 0) {
         const uint32_t target = (uint32_t)G + (a.inject_timeout ? 1u : 0u);
         while (!*(volatile int*)&c.abort_flag && ld_acquire_gpu(&a.ctr[par]) < target) {
             if (timed_out(c, a.err, deadline)) break;
-            __nanosleep(64);
+            __nanosleep(32);
         }
     }
     named_bar_sync(1, kCThreads);
     if (*(volatile int*)&c.abort_flag) {
-        snapshot_err();
+        reducer_done();
         return;
     }
     if (tl && tid == 0) tl[4] = globaltimer_ns();
 
-    // ---------------- reduction of output quads [q0, q1) ----------------
-    const int H = a.H, q0 = c.me.q0, nq = c.me.q1 - c.me.q0;
+    // ---------------- reduction of output quads [q0, q0 + nq) ----------------
+    const int H = a.H, H4 = H / 4;
+    const int q0 = (int)((long long)rr * H4 / NR), nq = (int)((long long)(rr + 1) * H4 / NR) - q0;
     const int nsegtot = min(c.sh.nsegtot, kMaxSegTotal), np = min(c.sh.np, kDecodeMaxPairs);
-    float4* Q = reinterpret_cast<float4*>(ring);  // [nsegtot][kGroupMax][nq] segment partials of the quads
-    float4* R = Q + (size_t)nsegtot * kGroupMax * nq;  // [np][nq] per-pair sums
-    if (nq > 0) {
+    const int nrows = c.sh.srow0[nsegtot];
+    float4* Q = reinterpret_cast<float4*>(ring);       // [nrows][nq] staged partial sums of the quads
+    float4* R = Q + (size_t)nrows * nq;                // [np][nq] per-pair sums
+    {   // every segment row's quads into shared memory: eight tasks of up to kGroupMax loads per thread in flight
+        constexpr int U = 8;
         const int ntask = nsegtot * nq;
-        for (int f0 = tid; f0 < ntask; f0 += 4 * kCThreads) {
-            float4 v[4][kGroupMax];
+        for (int f0 = tid; f0 < ntask; f0 += U * kCThreads) {
+            float4 v[U][kGroupMax];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < U; u++) {
                 const int f = f0 + u * kCThreads;
                 if (f < ntask) {
                     const int k = f / nq, q = f % nq, rows = c.sh.segrows[k];
-                    const float4* src = reinterpret_cast<const float4*>(a.part + (size_t)k * kGroupMax * H) + q0 + q;
+                    const float4* src =
+                        reinterpret_cast<const float4*>(a.part + (size_t)c.P.segslot[k] * kGroupMax * H) + q0 + q;
 #pragma unroll
                     for (int i = 0; i < kGroupMax; i++)
-                        if (i < rows) v[u][i] = __ldcg(src + (size_t)i * (H / 4));
+                        if (i < rows) v[u][i] = __ldcg(src + (size_t)i * H4);
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < U; u++) {
                 const int f = f0 + u * kCThreads;
                 if (f < ntask) {
-                    const int k = f / nq, q = f % nq, rows = c.sh.segrows[k];
+                    const int k = f / nq, q = f % nq, rows = c.sh.segrows[k], r0 = c.sh.srow0[k];
 #pragma unroll
                     for (int i = 0; i < kGroupMax; i++)
-                        if (i < rows) Q[((size_t)k * kGroupMax + i) * nq + q] = v[u][i];
+                        if (i < rows) Q[(size_t)(r0 + i) * nq + q] = v[u][i];
                 }
             }
         }
@@ -638,7 +713,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         const int k0 = max(c.sh.gvs0[g], 0), k1 = min(c.sh.gvs1[g], nsegtot);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int k = k0; k < k1; k++) {
-            const float4 v = Q[((size_t)k * kGroupMax + row) * nq + q];
+            const float4 v = Q[(size_t)(c.sh.srow0[k] + row) * nq + q];
             acc.x += v.x;
             acc.y += v.y;
             acc.z += v.z;
@@ -665,12 +740,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             mine[f] = acc;
         }
         named_bar_sync(1, kCThreads);
-        if (!ep_combine(a.ep, mine, a.out, a.T, H, q0, nq, s, a.accumulate, a.err, deadline, kCThreads, &c.abort_flag)) {
-            snapshot_err();
-            return;
-        }
+        ep_combine(a.ep, mine, a.out, a.T, H, q0, nq, rr, a.accumulate, a.err, deadline, kCThreads, &c.abort_flag);
         if (tl && tid == 0) tl[5] = globaltimer_ns();
-        snapshot_err();
+        reducer_done();
         return;
     }
     if (a.block) {  // MoE block: residual and combine into the next layer's input (combine.rs:1)
@@ -712,7 +784,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
                     make_uint2((uint32_t)yb[0] | ((uint32_t)yb[1] << 16), (uint32_t)yb[2] | ((uint32_t)yb[3] << 16));
         }
         if (tl && tid == 0) tl[5] = globaltimer_ns();
-        snapshot_err();
+        reducer_done();
         return;
     }
     for (int f = tid; f < a.T * nq; f += kCThreads) {
@@ -732,7 +804,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         *o = acc;
     }
     if (tl && tid == 0) tl[5] = globaltimer_ns();
-    snapshot_err();  // after the grid-wide arrival no CTA raises an error any more
+    reducer_done();
 }
 
 static size_t up128(size_t v) { return (v + 127) / 128 * 128; }
@@ -740,7 +812,7 @@ static size_t up128(size_t v) { return (v + 127) / 128 * 128; }
 bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     if (a.T < 1 || a.T > kDecodeMaxT || a.H % 64 || a.H > 8192 || a.F % 64 || a.E > kMaxExperts || a.K > kMaxTopK)
         return false;
-    if (grid < 1 || grid > plan_max_grid()) return false;
+    if (grid < 1 || grid > kPlanMaxGrid) return false;
     a.ch = a.H <= 2048 ? 1 : (a.H <= 4096 ? 2 : 4);
     a.gmax = a.ch == 4 ? 2 : 4;
     const int np = a.T * a.K;
@@ -771,10 +843,16 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     for (int kb : {kBatch, 2})
         for (int ups : {a.ups_bf16, a.ups_q8})
             if (span(kb, ups) > ns) return false;
-    // the ring doubles as reduction scratch once every stage is consumed
-    const size_t nq = (size_t)(a.H / 4 + grid - 1) / grid + 1;
-    const size_t red = ((size_t)(grid + np) * kGroupMax * nq + (size_t)np * nq + (size_t)a.T * nq) * 16;
-    if (red > (size_t)ns * slot) return false;
+    // The ring doubles as reduction scratch once every stage is consumed: each CTA stages one output
+    // slice of every segment's partial-sum rows.  Rows <= pairs (a shared expert's included) + one
+    // extra segment per share boundary.  (Letting only the last CTAs to arrive reduce, so that the
+    // others free their SMs early, measured slower: the next call's CTAs that land on the reducers'
+    // SMs start late with full-size shares and become its stragglers.)
+    const size_t npt = (size_t)np + a.T;
+    const size_t rows = npt + (size_t)(grid - 1) * std::min(a.gmax, a.T);
+    const size_t nqr = (size_t)(a.H / 4 + grid - 1) / grid;
+    a.nred = (rows * nqr + npt * nqr + (size_t)a.T * nqr) * 16 <= (size_t)ns * slot ? grid : 0;
+    if (a.nred == 0 || sizeof(PlanScratch) > (size_t)ns * slot) return false;
     a.NS = ns;
     *smem_bytes = ctrl + (size_t)ns * slot;
     return true;

@@ -1,4 +1,4 @@
-// Fused decode path: plan kernel + persistent decode kernel, launch interface.
+// Fused decode path: one persistent decode kernel per call (routing, expert GEMV, combine), launch interface.
 #pragma once
 #include "common.cuh"
 
@@ -8,7 +8,7 @@ constexpr int kDecodeMaxT = 16;  // largest batch the fused decode path takes
 constexpr int kDecodeMaxPairs = kDecodeMaxT * kMaxTopK;
 constexpr int kGroupMax = 4;     // tokens of one token group (their x / y slices live in registers)
 constexpr int kMaxGroups = kDecodeMaxPairs;
-constexpr int kPlanMaxGrid = 256;  // decode CTAs a plan can describe
+constexpr int kPlanMaxGrid = 256;  // largest decode grid
 constexpr int kSegPerCta = 8;      // segments (runs of one token group's units) per decode CTA
 constexpr int kMaxSegTotal = kPlanMaxGrid + kMaxGroups;  // segments of one call: <= grid + groups
 constexpr int kTimelineSlots = 16;  // per-CTA stamps recorded when DecodeArgs::timeline is set
@@ -19,11 +19,11 @@ struct __align__(16) Seg {
     const unsigned char* src;  // unit f0
     const float* sc;           // int8 scales [2F + H] of the expert (down scales at 2F), null for bf16
     int kind, f0, nu, nt;      // expert kind, first unit, units, tokens of the group (1..kGroupMax)
-    int gidx, grp, pad0, pad1; // call-wide segment index (its partial-sum slot), token group
+    int gidx, grp, pad0, pad1; // partial-sum slot (share * kSegPerCta + k), token group
     int tok[kGroupMax];        // the group's token rows of x
 };
 
-// One decode CTA's static share: its segments (in stream order) and the output quads it reduces.
+// One decode CTA's share: its segments (in stream order) and the output quads it reduces.
 struct __align__(16) PlanCta {
     int nseg, nstage, q0, q1;          // segments, ring stages, output quads [q0, q1) of H/4
     int seg_stage[kSegPerCta + 1];     // first ring stage of each segment
@@ -31,27 +31,21 @@ struct __align__(16) PlanCta {
     Seg seg[kSegPerCta];
 };
 
-// Routing result and reduction tables of one call, read by every CTA after its segments.
+// Reduction tables of one call (built inside every decode CTA).
 struct __align__(16) PlanShared {
     int T, np, ngrp, nsegtot;
     int sp0, pad_[3];                        // block calls: first pair of the shared expert (pair sp0 + t = token t)
-    int gvs0[kMaxGroups], gvs1[kMaxGroups];  // segment range [gvs0, gvs1) of each token group
+    int gvs0[kMaxGroups], gvs1[kMaxGroups];  // call-wide segment range [gvs0, gvs1) of each token group
     int pgrp[kDecodeMaxPairs];               // token group of pair p (pairs job-major)
     int prow[kDecodeMaxPairs];               // row of pair p inside its group
     float pw[kDecodeMaxPairs];               // routing weight of pair p
     int tpn[kDecodeMaxT];                    // local pairs of token t
     int tpair[kDecodeMaxT][kMaxTopK];        // token t's pairs in job order
-    int segrows[kMaxSegTotal];               // rows (tokens) of each segment's partial sums
-};
-
-struct __align__(16) DecodePlan {
-    PlanShared sh;
-    PlanCta cta[kPlanMaxGrid];
+    int segrows[kMaxSegTotal];               // rows (tokens) of each call-wide segment's partial sums
+    int srow0[kMaxSegTotal + 1];             // first staged row of each call-wide segment (prefix of segrows)
 };
 static_assert(sizeof(Seg) == 64, "Seg layout");
-static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0 && sizeof(DecodePlan) % 16 == 0,
-              "plan structs are copied as int4");
-static_assert(alignof(PlanShared) == 16 && alignof(PlanCta) == 16, "plan structs are copied as int4");
+static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0, "plan structs are 16-byte multiples");
 
 // Expert-parallel combine over NVLink peer memory.  Every rank owns an exchange buffer
 // x[2][world][kEpMaxT][H] fp32 (call parity, source rank, token) and flags[world][kPlanMaxGrid]
@@ -72,35 +66,26 @@ struct EpExchange {
     uint32_t epoch;                // this call's exchange number (same on all ranks), >= 1
 };
 
-struct PlanArgs {
-    const float* logits;   // [T, E] (device memory or device-accessible pinned host memory)
-    const float* bias;     // [E] or null
+struct DecodeArgs {
+    // routing inputs (every CTA routes the call itself)
+    const float* logits;   // [T, E] fp32 device memory (host calls: the device copy the kernel makes)
+    const float* bias;     // [E] or null (sigmoid scoring)
     const ExpDesc* desc;   // [E] expert table of the layer
-    DecodePlan* plan;      // this call's plan (parity buffer)
-    uint32_t* flag;        // this call's plan flag: set to stamp once the plan is written
-    uint32_t stamp;
-    int32_t* idx_out;      // [T, K] router indices
-    float* w_out;          // [T, K] router weights
-    uint32_t* err;
-    int T, E, K, H, F, scoring;
-    int G;                 // decode grid size
-    int gmax;              // tokens per token group (<= kGroupMax)
-    int ups_bf16, ups_q8;  // units per ring stage of each kind
-    uint64_t* timeline;    // optional kTimelineSlots phase stamps of the plan kernel, else null
-    const uint16_t* x_src; // optional: hidden states in device-accessible pinned host memory, copied
-    uint16_t* x_dst;       //   by the plan kernel to x_dst ([T, H] bf16) before it publishes the plan
     const ExpDesc* shared; // block calls: the layer's shared expert, appended as one more job whose
                            //   pairs are every token with weight 1 (kept out of the routed sum)
-};
-
-struct DecodeArgs {
-    const DecodePlan* plan;    // written by plan_kernel for this call
-    const uint32_t* flag;      // plan flag; the plan is valid once *flag == stamp
-    uint32_t stamp;
+    int32_t* idx_out;      // [T, K] router indices (written by CTA 0), or null
+    float* w_out;          // [T, K] router weights, or null
+    // host calls: pinned host sources the CTAs copy (a slice each) into x / logits before routing;
+    // hctr [2] counts the CTAs whose slice is in place (parity double-buffered like ctr)
+    const uint16_t* x_src;
+    const float* lg_src;
+    uint32_t* hctr;
     const uint16_t* x;     // [T, H] bf16
     float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
-    float* part;           // [kMaxSegTotal, kGroupMax, H] fp32 partial sums, one block per segment
-    uint32_t* ctr;         // [2] grid-barrier counters (parity double-buffered)
+    float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums: block s * kSegPerCta + k
+                           //   holds the k-th segment of CTA s's share
+    uint32_t* ctr;         // [4] arrival tickets [2] and finished reducers [2] (parity double-buffered)
+    int nred;              // reducing CTAs: the last nred CTAs to arrive reduce one output slice each
     uint32_t* err;
     uint32_t* err_host;    // optional host-mapped word: CTA 0 stores the error bits there when it exits
     int T, E, K, H, F, scoring, accumulate;
@@ -131,18 +116,14 @@ struct DecodeArgs {
 // Returns false when the shape does not fit the fused path.
 bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes);
 
-// Both launches use programmatic dependent launch: the plan kernel (one CTA) runs beside the
-// previous decode grid on the SM that grid leaves free.
-cudaError_t launch_plan(const PlanArgs& p, cudaStream_t st);
+// One launch per call, with programmatic dependent launch: the grid's CTAs take the SMs the
+// previous decode grid frees and wait (griddepcontrol.wait) for its completion before routing.
 cudaError_t launch_decode(const DecodeArgs& a, int grid, size_t smem, cudaStream_t st);
 
 cudaError_t decode_set_smem_limit();
 // True when every decode kernel instantiation is launched with enough registers per thread for its
 // producer / consumer register split (otherwise the fused path must not be used).
 bool decode_register_split_fits();
-cudaError_t plan_set_smem_limit();
-// Largest decode grid the plan kernel can describe (its shared memory stages one share per CTA).
-int plan_max_grid();
 
 // Cross-rank combine of out[t0 .. t0+T) for a T <= kEpMaxT chunk already holding this rank's partial
 // (multi-kernel path): `part` is the local partial [T, H], `out` receives base (accumulate) + the sum
@@ -150,7 +131,7 @@ int plan_max_grid();
 cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* out, int T, int H, int accumulate,
                                uint32_t* err, uint64_t timeout_ns, int grid, cudaStream_t st);
 
-// Partial-sum floats the decode path needs for hidden size H.
-inline size_t decode_part_floats(int H) { return (size_t)kMaxSegTotal * kGroupMax * H; }
+// Partial-sum floats the decode path needs for hidden size H on a grid of G CTAs.
+inline size_t decode_part_floats(int H, int G) { return (size_t)G * kSegPerCta * kGroupMax * H; }
 
 }  // namespace moe

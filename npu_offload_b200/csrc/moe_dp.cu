@@ -126,7 +126,7 @@ struct moe_ctx {
     int64_t launches = 0;
     uint32_t latched = 0;
     // fused decode kernel state
-    uint32_t* d_ctr = nullptr;  // [2] grid-barrier counters of the fused decode kernel
+    uint32_t* d_ctr = nullptr;  // [4] arrival tickets and finished reducers of the fused decode kernel
     float* d_part = nullptr;    // fused decode partial sums
     // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
     float* d_xbuf = nullptr;            // [2][world][kEpMaxT][H] this rank's receive buffer
@@ -157,8 +157,7 @@ struct moe_ctx {
     uint16_t* d_blk_y = nullptr;        // [max_tokens, H] y = bf16(x2 + shared)
     uint16_t* d_blk_io = nullptr;       // [3][max_tokens, H] host-buffer calls: h2, x2, x_next
     float* d_blk_extra = nullptr;       // [max_tokens, H] host-buffer calls: extra
-    DecodePlan* d_plan = nullptr;   // [2] plans (parity of the call counter)
-    uint32_t* d_plan_flag = nullptr;  // [2] plan publication stamps
+    uint32_t* d_hctr = nullptr;     // [2] host calls: CTAs whose slice of the inputs is on the device
     uint32_t epoch = 0;
     bool fused = true;
     uint64_t timeout_ns = 1000000000ull;
@@ -214,7 +213,10 @@ int finish_sync(moe_ctx* c, cudaStream_t st) {
     uint32_t bits = *c->h_err | c->latched;
     c->latched = 0;
     // a fused call that gave up may leave its grid-arrival counter short of the grid: clear both
-    if ((bits & kErrTimeout) && c->d_ctr) CUDA_TRY(cudaMemset(c->d_ctr, 0, 2 * sizeof(uint32_t)));
+    if ((bits & kErrTimeout) && c->d_ctr) {
+        CUDA_TRY(cudaMemset(c->d_ctr, 0, 4 * sizeof(uint32_t)));
+        CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
+    }
     return map_err(bits);
 }
 
@@ -336,7 +338,7 @@ EpExchange next_ep(moe_ctx* c) {
 // Fills the fused-path arguments that do not depend on the call's buffers; false when the call does
 // not fit the fused path (then the multi-kernel path runs).
 bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) {
-    const int dgrid = c->sm_count - 1;  // one SM stays free for the next call's plan kernel
+    const int dgrid = c->sm_count;  // one persistent CTA per SM
     if (T <= 0 || !c->fused || dgrid < 1) return false;
     da = DecodeArgs{};
     da.part = c->d_part;
@@ -358,47 +360,31 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
     return plan_decode(da, dgrid, dsmem);
 }
 
-// Launches plan_kernel + decode_kernel for one layer (da prepared by prepare_fused, x / out set).
+// Launches the fused decode kernel for one layer (da prepared by prepare_fused, x / out set).  Host
+// calls pass the pinned sources: the kernel copies them to da.x and the context's logits buffer.
 int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t dsmem, cudaStream_t st,
                  cudaEvent_t* marks, const uint16_t* x_host = nullptr, const ExpDesc* shared = nullptr) {
-    const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
+    const int E = c->cfg.n_experts, dgrid = c->sm_count;
     da.ep = next_ep(c);
-    const uint32_t epoch = c->epoch++;
-    PlanArgs pa{};
-    pa.logits = lg;
-    pa.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
-    pa.desc = c->d_desc + (size_t)layer * E;
-    pa.plan = c->d_plan + (epoch & 1);
-    pa.flag = c->d_plan_flag + (epoch & 1);
-    pa.stamp = epoch + 1;
-    pa.idx_out = c->d_idx;
-    pa.w_out = c->d_w;
-    pa.err = c->d_err;
-    pa.T = da.T;
-    pa.E = E;
-    pa.K = da.K;
-    pa.H = da.H;
-    pa.F = da.F;
-    pa.scoring = da.scoring;
-    pa.G = dgrid;
-    pa.gmax = da.gmax;
-    pa.ups_bf16 = da.ups_bf16;
-    pa.ups_q8 = da.ups_q8;
-    pa.timeline = c->d_timeline ? c->d_timeline + (size_t)(c->sm_count - 1) * kTimelineSlots : nullptr;
-    pa.shared = shared;
-    if (x_host) {  // the plan kernel moves the hidden states: da.x is the device copy it writes
-        pa.x_src = x_host;
-        pa.x_dst = const_cast<uint16_t*>(da.x);
+    da.epoch = c->epoch++;
+    da.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
+    da.desc = c->d_desc + (size_t)layer * E;
+    da.shared = shared;
+    da.idx_out = c->d_idx;
+    da.w_out = c->d_w;
+    da.hctr = c->d_hctr;
+    if (x_host) {
+        da.x_src = x_host;
+        da.lg_src = lg;
+        da.logits = c->d_logits;
+    } else {
+        da.x_src = nullptr;
+        da.lg_src = nullptr;
+        da.logits = lg;
     }
-    cudaError_t e = launch_plan(pa, st);
-    if (e != cudaSuccess) return fail(MOE_ECUDA, "plan launch: %s", cudaGetErrorString(e));
     if (marks) cudaEventRecord(marks[1], st);
-    da.plan = pa.plan;
-    da.flag = pa.flag;
-    da.stamp = pa.stamp;
-    da.epoch = epoch;
-    e = launch_decode(da, dgrid, dsmem, st);
-    c->launches += 2;
+    cudaError_t e = launch_decode(da, dgrid, dsmem, st);
+    c->launches += 1;
     if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
     if (marks)
         for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
@@ -452,10 +438,11 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
 }
 
 // Host buffers on the fused path.  Pinned host memory is device-accessible under unified addressing,
-// so the kernels use it in place: the plan kernel reads the logits and copies the hidden states to
-// the device (every decode CTA reads them) before it publishes the plan, the decode kernel writes
-// the output and leaves its error bits in a pinned word.  No copy is issued on the stream.  Unpinned (or, for the output, unaligned) buffers go through the
-// context's pinned staging.  One stream synchronisation ends the call.
+// so the kernel uses it in place: every decode CTA copies a slice of the pinned hidden states and
+// logits into the context's device buffers and routes once all slices are there, writes its part of
+// the output over the bus and CTA 0 leaves the error bits in a pinned word.  No copy is issued on
+// the stream.  Unpinned (or, for the output, unaligned) buffers go through the context's pinned
+// staging.  One stream synchronisation ends the call.
 int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, const float* logits, float* out,
                        int32_t* topk_idx, float* topk_w, int flags, cudaStream_t st, DecodeArgs& da, size_t dsmem) {
     const int H = c->cfg.hidden, E = c->cfg.n_experts, K = c->cfg.top_k;
@@ -464,7 +451,7 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
     const bool pin_o = device_mapped(out) && ((uintptr_t)out & 15u) == 0;
     int s;
     const float* lg = logits;
-    const uint16_t* xs = hidden;  // pinned source the plan kernel copies to the device
+    const uint16_t* xs = hidden;  // pinned source the decode kernel copies to the device
     if (!pin_x || !pin_l) {
         if ((s = c->in_stage.reserve(align_up(hb, 256) + lb))) return s;
         if (!pin_l) {
@@ -495,7 +482,10 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
     c->latched = 0;
     if (bits) {  // clear the sticky device word (and, after a timeout, the grid counters)
         CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(uint32_t)));
-        if (bits & kErrTimeout) CUDA_TRY(cudaMemset(c->d_ctr, 0, 2 * sizeof(uint32_t)));
+        if (bits & kErrTimeout) {
+            CUDA_TRY(cudaMemset(c->d_ctr, 0, 4 * sizeof(uint32_t)));
+            CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
+        }
     }
     if (!pin_o) memcpy(out, o, ob);
     return map_err(bits);
@@ -583,12 +573,11 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
-    if (!st) st = dalloc(&c->d_ctr, 2);
-    if (!st) st = dalloc(&c->d_part, decode_part_floats(k.hidden));
-    if (!st) st = dalloc(&c->d_plan, 2);
-    if (!st) st = dalloc(&c->d_plan_flag, 2);
-    if (!st && cudaMemset(c->d_plan_flag, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
-    if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 2) != cudaSuccess)
+    if (!st) st = dalloc(&c->d_ctr, 4);
+    if (!st) st = dalloc(&c->d_part, decode_part_floats(k.hidden, c->sm_count));
+    if (!st) st = dalloc(&c->d_hctr, 2);
+    if (!st && cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
+    if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 4) != cudaSuccess)
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && cudaMallocHost((void**)&c->h_errsnap, 16) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
@@ -600,10 +589,6 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
         st = fail(MOE_ECUDA, "descriptor upload failed");
     if (!st && cudaMemset(c->d_err, 0, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMemset(c->d_bias, 0, sizeof(float) * (size_t)L * E) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
-    if (!st) {
-        cudaError_t e = plan_set_smem_limit();
-        if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
-    }
     if (!st) {
         cudaError_t e = decode_set_smem_limit();
         if (e != cudaSuccess) st = fail(MOE_ECUDA, "kernel attribute: %s", cudaGetErrorString(e));
@@ -639,8 +624,8 @@ int moe_destroy(moe_ctx* c) {
     if (c->d_timeline) cudaFree(c->d_timeline);
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
                   c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
-                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_plan,
-                  c->d_plan_flag, c->d_part, c->d_route_scratch};
+                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_hctr,
+                  c->d_part, c->d_route_scratch};
     for (void* p : ps) cudaFree(p);
     for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_yf, (void*)c->d_tc_sched,
                     (void*)c->d_tc_items, (void*)c->d_tc_cnt})
@@ -886,7 +871,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
             for (int t0 = 0; t0 < T; t0 += kEpMaxT) {
                 const int tc = std::min(kEpMaxT, T - t0);
                 e = launch_ep_exchange(next_ep(c), c->d_xpart + (size_t)t0 * H, o + (size_t)t0 * H, tc, H, acc ? 1 : 0,
-                                       c->d_err, c->timeout_ns, c->sm_count - 1, st);
+                                       c->d_err, c->timeout_ns, c->sm_count, st);
                 c->launches += 1;
                 if (e != cudaSuccess) return fail(MOE_ECUDA, "exchange launch: %s", cudaGetErrorString(e));
             }
@@ -1387,7 +1372,7 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
     // reduction writes y and x_next (one plan, one decode grid)
     const bool fused = c->cfg.ep_world == 1 && !c->prof_on && c->shared->cfg.inter == c->cfg.inter &&
                        T * (K + 1) <= kDecodeMaxPairs &&
-                       c->sm_count - 1 + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
+                       c->sm_count + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
     if (fused) {
         da.x = dh;
         da.out = c->d_blk_moe;

@@ -1,7 +1,9 @@
 """Expert parallelism across two GPUs with the in-kernel NVLink peer exchange: one process per GPU,
 each owning half of the experts (popularity stripe) or half of every expert's units, both mapping
 each other's exchange buffers.
-Every rank must return the same full layer output, bit for bit, and it must match the oracle.
+Every rank must return the same full layer output, bit for bit, and it must match the oracle; the
+same for the whole MoE block (moe_block_forward: router GEMV, routed experts, shared expert at its
+full width on every rank, residual combine).
 Needs two GPUs (skipped otherwise): kernels that wait on each other must never share one GPU."""
 import os
 import socket
@@ -29,6 +31,17 @@ def _inputs(T, seed):
     from npu_offload_b200.synth import f2bf
     rng = np.random.default_rng(seed)
     return f2bf(rng.standard_normal((T, H), np.float32)), rng.standard_normal((T, E)).astype(np.float32)
+
+
+BLOCK_TS = (1, 5, 40)  # fused block path for T <= 16, composed calls for 40
+
+
+def _shared(seed):
+    """The shared expert (gate, up [F,H], down [H,F]) at the full width F and the router [E,H]."""
+    from npu_offload_b200.synth import f2bf
+    rng = np.random.default_rng(seed)
+    return (f2bf(rng.standard_normal((F, H), np.float32) * 0.05), f2bf(rng.standard_normal((F, H), np.float32) * 0.05),
+            f2bf(rng.standard_normal((H, F), np.float32) * 0.05), f2bf(rng.standard_normal((E, H), np.float32) * 0.05))
 
 
 def _rank(rank, world, port, q, mode):
@@ -62,6 +75,16 @@ def _rank(rank, world, port, q, mode):
             xd = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda()
             out = p.forward(0, xd, torch.from_numpy(lg).cuda(), sync=True)
             res[T] = out.cpu().numpy()
+        # the whole MoE block (router GEMV, routed experts with the peer exchange, the shared expert
+        # replicated on every rank at its full width, residual combine) on both splits
+        sg, su, sd, wr = _shared(6)
+        p.load_shared(0, *(torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).cuda()
+                           for a in (sg, su, sd, wr)))
+        for T in BLOCK_TS:
+            h2, x2 = _inputs(T, 200 + T)[0], _inputs(T, 300 + T)[0]
+            xn = p.block_forward(0, *(torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda() for a in (h2, x2)),
+                                 sync=True)
+            res[("block", T)] = xn.view(torch.int16).cpu().numpy().view(np.uint16)
         x, lg = _inputs(3, 103)  # host buffers (pinned, in place) on the fused path
         px = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory()
         pl = torch.from_numpy(lg).pin_memory()
@@ -115,6 +138,17 @@ def test_peer_exchange_two_gpus_matches_single_rank(mode):
         ref, _, _, st = Port.moe_layer(x, lg, ex, K)
         assert st == 0
         assert_close(got[0][T], ref, what=f"ep2 {mode} peer exchange T={T}")
+    sg, su, sd, wr = _shared(6)
+    from oracle.oracle import bf2f
+    for T in BLOCK_TS:
+        np.testing.assert_array_equal(got[0][("block", T)], got[1][("block", T)])
+        h2, x2 = _inputs(T, 200 + T)[0], _inputs(T, 300 + T)[0]
+        logits = Port.router_logits(h2, wr)
+        moe, _, _, st = Port.moe_layer(h2, logits, ex, K)
+        assert st == 0
+        y, _ = Port.shared_expert(h2, x2, sg, su, sd)
+        ref = Port.combine_residual(y, None, moe)
+        assert_close(bf2f(got[0][("block", T)]), bf2f(ref), what=f"ep2 {mode} moe_block_forward T={T}")
     np.testing.assert_array_equal(got[0]["host_acc"], got[1]["host_acc"])
     x, lg = _inputs(3, 103)
     ref, _, _, _ = Port.moe_layer(x, lg, ex, K)
