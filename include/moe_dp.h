@@ -231,8 +231,9 @@ MOE_API int moe_status(moe_ctx* ctx, void* stream);
 MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 
 /* Context options (moe_set_option):
- *   MOE_OPT_FUSED_DECODE        1 (default): batches of T <= 16 run as one fused persistent kernel
- *                               (routing + expert GEMV + combine); 0: the multi-kernel path.
+ *   MOE_OPT_FUSED_DECODE        1 (default): batches of T <= 16 below the tensor-core threshold run as one
+ *                               fused persistent kernel (routing + expert GEMV + combine); 0: the
+ *                               multi-kernel path.
  *   MOE_OPT_WAIT_TIMEOUT_US     bound on every device-side wait of the fused kernel (default 1 s);
  *                               a wait that runs out makes the call report MOE_ETIMEOUT.
  *   MOE_OPT_INJECT_WAIT_TIMEOUT test hook: 1 makes the fused kernel's grid-wide arrival wait for one
@@ -242,9 +243,11 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               0 = as deep as shared memory allows, the default).
  *   MOE_OPT_STAGE_BYTES         tuning: target bytes per ring stage of the fused kernel (a stage holds
  *                               max(1, target / unit bytes) units; 0 = the default, 32 KiB).
- *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 128) run the expert
- *                               FFN as grouped tensor-core GEMMs when every routed local expert is
- *                               bf16; 0 keeps every batch on the CUDA-core paths.
+ *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 8) run the expert FFN as
+ *                               grouped tensor-core GEMMs (each routed expert read once) when every
+ *                               local expert of the layer is bf16; smaller batches, and layers holding
+ *                               int8 experts, take the fused decode kernel (T <= 16) or the CUDA-core
+ *                               path; 0 keeps every batch off the tensor-core path.
  *   MOE_OPT_PREFILL_TC          1 (default): prefill batches run the gate/up and down GEMMs on the
  *                               library's persistent tcgen05 kernels (SwiGLU fused, g / u / y kept in
  *                               fp32); 0: they stay on the CUDA-core multi-kernel path.

@@ -139,7 +139,7 @@ struct moe_ctx {
     uint32_t xepoch = 0;
     // prefill: grouped GEMMs on the tcgen05 tensor cores between the gather and the combine
     bool prefill = true;
-    int prefill_min_t = 128;            // smallest batch that takes the prefill path
+    int prefill_min_t = 8;              // smallest batch that takes the tensor-core path
     uint16_t* d_pf_x = nullptr;         // [NP, H] gathered token rows (job-major pairs)
     float* d_pf_yf = nullptr;           // [NP, H] down . act (fp32)
     bool prefill_tc = true;             // prefill batches on the tcgen05 kernels; else the CUDA-core path
@@ -389,6 +389,19 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     if (marks)
         for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
     return MOE_OK;
+}
+
+// True when the grouped tensor-core GEMMs take a T-token call of this layer: batches of at least
+// prefill_min_t tokens, every local expert of the layer bf16, a supported shape.  From 8 tokens on
+// they read each routed expert once, while the fused decode kernel streams an expert once per token
+// group of at most 4 tokens (measured on B200 at batch 16: 257 us against 335 us per Solar layer).
+bool prefill_applies(moe_ctx* c, int layer, int T) {
+    const int H = c->cfg.hidden, F = c->cfg.inter, E = c->cfg.n_experts;
+    if (!c->prefill || !c->prefill_tc || T < c->prefill_min_t || !tc_available() || F % 128 || H % 256 || E > kMaxExperts)
+        return false;
+    for (int e = 0; e < E; e++)
+        if (c->h_desc[(size_t)layer * E + e].kind == kKindQ8) return false;
+    return true;
 }
 
 // Prefill: after the router has grouped the pairs (d_jobs, d_ptok, d_pw, combine lists), the expert
@@ -788,7 +801,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
     int s;
     DecodeArgs da{};
     size_t dsmem = 0;
-    const bool use_fused = prepare_fused(c, T, flags, da, &dsmem);
+    const bool use_fused = !prefill_applies(c, layer, T) && prepare_fused(c, T, flags, da, &dsmem);
     if (host && use_fused && !c->prof_on)
         return forward_host_fused(c, layer, T, hidden, logits, out, topk_idx, topk_w, flags, st, da, dsmem);
     if (host && T > 0) {
@@ -858,7 +871,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         bool done = false;
         c->launches += n;
         n = 0;
-        if (c->prefill && T >= c->prefill_min_t && !marks) {
+        if (prefill_applies(c, layer, T) && !marks) {
             int r = run_prefill(c, layer, T, x, ea.out, ea.accumulate, st, &done);
             if (r) return r;
         }
@@ -1371,6 +1384,7 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
     // fused: the shared expert is one more job of the routed unit stream, and the decode kernel's
     // reduction writes y and x_next (one plan, one decode grid)
     const bool fused = c->cfg.ep_world == 1 && !c->prof_on && c->shared->cfg.inter == c->cfg.inter &&
+                       !prefill_applies(c, layer, T) &&
                        T * (K + 1) <= kDecodeMaxPairs &&
                        c->sm_count + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
     if (fused) {

@@ -94,7 +94,7 @@ def test_shared_router_and_block_small(T):
         xb, yb, lb = p.block_forward(layer, _dev(h2), _dev(x2), extra=torch.from_numpy(extra).cuda(),
                                      return_parts=True, sync=True)
         np.testing.assert_array_equal(lb.cpu().numpy(), lg)
-        if T <= 16:
+        if T < 8:  # from 8 tokens on the tensor-core path composes the separate calls
             # one fused decode grid streams the shared expert with the routed ones: its share
             # boundaries, hence the partial-sum order, differ from the separate calls'
             assert_bf16_close(bf16_np(yb), bf16_np(y), f"fused y T={T}")
@@ -118,7 +118,7 @@ def test_shared_router_and_block_small(T):
         xb0 = p.block_forward(layer, _dev(h2), _dev(x2), sync=True)
         np.testing.assert_array_equal(bf16_np(p.block_forward(layer, _dev(h2), _dev(x2), sync=True)), bf16_np(xb0))
         ref0 = Port.combine_residual(bf16_np(y), None, moe.cpu().numpy())
-        if T <= 16:
+        if T < 8:
             assert_bf16_close(bf16_np(xb0), ref0, f"fused x_next, no extra, T={T}", slack=_ulp_bf16(bf2f(bf16_np(y))))
         else:
             np.testing.assert_array_equal(bf16_np(xb0), ref0)

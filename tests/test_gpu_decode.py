@@ -17,9 +17,11 @@ H, F, E, K = 4096, 1280, 128, 8
 def layer():
     from npu_offload_b200.moe import MoEDataPlane
     W = gpu_experts(33, E, H, F)
+    from npu_offload_b200._lib import MOE_OPT_PREFILL_MIN_T
     p = MoEDataPlane(H, F, E, K, n_layers=1, max_tokens=32)
     for e, (g, u, d) in enumerate(W):
         p.load_expert(0, e, g, u, d)
+    p.set_option(MOE_OPT_PREFILL_MIN_T, 0)  # every batch up to 16 tokens on the fused kernel
     yield p, W
     p.close()
 
@@ -134,8 +136,11 @@ def test_expert_parallel_partials_sum_to_the_full_layer(layer):
     ranks = [MoEDataPlane(H, F, E, K, n_layers=1, max_tokens=32, ep_rank=r, ep_world=2, shard_map=smap)
              for r in range(2)]
     try:
+        from npu_offload_b200._lib import MOE_OPT_PREFILL_MIN_T
         for e in range(E):
             ranks[int(smap[0, e])].load_expert(0, e, *W[e])
+        for r in ranks:
+            r.set_option(MOE_OPT_PREFILL_MIN_T, 0)  # the same paths as the unsharded layer's
         for T in (1, 4, 16, 24):
             x, lg, xd, lgd = _inputs(1200 + T, T)
             full = p.forward(0, xd, lgd, sync=True).cpu().numpy()
@@ -144,3 +149,28 @@ def test_expert_parallel_partials_sum_to_the_full_layer(layer):
     finally:
         for r in ranks:
             r.close()
+
+
+@pytest.mark.parametrize("T", [8, 16])
+def test_batches_from_8_tokens_take_the_tensor_core_path(layer, T):
+    """With the default threshold (MOE_OPT_PREFILL_MIN_T = 8) a bf16 layer's batch of 8 or more tokens
+    runs as grouped tensor-core GEMMs (each routed expert read once): the same top-k, the output
+    within the parity bar of the fused kernel's and of the oracle, and more than one launch."""
+    from npu_offload_b200._lib import MOE_OPT_PREFILL_MIN_T
+    p, W = layer
+    x, lg, xd, lgd = _inputs(1400 + T, T)
+    fused, fi, _ = p.forward(0, xd, lgd, return_topk=True, sync=True)
+    p.set_option(MOE_OPT_PREFILL_MIN_T, 8)
+    try:
+        n0 = p.launch_count
+        tc, ti, _ = p.forward(0, xd, lgd, return_topk=True, sync=True)
+        assert p.launch_count - n0 > 1
+    finally:
+        p.set_option(MOE_OPT_PREFILL_MIN_T, 0)
+    np.testing.assert_array_equal(ti.cpu().numpy(), fi.cpu().numpy())
+    assert_close(tc.cpu().numpy(), fused.cpu().numpy(), what=f"tensor cores vs fused T={T}")
+    ids = sorted(set(fi.cpu().numpy().ravel().tolist()))
+    ex = {e: ("bf16", np.concatenate([bf16_np(W[e][0]), bf16_np(W[e][1])], 0), bf16_np(W[e][2])) for e in ids}
+    ref, idx, _, _, kind = oracle_layer(x, lg, ex, K)
+    np.testing.assert_array_equal(ti.cpu().numpy(), idx)
+    assert_close(tc.cpu().numpy(), ref, what=f"tensor cores T={T} vs {kind}")
