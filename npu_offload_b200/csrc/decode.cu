@@ -65,7 +65,8 @@ struct __align__(16) Ctrl {
     uint64_t xbar[kXB];     // slice-sum exchange of a batch (8 warp arrivals), batch % kXB
     int abort_flag;
     int ticket;             // this CTA's arrival order (-1: it gave up)
-    int pad[2];
+    int use_pub;            // the CTA took the published plan
+    int pad;
     float red[kXB][kCW][32];  // slice sums of one batch, by batch % kXB
     PlanCta me;             // this CTA's share
     PlanShared sh;          // reduction tables
@@ -544,12 +545,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             }
         }
     }
+    if (tid == 0) c.use_pub = a.pub && ld_acquire_gpu(a.pub_flag) == a.stamp;
     __syncthreads();  // also makes the barrier initialisation visible
     if (c.abort_flag) {  // the inputs never arrived: write nothing, the call reports MOE_ETIMEOUT
         snapshot_err();
         return;
     }
-    {
+    if (c.use_pub) {  // the planner got ahead: this CTA's share, as published
+        const int4* src = reinterpret_cast<const int4*>(&a.pub->cta[s]);
+        int4* dst = reinterpret_cast<int4*>(&c.me);
+        for (int q = tid; q < (int)(sizeof(PlanCta) / 16); q += kDecThreads) dst[q] = __ldcg(src + q);
+    } else {
         PlanIn pin;
         pin.logits = a.logits;
         pin.bias = a.bias;
@@ -609,9 +615,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
 
     // ---------------- consumer warpgroups ----------------
     setmaxnreg_inc<kConsRegs>();
-    griddep_wait();  // the previous grid's x / partial / counter / output accesses are complete beyond this point
     const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
-    if (s == 0 && tid == 0) a.ctr[par ^ 1] = a.ctr[2 + (par ^ 1)] = 0;  // the previous call's counters
+    const unsigned long long cbase = (unsigned long long)a.epoch * (unsigned long long)G;
+    // the previous calls' reducers are done: their x / partial-sum / output accesses are complete
+    if (tid == 0) {
+        while (ld_acquire_gpu_u64(&a.cnt[1]) < cbase) {
+            if (timed_out(c, a.err, deadline)) break;
+            __nanosleep(32);
+        }
+    }
+    named_bar_sync(1, kCThreads);
     LoopStat st, *ls = (tl && warp == 0) ? &st : nullptr;
     int stage = 0, batch = 0;
     bool ok = true;
@@ -635,30 +648,44 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     // stream while this call's reduction finishes).  Reducer r owns output quads [r*H/4/nred, ...).
     __threadfence();
     named_bar_sync(1, kCThreads);
-    if (tid == 0) c.ticket = ok ? (int)atomicAdd(&a.ctr[par], 1u) : -1;
+    if (tid == 0) c.ticket = ok && !*(volatile int*)&c.abort_flag ? (int)(atomicAdd(&a.cnt[0], 1ull) - cbase) : -1;
     named_bar_sync(1, kCThreads);
     const int NR = a.nred, tk = c.ticket;
     if (tk < 0) {  // gave up (its error is raised): leave the error bits for host callers
+        if (tid == 0) griddep_wait();
         if (a.err_host && tid == 0) *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
         return;
     }
     if (tk < G - NR) {
+        if (tid == 0) griddep_wait();
         if (tl && tid == 0) tl[4] = tl[5] = globaltimer_ns();
         return;
     }
     const int rr = tk - (G - NR);
     // the last reducer to finish leaves the call's error bits for host callers
     auto reducer_done = [&]() {
+        __threadfence();  // this reducer's outputs before its count (the next call waits for the count)
         named_bar_sync(1, kCThreads);
-        if (tid == 0 && atomicAdd(&a.ctr[2 + par], 1u) == (uint32_t)(NR - 1) && a.err_host)
+        if (tid == 0) griddep_wait();  // this grid completes after its predecessor (the call's planner)
+        if (tid == 0 && atomicAdd(&a.cnt[1], 1ull) == cbase + (unsigned long long)(NR - 1) && a.err_host)
             *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
     };
-    // the reduction's segment tables (the same in every CTA) while the last CTAs arrive
-    plan_tables(c.P, c.sh, G, a.F, a.H, a.gmax, tid, kCThreads, 1);
+    // the reduction's segment tables (the same in every CTA) while the last CTAs arrive: published
+    // with the plan, or built here
+    if (c.use_pub) {
+        const int4* s1 = reinterpret_cast<const int4*>(&a.pub->sh);
+        int4* d1 = reinterpret_cast<int4*>(&c.sh);
+        for (int q = tid; q < (int)(sizeof(PlanShared) / 16); q += kCThreads) d1[q] = __ldcg(s1 + q);
+        const int4* s2 = reinterpret_cast<const int4*>(&a.pub->P);
+        int4* d2 = reinterpret_cast<int4*>(&c.P);
+        for (int q = tid; q < (int)(sizeof(CallPlan) / 16); q += kCThreads) d2[q] = __ldcg(s2 + q);
+    } else {
+        plan_tables(c.P, c.sh, G, a.F, a.H, a.gmax, tid, kCThreads, 1);
+    }
     named_bar_sync(1, kCThreads);
     if (tid == 0) {
-        const uint32_t target = (uint32_t)G + (a.inject_timeout ? 1u : 0u);
-        while (!*(volatile int*)&c.abort_flag && ld_acquire_gpu(&a.ctr[par]) < target) {
+        const unsigned long long target = cbase + (unsigned long long)G + (a.inject_timeout ? 1ull : 0ull);
+        while (!*(volatile int*)&c.abort_flag && ld_acquire_gpu_u64(&a.cnt[0]) < target) {
             if (timed_out(c, a.err, deadline)) break;
             __nanosleep(32);
         }
@@ -896,8 +923,91 @@ cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* o
     return cudaGetLastError();
 }
 
+// The planner: one CTA computes the whole plan of a call with the decode CTAs' own code and
+// publishes it (st.release of the stamp).  It lets its decode grid launch at once, and before exiting
+// it waits for its own predecessor grid; its decode grid waits for it only as its last step, so the
+// completion of a decode grid implies that of every grid before it in the stream while no decode
+// CTA's start waits for a planner.  The planner runs on the SM the decode grid leaves free.  Plans
+// rotate over four buffers: a decode grid reads its plan before its reducers finish, and a call's
+// CTAs wait for the previous call's reducers, so the planner of call e + 4 never meets a grid still
+// reading plan e.
+struct __align__(16) PlannerSmem {
+    CallPlan P;
+    PlanShared sh;
+    PlanCta me;
+    PlanScratch R;
+};
+
+__global__ void __launch_bounds__(kDecThreads, 1) planner_kernel(const DecodeArgs a, int G, PubPlan* out, uint32_t* flag,
+                                                                 uint32_t stamp) {
+    extern __shared__ __align__(16) unsigned char psm[];
+    PlannerSmem& m = *reinterpret_cast<PlannerSmem*>(psm);
+    const int tid = threadIdx.x;
+    if (tid == 0) griddep_launch_dependents();
+    PlanIn pin;
+    pin.logits = a.logits;
+    pin.bias = a.bias;
+    pin.desc = a.desc;
+    pin.shared = a.shared;
+    pin.idx_out = a.idx_out;
+    pin.w_out = a.w_out;
+    pin.err = a.err;
+    pin.T = a.T;
+    pin.E = a.E;
+    pin.K = a.K;
+    pin.H = a.H;
+    pin.F = a.F;
+    pin.scoring = a.scoring;
+    pin.G = G;
+    pin.gmax = a.gmax;
+    pin.ups_bf16 = a.ups_bf16;
+    pin.ups_q8 = a.ups_q8;
+    plan_call(pin, m.P, m.R, m.sh, m.me);
+    plan_tables(m.P, m.sh, G, a.F, a.H, a.gmax, tid, kDecThreads, 1);
+    named_bar_sync(1, kDecThreads);
+    for (int ss = tid; ss < G; ss += kDecThreads) {  // every share, straight to the published plan
+        PlanCta pc;
+        plan_share_seq(pin, m.P, m.sh, ss, pc);
+        const int4* src = reinterpret_cast<const int4*>(&pc);
+        int4* dst = reinterpret_cast<int4*>(&out->cta[ss]);
+        const int n16 = (int)((offsetof(PlanCta, seg) + (size_t)pc.nseg * sizeof(Seg)) / 16);
+        for (int q = 0; q < n16; q++) dst[q] = src[q];
+    }
+    {
+        const int4* s1 = reinterpret_cast<const int4*>(&m.P);
+        int4* d1 = reinterpret_cast<int4*>(&out->P);
+        for (int q = tid; q < (int)(sizeof(CallPlan) / 16); q += kDecThreads) d1[q] = s1[q];
+        const int4* s2 = reinterpret_cast<const int4*>(&m.sh);
+        int4* d2 = reinterpret_cast<int4*>(&out->sh);
+        for (int q = tid; q < (int)(sizeof(PlanShared) / 16); q += kDecThreads) d2[q] = s2[q];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(stamp) : "memory");
+        griddep_wait();  // complete only after the preceding grid (see above)
+    }
+}
+
+size_t pub_plan_bytes() { return sizeof(PubPlan); }
+
+cudaError_t launch_planner(const DecodeArgs& a, int grid, PubPlan* out, uint32_t* flag, uint32_t stamp, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = sizeof(PlannerSmem);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, planner_kernel, a, grid, out, flag, stamp);
+}
+
 cudaError_t decode_set_smem_limit() {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
+    cudaError_t e = cudaFuncSetAttribute(planner_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PlannerSmem));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
     return e;

@@ -66,8 +66,15 @@ struct EpExchange {
     uint32_t epoch;                // this call's exchange number (same on all ranks), >= 1
 };
 
+struct PubPlan;
+
 struct DecodeArgs {
-    // routing inputs (every CTA routes the call itself)
+    // a plan published by the call's planner kernel (null: none); a CTA that finds pub_flag == stamp
+    // when it starts copies its share from it instead of planning itself
+    const PubPlan* pub;
+    const uint32_t* pub_flag;
+    uint32_t stamp;
+    // routing inputs (every CTA routes the call itself unless the published plan is ready)
     const float* logits;   // [T, E] fp32 device memory (host calls: the device copy the kernel makes)
     const float* bias;     // [E] or null (sigmoid scoring)
     const ExpDesc* desc;   // [E] expert table of the layer
@@ -84,7 +91,10 @@ struct DecodeArgs {
     float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
     float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums: block s * kSegPerCta + k
                            //   holds the k-th segment of CTA s's share
-    uint32_t* ctr;         // [4] arrival tickets [2] and finished reducers [2] (parity double-buffered)
+    unsigned long long* cnt; // [2] monotonic over the context's fused calls: CTAs arrived, reducers finished.
+                             //   Call `epoch` on G CTAs owns the counts [epoch * G, (epoch + 1) * G): its
+                             //   CTAs wait for the previous calls to finish (cnt[1] >= epoch * G) before
+                             //   touching x, partial sums or outputs, so no grid ever waits for a planner
     int nred;              // reducing CTAs: the last nred CTAs to arrive reduce one output slice each
     uint32_t* err;
     uint32_t* err_host;    // optional host-mapped word: CTA 0 stores the error bits there when it exits
@@ -116,9 +126,13 @@ struct DecodeArgs {
 // Returns false when the shape does not fit the fused path.
 bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes);
 
-// One launch per call, with programmatic dependent launch: the grid's CTAs take the SMs the
-// previous decode grid frees and wait (griddepcontrol.wait) for its completion before routing.
+// Per call: the planner kernel (one CTA, published plan) and the decode grid, both with programmatic
+// dependent launch.  The planner runs on the SM the decode grid leaves free, so for back-to-back
+// calls the next plan is usually ready before its decode CTAs start; a decode CTA that finds it not
+// ready plans itself (the same code, the same bits).
+cudaError_t launch_planner(const DecodeArgs& a, int grid, PubPlan* out, uint32_t* flag, uint32_t stamp, cudaStream_t st);
 cudaError_t launch_decode(const DecodeArgs& a, int grid, size_t smem, cudaStream_t st);
+size_t pub_plan_bytes();
 
 cudaError_t decode_set_smem_limit();
 // True when every decode kernel instantiation is launched with enough registers per thread for its

@@ -126,7 +126,7 @@ struct moe_ctx {
     int64_t launches = 0;
     uint32_t latched = 0;
     // fused decode kernel state
-    uint32_t* d_ctr = nullptr;  // [4] arrival tickets and finished reducers of the fused decode kernel
+    unsigned long long* d_cnt = nullptr;  // [2] fused decode calls: CTAs arrived, reducers finished (monotonic)
     float* d_part = nullptr;    // fused decode partial sums
     // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
     float* d_xbuf = nullptr;            // [2][world][kEpMaxT][H] this rank's receive buffer
@@ -158,6 +158,8 @@ struct moe_ctx {
     uint16_t* d_blk_io = nullptr;       // [3][max_tokens, H] host-buffer calls: h2, x2, x_next
     float* d_blk_extra = nullptr;       // [max_tokens, H] host-buffer calls: extra
     uint32_t* d_hctr = nullptr;     // [2] host calls: CTAs whose slice of the inputs is on the device
+    PubPlan* d_pub = nullptr;       // [4] plans published by the planner kernel (call number mod 4)
+    uint32_t* d_pub_flag = nullptr; // [4] their stamps
     uint32_t epoch = 0;
     bool fused = true;
     uint64_t timeout_ns = 1000000000ull;
@@ -207,15 +209,24 @@ void queue_err_readback(moe_ctx* c, cudaStream_t st) {
     cudaMemsetAsync(c->d_err, 0, sizeof(uint32_t), st);
 }
 
+// After a fused call gave up, its counts fall short: every call so far counts as finished.
+int reset_counters(moe_ctx* c) {
+    const unsigned long long v = (unsigned long long)c->epoch * (unsigned long long)(c->sm_count - 1);
+    const unsigned long long h[2] = {v, v};
+    CUDA_TRY(cudaMemcpy(c->d_cnt, h, sizeof(h), cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
+    return MOE_OK;
+}
+
 int finish_sync(moe_ctx* c, cudaStream_t st) {
     queue_err_readback(c, st);
     CUDA_TRY(cudaStreamSynchronize(st));
     uint32_t bits = *c->h_err | c->latched;
     c->latched = 0;
     // a fused call that gave up may leave its grid-arrival counter short of the grid: clear both
-    if ((bits & kErrTimeout) && c->d_ctr) {
-        CUDA_TRY(cudaMemset(c->d_ctr, 0, 4 * sizeof(uint32_t)));
-        CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
+    if ((bits & kErrTimeout) && c->d_cnt) {
+        int r = reset_counters(c);
+        if (r) return r;
     }
     return map_err(bits);
 }
@@ -338,11 +349,11 @@ EpExchange next_ep(moe_ctx* c) {
 // Fills the fused-path arguments that do not depend on the call's buffers; false when the call does
 // not fit the fused path (then the multi-kernel path runs).
 bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) {
-    const int dgrid = c->sm_count;  // one persistent CTA per SM
+    const int dgrid = c->sm_count - 1;  // one persistent CTA per SM; one SM for the next call's planner
     if (T <= 0 || !c->fused || dgrid < 1) return false;
     da = DecodeArgs{};
     da.part = c->d_part;
-    da.ctr = c->d_ctr;
+    da.cnt = c->d_cnt;
     da.err = c->d_err;
     da.T = T;
     da.E = c->cfg.n_experts;
@@ -363,8 +374,9 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
 // Launches the fused decode kernel for one layer (da prepared by prepare_fused, x / out set).  Host
 // calls pass the pinned sources: the kernel copies them to da.x and the context's logits buffer.
 int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t dsmem, cudaStream_t st,
-                 cudaEvent_t* marks, const uint16_t* x_host = nullptr, const ExpDesc* shared = nullptr) {
-    const int E = c->cfg.n_experts, dgrid = c->sm_count;
+                 cudaEvent_t* marks, const uint16_t* x_host = nullptr, const ExpDesc* shared = nullptr,
+                 bool planner = true) {
+    const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
     da.ep = next_ep(c);
     da.epoch = c->epoch++;
     da.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
@@ -382,8 +394,21 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
         da.lg_src = nullptr;
         da.logits = lg;
     }
+    da.pub = nullptr;
+    da.pub_flag = nullptr;
+    da.stamp = da.epoch + 1;
+    cudaError_t e = cudaSuccess;
+    if (!x_host && planner) {  // the planner publishes the plan if it gets ahead of the decode CTAs
+        PubPlan* pub = reinterpret_cast<PubPlan*>(reinterpret_cast<char*>(c->d_pub) + (da.epoch & 3) * pub_plan_bytes());
+        uint32_t* flag = c->d_pub_flag + (da.epoch & 3);
+        e = launch_planner(da, dgrid, pub, flag, da.stamp, st);
+        if (e != cudaSuccess) return fail(MOE_ECUDA, "planner launch: %s", cudaGetErrorString(e));
+        c->launches += 1;
+        da.pub = pub;
+        da.pub_flag = flag;
+    }
     if (marks) cudaEventRecord(marks[1], st);
-    cudaError_t e = launch_decode(da, dgrid, dsmem, st);
+    e = launch_decode(da, dgrid, dsmem, st);
     c->launches += 1;
     if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
     if (marks)
@@ -496,8 +521,8 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
     if (bits) {  // clear the sticky device word (and, after a timeout, the grid counters)
         CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(uint32_t)));
         if (bits & kErrTimeout) {
-            CUDA_TRY(cudaMemset(c->d_ctr, 0, 4 * sizeof(uint32_t)));
-            CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
+            int r = reset_counters(c);
+            if (r) return r;
         }
     }
     if (!pin_o) memcpy(out, o, ob);
@@ -586,11 +611,14 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
-    if (!st) st = dalloc(&c->d_ctr, 4);
+    if (!st) st = dalloc(&c->d_cnt, 2);
     if (!st) st = dalloc(&c->d_part, decode_part_floats(k.hidden, c->sm_count));
     if (!st) st = dalloc(&c->d_hctr, 2);
+    if (!st) st = dalloc(reinterpret_cast<char**>(&c->d_pub), 4 * pub_plan_bytes());
+    if (!st) st = dalloc(&c->d_pub_flag, 4);
+    if (!st && cudaMemset(c->d_pub_flag, 0, 4 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
-    if (!st && cudaMemset(c->d_ctr, 0, sizeof(uint32_t) * 4) != cudaSuccess)
+    if (!st && cudaMemset(c->d_cnt, 0, sizeof(unsigned long long) * 2) != cudaSuccess)
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && cudaMallocHost((void**)&c->h_errsnap, 16) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
@@ -637,8 +665,8 @@ int moe_destroy(moe_ctx* c) {
     if (c->d_timeline) cudaFree(c->d_timeline);
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
                   c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
-                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_ctr, c->d_hctr,
-                  c->d_part, c->d_route_scratch};
+                  c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_cnt, c->d_hctr,
+                  c->d_part, c->d_route_scratch, c->d_pub, c->d_pub_flag};
     for (void* p : ps) cudaFree(p);
     for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_yf, (void*)c->d_tc_sched,
                     (void*)c->d_tc_items, (void*)c->d_tc_cnt})
@@ -884,7 +912,7 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
             for (int t0 = 0; t0 < T; t0 += kEpMaxT) {
                 const int tc = std::min(kEpMaxT, T - t0);
                 e = launch_ep_exchange(next_ep(c), c->d_xpart + (size_t)t0 * H, o + (size_t)t0 * H, tc, H, acc ? 1 : 0,
-                                       c->d_err, c->timeout_ns, c->sm_count, st);
+                                       c->d_err, c->timeout_ns, c->sm_count - 1, st);
                 c->launches += 1;
                 if (e != cudaSuccess) return fail(MOE_ECUDA, "exchange launch: %s", cudaGetErrorString(e));
             }
@@ -1386,7 +1414,7 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
     const bool fused = c->cfg.ep_world == 1 && !c->prof_on && c->shared->cfg.inter == c->cfg.inter &&
                        !prefill_applies(c, layer, T) &&
                        T * (K + 1) <= kDecodeMaxPairs &&
-                       c->sm_count + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
+                       c->sm_count - 1 + T * (K + 1) <= kMaxSegTotal && prepare_fused(c, T, 0, da, &dsmem);
     if (fused) {
         da.x = dh;
         da.out = c->d_blk_moe;
@@ -1395,7 +1423,8 @@ int moe_block_forward(moe_ctx* c, int layer, int T, const uint16_t* h2, const ui
         da.extra = de;
         da.x_next = dn;
         da.y_out = y;
-        if ((st = launch_fused(c, layer, lg, da, dsmem, s, nullptr, nullptr, c->shared->d_desc + layer))) return st;
+        // the logits come from the GEMV just launched: a planner could never get ahead, only add a hop
+        if ((st = launch_fused(c, layer, lg, da, dsmem, s, nullptr, nullptr, c->shared->d_desc + layer, false))) return st;
     } else {
         // routed experts (their plan runs as soon as the logits exist), shared expert (its plan
         // overlaps the routed stream), then one element-wise pass for y and x_next

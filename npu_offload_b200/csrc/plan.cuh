@@ -416,6 +416,51 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
     __syncthreads();
 }
 
+// A call's plan as a planner CTA publishes it for the decode grid: the structures every decode CTA
+// would otherwise compute itself (routing and jobs, the reduction tables, every CTA's share).
+struct __align__(16) PubPlan {
+    CallPlan P;
+    PlanShared sh;
+    PlanCta cta[kPlanMaxGrid];
+};
+
+// Share s's segments, built by one thread (the planner's: a thread per share), after plan_tables
+// filled P.uf.  The same segments as plan_call's P7 builds for its own share.
+__device__ void plan_share_seq(const PlanIn& a, const CallPlan& P, const PlanShared& sh, int s, PlanCta& me) {
+    const int H = a.H, F = a.F, G = a.G, GM = a.gmax;
+    const int uf = P.uf[s], ue = P.uf[s + 1];
+    const int nseg = min(kSegPerCta, ue > uf ? (ue - 1) / F - uf / F + 1 : 0);
+    int stage = 0;
+    for (int k = 0; k < nseg; k++) {
+        const int g = uf / F + k, j = P.gjob[g], kind = P.jkind[j];
+        const int f0 = k == 0 ? uf % F : 0;
+        const int fend = g == (ue - 1) / F ? (ue - 1) % F + 1 : F;
+        const int r0 = (g - P.jg0[j]) * GM;
+        const int nt = min(GM, P.jp0[j + 1] - P.jp0[j] - r0);
+        Seg& sg = me.seg[k];
+        sg.src = P.jw1[j] + (size_t)f0 * unit_bytes(kind, H);
+        sg.sc = kind == kKindQ8 ? P.jsc[j] : nullptr;
+        sg.kind = kind;
+        sg.f0 = f0;
+        sg.nu = fend - f0;
+        sg.nt = nt;
+        sg.gidx = s * kSegPerCta + k;
+        sg.grp = g;
+        sg.pad0 = sg.pad1 = 0;
+        for (int i = 0; i < kGroupMax; i++) sg.tok[i] = P.ptok[P.jp0[j] + r0 + min(i, nt - 1)];
+        me.seg_stage[k] = stage;
+        const int ups = kind == kKindQ8 ? a.ups_q8 : a.ups_bf16;
+        stage += (sg.nu + ups - 1) / ups;
+    }
+    me.seg_stage[nseg] = stage;
+    me.nstage = stage;
+    me.nseg = nseg;
+    const int H4 = H / 4;
+    me.q0 = (int)((long long)s * H4 / G);
+    me.q1 = (int)((long long)(s + 1) * H4 / G);
+    (void)sh;
+}
+
 // The reduction's segment tables: every share's boundaries, segment counts and call-wide numbering,
 // then per call-wide segment its slot and rows and per group its segment range.  The nthr threads
 // with ids tid in [0, nthr) of named barrier `bar` take part; G <= kPlanMaxGrid.

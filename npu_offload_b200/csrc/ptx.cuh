@@ -126,6 +126,12 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // 16-byte load that bypasses L1 (data written by other SMs during this kernel).
 __device__ __forceinline__ uint4 ld_cg_u4(const void* p) {
     uint4 r;
