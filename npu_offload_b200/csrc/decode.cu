@@ -617,9 +617,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     setmaxnreg_inc<kConsRegs>();
     const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
     const unsigned long long cbase = (unsigned long long)a.epoch * (unsigned long long)G;
-    // the previous calls' reducers are done: their x / partial-sum / output accesses are complete
+    // the previous calls' reducers have staged their partial sums: the partial-sum buffer is free
+    // (their exchanges and output writes may still run: this call's reducers wait for those below)
     if (tid == 0) {
-        while (ld_acquire_gpu_u64(&a.cnt[1]) < cbase) {
+        while (ld_acquire_gpu_u64(&a.cnt[2]) < cbase) {
             if (timed_out(c, a.err, deadline)) break;
             __nanosleep(32);
         }
@@ -692,6 +693,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     }
     named_bar_sync(1, kCThreads);
     if (*(volatile int*)&c.abort_flag) {
+        if (tid == 0) atomicAdd(&a.cnt[2], 1ull);
         reducer_done();
         return;
     }
@@ -731,6 +733,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
                         if (i < rows) Q[(size_t)(r0 + i) * nq + q] = v[u][i];
                 }
             }
+        }
+    }
+    named_bar_sync(1, kCThreads);
+    if (tid == 0) {
+        atomicAdd(&a.cnt[2], 1ull);  // this reducer's partial sums are read: the next call may overwrite them
+        // outputs and the exchange buffer after the previous calls' reducers are done with theirs
+        while (ld_acquire_gpu_u64(&a.cnt[1]) < cbase) {
+            if (timed_out(c, a.err, deadline)) break;
+            __nanosleep(32);
         }
     }
     named_bar_sync(1, kCThreads);

@@ -91,10 +91,12 @@ struct DecodeArgs {
     float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
     float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums: block s * kSegPerCta + k
                            //   holds the k-th segment of CTA s's share
-    unsigned long long* cnt; // [2] monotonic over the context's fused calls: CTAs arrived, reducers finished.
-                             //   Call `epoch` on G CTAs owns the counts [epoch * G, (epoch + 1) * G): its
-                             //   CTAs wait for the previous calls to finish (cnt[1] >= epoch * G) before
-                             //   touching x, partial sums or outputs, so no grid ever waits for a planner
+    unsigned long long* cnt; // [3] monotonic over the context's fused calls: CTAs arrived, reducers finished,
+                             //   reducers that staged their partial sums.  Call `epoch` on G CTAs owns the
+                             //   counts [epoch * G, (epoch + 1) * G).  Its CTAs write partial sums once the
+                             //   previous calls' reducers staged theirs (cnt[2] >= epoch * G), and its
+                             //   reducers write outputs once those finished (cnt[1] >= epoch * G), so a
+                             //   call streams while the previous one exchanges and no grid waits for a planner
     int nred;              // reducing CTAs: the last nred CTAs to arrive reduce one output slice each
     uint32_t* err;
     uint32_t* err_host;    // optional host-mapped word: CTA 0 stores the error bits there when it exits

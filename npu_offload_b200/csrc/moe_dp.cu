@@ -126,7 +126,7 @@ struct moe_ctx {
     int64_t launches = 0;
     uint32_t latched = 0;
     // fused decode kernel state
-    unsigned long long* d_cnt = nullptr;  // [2] fused decode calls: CTAs arrived, reducers finished (monotonic)
+    unsigned long long* d_cnt = nullptr;  // [3] fused decode calls: arrived, reducers finished, partials staged
     float* d_part = nullptr;    // fused decode partial sums
     // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
     float* d_xbuf = nullptr;            // [2][world][kEpMaxT][H] this rank's receive buffer
@@ -212,7 +212,7 @@ void queue_err_readback(moe_ctx* c, cudaStream_t st) {
 // After a fused call gave up, its counts fall short: every call so far counts as finished.
 int reset_counters(moe_ctx* c) {
     const unsigned long long v = (unsigned long long)c->epoch * (unsigned long long)(c->sm_count - 1);
-    const unsigned long long h[2] = {v, v};
+    const unsigned long long h[3] = {v, v, v};
     CUDA_TRY(cudaMemcpy(c->d_cnt, h, sizeof(h), cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
     return MOE_OK;
@@ -611,14 +611,14 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
-    if (!st) st = dalloc(&c->d_cnt, 2);
+    if (!st) st = dalloc(&c->d_cnt, 3);
     if (!st) st = dalloc(&c->d_part, decode_part_floats(k.hidden, c->sm_count));
     if (!st) st = dalloc(&c->d_hctr, 2);
     if (!st) st = dalloc(reinterpret_cast<char**>(&c->d_pub), 4 * pub_plan_bytes());
     if (!st) st = dalloc(&c->d_pub_flag, 4);
     if (!st && cudaMemset(c->d_pub_flag, 0, 4 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
-    if (!st && cudaMemset(c->d_cnt, 0, sizeof(unsigned long long) * 2) != cudaSuccess)
+    if (!st && cudaMemset(c->d_cnt, 0, sizeof(unsigned long long) * 3) != cudaSuccess)
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && cudaMallocHost((void**)&c->h_errsnap, 16) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");

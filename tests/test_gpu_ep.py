@@ -13,6 +13,7 @@ import pytest
 import torch
 
 from tests.parity import assert_close
+from tests.test_gpu_block import _ulp_bf16, assert_bf16_close
 
 pytestmark = pytest.mark.gpu
 
@@ -148,7 +149,11 @@ def test_peer_exchange_two_gpus_matches_single_rank(mode):
         assert st == 0
         y, _ = Port.shared_expert(h2, x2, sg, su, sd)
         ref = Port.combine_residual(y, None, moe)
-        assert_close(bf2f(got[0][("block", T)]), bf2f(ref), what=f"ep2 {mode} moe_block_forward T={T}")
+        # x_next = bf16(y + moe): one rounding step of x_next and of y apart at most, plus the
+        # north-star bar of the routed output moe (max-abs 2e-2; with these weights, scale 0.05, one
+        # SwiGLU activation of ~50 rounding the other way moves it by ~0.01)
+        assert_bf16_close(got[0][("block", T)], ref, f"ep2 {mode} moe_block_forward T={T}", slack=_ulp_bf16(bf2f(y)),
+                          atol=2e-2)
     np.testing.assert_array_equal(got[0]["host_acc"], got[1]["host_acc"])
     x, lg = _inputs(3, 103)
     ref, _, _, _ = Port.moe_layer(x, lg, ex, K)
