@@ -442,47 +442,44 @@ __device__ bool run_segment_any(const DecodeArgs& a, Ctrl& c, const unsigned cha
 }
 
 // Cross-rank combine of output quads [q0, q0 + nq) of tokens [0, T) (see EpExchange): mine[t * nq + q]
-// holds this rank's sums in shared memory; out receives (accumulate ? out : 0) + the partials of
-// ranks 0..world-1 added in that order.  The nthr threads of named barrier 1 take part.  Returns
-// false when a rank's slice did not arrive in time (kErrTimeout raised, *abort set).
-__device__ bool ep_combine(const EpExchange& ep, const float4* mine, float* out, int T, int H, int q0, int nq, int s,
+// holds this rank's sums in shared memory; out receives (accumulate ? out : 0) + the partials of ranks
+// 0..world-1 added in that order.  The nthr threads of named barrier 1 take part.  Returns false when
+// a rank's values did not arrive in time (kErrTimeout raised, *abort set).
+__device__ bool ep_combine(const EpExchange& ep, const float4* mine, float* out, int T, int H, int q0, int nq,
                            int accumulate, uint32_t* err, uint64_t deadline, int nthr, int* abort) {
-    const int tid = threadIdx.x, W = ep.world, H4 = H / 4, par = ep.epoch & 1;
-    for (int f = tid; f < W * T * nq; f += nthr) {  // this rank's partial into every rank's buffer
-        const int q = f % nq, t = (f / nq) % T, r = f / (nq * T);
-        float4* dst = reinterpret_cast<float4*>(ep.peer_x[r]) + ((size_t)(par * W + ep.rank) * kEpMaxT + t) * H4 + q0 + q;
-        *dst = mine[t * nq + q];
+    const int tid = threadIdx.x, W = ep.world, par = ep.epoch & 1;
+    const int nv = nq * 4, ne = T * nv;  // values of the slice per token, of the slice
+    const uint64_t tag = (uint64_t)ep.epoch << 32;
+    const float* mv = reinterpret_cast<const float*>(mine);
+    for (int f = tid; f < W * ne; f += nthr) {  // this rank's values into every rank's buffer
+        const int r = f / ne, i = f - r * ne, t = i / nv, j = i - t * nv;
+        uint64_t* dst = ep.peer_x[r] + ((size_t)(par * W + ep.rank) * kEpMaxT + t) * H + 4 * q0 + j;
+        st_relaxed_sys_u64(dst, tag | __float_as_uint(mv[i]));
     }
-    __threadfence_system();
-    named_bar_sync(1, nthr);
-    if (tid < W) st_release_sys(ep.peer_flag[tid] + ep.rank * kPlanMaxGrid + s, ep.epoch);
-    if (tid < W) {
-        const uint32_t* f = ep.flag_local + tid * kPlanMaxGrid + s;
-        while (ld_acquire_sys(f) < ep.epoch) {
-            if (*(volatile int*)abort || globaltimer_ns() > deadline) {
-                atomicOr(err, kErrTimeout);
-                *(volatile int*)abort = 1;
-                break;
+    bool ok = true;
+    for (int i = tid; i < ne; i += nthr) {  // every rank adds the same values in rank order
+        const int t = i / nv, j = i - t * nv;
+        float* o = out + (size_t)t * H + 4 * q0 + j;
+        float acc = accumulate ? *o : 0.f;
+        for (int r = 0; r < W && ok; r++) {
+            const uint64_t* src = ep.x_local + ((size_t)(par * W + r) * kEpMaxT + t) * H + 4 * q0 + j;
+            uint64_t w = ld_relaxed_sys_u64(src);
+            for (int spin = 0; (uint32_t)(w >> 32) != ep.epoch; spin++) {
+                if ((spin & 31) == 31 && (*(volatile int*)abort || globaltimer_ns() > deadline)) {
+                    atomicOr(err, kErrTimeout);
+                    *(volatile int*)abort = 1;
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+                w = ld_relaxed_sys_u64(src);
             }
-            __nanosleep(64);
+            acc += __uint_as_float((uint32_t)w);
         }
+        if (ok) *o = acc;
     }
     named_bar_sync(1, nthr);
-    if (*(volatile int*)abort) return false;
-    for (int f = tid; f < T * nq; f += nthr) {  // every rank adds the same partials in rank order
-        const int q = f % nq, t = f / nq;
-        float4* o = reinterpret_cast<float4*>(out + (size_t)t * H) + q0 + q;
-        float4 acc = accumulate ? *o : make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < W; r++) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(ep.x_local) + ((size_t)(par * W + r) * kEpMaxT + t) * H4 + q0 + q);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
-        }
-        *o = acc;
-    }
-    return true;
+    return !*(volatile int*)abort;
 }
 
 template <int CH>
@@ -778,7 +775,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             mine[f] = acc;
         }
         named_bar_sync(1, kCThreads);
-        ep_combine(a.ep, mine, a.out, a.T, H, q0, nq, rr, a.accumulate, a.err, deadline, kCThreads, &c.abort_flag);
+        ep_combine(a.ep, mine, a.out, a.T, H, q0, nq, a.accumulate, a.err, deadline, kCThreads, &c.abort_flag);
         if (tl && tid == 0) tl[5] = globaltimer_ns();
         reducer_done();
         return;
@@ -923,7 +920,7 @@ __global__ void __launch_bounds__(256) ep_exchange_kernel(const EpExchange ep, c
         mine[f] = reinterpret_cast<const float4*>(part + (size_t)t * H)[q0 + q];
     }
     named_bar_sync(1, blockDim.x);
-    ep_combine(ep, mine, out, T, H, q0, nq, s, accumulate, err, globaltimer_ns() + timeout_ns, blockDim.x, &abort_flag);
+    ep_combine(ep, mine, out, T, H, q0, nq, accumulate, err, globaltimer_ns() + timeout_ns, blockDim.x, &abort_flag);
 }
 
 cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* out, int T, int H, int accumulate,

@@ -48,20 +48,18 @@ static_assert(sizeof(Seg) == 64, "Seg layout");
 static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0, "plan structs are 16-byte multiples");
 
 // Expert-parallel combine over NVLink peer memory.  Every rank owns an exchange buffer
-// x[2][world][kEpMaxT][H] fp32 (call parity, source rank, token) and flags[world][kPlanMaxGrid]
-// (source rank, output slice) holding the epoch of the latest slice a rank delivered.  For each
-// output slice s (the quads [s*H/4/G, (s+1)*H/4/G) that CTA s of every rank reduces) a rank stores
-// its partial into every rank's buffer, releases flags[me][s] there (system scope), waits until all
-// ranks' flags for s reach the epoch, and adds the partials in rank order -- every rank ends with
-// the same full output, bit for bit.  Buffers alternate by epoch parity, so a rank one call ahead
-// never overwrites data a slower rank still reads; flags only grow and are never reset.
+// x[2][world][kEpMaxT][H] of 64-bit words (call parity, source rank, token, element).  For each
+// output slice (the quads one reducing CTA owns, the same slicing on every rank) a rank stores every
+// value of its partial into every rank's buffer as one word {epoch, fp32 bits} -- an aligned 64-bit
+// store is single-copy atomic, so a reader polls each word until it carries the call's epoch, with no
+// fence and no flag (the low-latency protocol of NCCL's LL transport) -- and adds the ranks' values
+// in rank order: every rank ends with the same full output, bit for bit.  Buffers alternate by call
+// parity, so a rank one call ahead never overwrites words a slower rank still reads.
 constexpr int kEpMaxT = 64;     // tokens per exchange (longer calls exchange in chunks)
 constexpr int kEpMaxWorld = 8;  // ranks of one box
 struct EpExchange {
-    float* const* peer_x;          // [world] every rank's exchange buffer (peer pointers; own = local)
-    uint32_t* const* peer_flag;    // [world] every rank's flag array
-    const float* x_local;          // this rank's exchange buffer
-    const uint32_t* flag_local;    // this rank's flags
+    uint64_t* const* peer_x;       // [world] every rank's exchange buffer (peer pointers; own = local)
+    const uint64_t* x_local;       // this rank's exchange buffer
     int rank, world;
     uint32_t epoch;                // this call's exchange number (same on all ranks), >= 1
 };

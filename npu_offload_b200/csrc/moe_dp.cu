@@ -129,10 +129,8 @@ struct moe_ctx {
     unsigned long long* d_cnt = nullptr;  // [3] fused decode calls: arrived, reducers finished, partials staged
     float* d_part = nullptr;    // fused decode partial sums
     // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
-    float* d_xbuf = nullptr;            // [2][world][kEpMaxT][H] this rank's receive buffer
-    uint32_t* d_xflag = nullptr;        // [world][kPlanMaxGrid]
-    float** d_peer_x = nullptr;         // [kEpMaxWorld] device copy of every rank's buffer pointer
-    uint32_t** d_peer_flag = nullptr;   // [kEpMaxWorld]
+    uint64_t* d_xbuf = nullptr;         // [2][world][kEpMaxT][H] words {epoch, fp32}: this rank's receive buffer
+    uint64_t** d_peer_x = nullptr;      // [kEpMaxWorld] device copy of every rank's buffer pointer
     float* d_xpart = nullptr;           // multi-kernel path: this rank's partial before the exchange
     std::vector<void*> ipc_opened;      // peer mappings to close
     bool ep_attached = false;
@@ -337,9 +335,7 @@ EpExchange next_ep(moe_ctx* c) {
     EpExchange ep{};
     if (!c->ep_attached) return ep;
     ep.peer_x = c->d_peer_x;
-    ep.peer_flag = c->d_peer_flag;
     ep.x_local = c->d_xbuf;
-    ep.flag_local = c->d_xflag;
     ep.rank = c->cfg.ep_rank;
     ep.world = c->cfg.ep_world;
     ep.epoch = ++c->xepoch;
@@ -672,7 +668,7 @@ int moe_destroy(moe_ctx* c) {
                     (void*)c->d_tc_items, (void*)c->d_tc_cnt})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
-    for (void* q : {(void*)c->d_xbuf, (void*)c->d_xflag, (void*)c->d_peer_x, (void*)c->d_peer_flag, (void*)c->d_xpart})
+    for (void* q : {(void*)c->d_xbuf, (void*)c->d_peer_x, (void*)c->d_xpart})
         if (q) cudaFree(q);
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_errsnap) cudaFreeHost(c->h_errsnap);
@@ -1186,7 +1182,7 @@ namespace {
 constexpr uint32_t kEpMagic = 0x4D4F4550u;  // "MOEP"
 struct EpBlob {
     uint32_t magic, sm_count, world, rank;
-    cudaIpcMemHandle_t x, flag;
+    cudaIpcMemHandle_t x;
 };
 }  // namespace
 
@@ -1201,20 +1197,21 @@ int moe_ep_export(moe_ctx* c, void* out, int cap) {
     int st = MOE_OK;
     if (!c->d_xbuf) {
         if (!st) st = dalloc(&c->d_xbuf, (size_t)2 * W * kEpMaxT * H);
-        if (!st) st = dalloc(&c->d_xflag, (size_t)W * kPlanMaxGrid);
         if (!st) st = dalloc(&c->d_peer_x, (size_t)kEpMaxWorld);
-        if (!st) st = dalloc(&c->d_peer_flag, (size_t)kEpMaxWorld);
         if (!st) st = dalloc(&c->d_xpart, (size_t)kEpMaxT * H * ((c->cfg.max_tokens + kEpMaxT - 1) / kEpMaxT));
         if (st) return st;
-        CUDA_TRY(cudaMemset(c->d_xflag, 0, sizeof(uint32_t) * W * kPlanMaxGrid));
     }
+    // No word may carry an epoch of an earlier attachment (epochs restart at 1 on import).  Every rank
+    // exports before the records are exchanged and imports after, so clearing here precedes every
+    // rank's first call.
+    CUDA_TRY(cudaMemset(c->d_xbuf, 0, sizeof(uint64_t) * 2 * (size_t)W * kEpMaxT * H));
+    CUDA_TRY(cudaDeviceSynchronize());
     EpBlob b{};
     b.magic = kEpMagic;
     b.sm_count = (uint32_t)c->sm_count;
     b.world = (uint32_t)W;
     b.rank = (uint32_t)c->cfg.ep_rank;
     CUDA_TRY(cudaIpcGetMemHandle(&b.x, c->d_xbuf));
-    CUDA_TRY(cudaIpcGetMemHandle(&b.flag, c->d_xflag));
     memset(out, 0, MOE_EP_RECORD_BYTES);
     memcpy(out, &b, sizeof(b));
     return MOE_OK;
@@ -1225,8 +1222,7 @@ int moe_ep_import(moe_ctx* c, const void* blobs, int world) {
     if (!c->d_xbuf) return fail(MOE_ESTATE, "moe_ep_export must come first");
     if (world != c->cfg.ep_world) return fail(MOE_EINVAL, "world %d != ep_world %d", world, c->cfg.ep_world);
     DeviceGuard dg(c->dev);
-    std::vector<float*> px(kEpMaxWorld, nullptr);
-    std::vector<uint32_t*> pf(kEpMaxWorld, nullptr);
+    std::vector<uint64_t*> px(kEpMaxWorld, nullptr);
     for (int r = 0; r < world; r++) {
         EpBlob b;
         memcpy(&b, (const char*)blobs + (size_t)r * MOE_EP_RECORD_BYTES, sizeof(b));
@@ -1236,24 +1232,18 @@ int moe_ep_import(moe_ctx* c, const void* blobs, int world) {
             return fail(MOE_EINVAL, "rank %d has %u SMs, this GPU %d (the output slicing must agree)", r, b.sm_count, c->sm_count);
         if (r == c->cfg.ep_rank) {
             px[r] = c->d_xbuf;
-            pf[r] = c->d_xflag;
             continue;
         }
-        void *x = nullptr, *f = nullptr;
+        void* x = nullptr;
         cudaError_t e = cudaIpcOpenMemHandle(&x, b.x, cudaIpcMemLazyEnablePeerAccess);
-        if (e == cudaSuccess) e = cudaIpcOpenMemHandle(&f, b.flag, cudaIpcMemLazyEnablePeerAccess);
         if (e != cudaSuccess) {
             cudaGetLastError();
-            if (x) cudaIpcCloseMemHandle(x);
             return fail(MOE_ECOMM, "opening rank %d's exchange buffer: %s", r, cudaGetErrorString(e));
         }
         c->ipc_opened.push_back(x);
-        c->ipc_opened.push_back(f);
-        px[r] = static_cast<float*>(x);
-        pf[r] = static_cast<uint32_t*>(f);
+        px[r] = static_cast<uint64_t*>(x);
     }
-    CUDA_TRY(cudaMemcpy(c->d_peer_x, px.data(), sizeof(float*) * kEpMaxWorld, cudaMemcpyHostToDevice));
-    CUDA_TRY(cudaMemcpy(c->d_peer_flag, pf.data(), sizeof(uint32_t*) * kEpMaxWorld, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(c->d_peer_x, px.data(), sizeof(uint64_t*) * kEpMaxWorld, cudaMemcpyHostToDevice));
     c->ep_attached = true;
     c->xepoch = 0;
     return MOE_OK;

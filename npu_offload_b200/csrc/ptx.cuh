@@ -132,6 +132,16 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
     return v;
 }
 
+// Relaxed system-scope 64-bit store / load (words another GPU reads or writes over NVLink).
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // 16-byte load that bypasses L1 (data written by other SMs during this kernel).
 __device__ __forceinline__ uint4 ld_cg_u4(const void* p) {
     uint4 r;
