@@ -242,7 +242,7 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *   MOE_OPT_RING_STAGES         tuning: cap on the fused kernel's shared-memory ring depth (2..16;
  *                               0 = as deep as shared memory allows, the default).
  *   MOE_OPT_STAGE_BYTES         tuning: target bytes per ring stage of the fused kernel (a stage holds
- *                               max(1, target / unit bytes) units; 0 = the default, 32 KiB).
+ *                               max(1, target / unit bytes) units; 0 = the default, 48 KiB).
  *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 8) run the expert FFN as
  *                               grouped tensor-core GEMMs (each routed expert read once) when every
  *                               local expert of the layer is bf16; smaller batches, and layers holding
@@ -262,7 +262,25 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *   MOE_OPT_SHARED_INTER        intermediate size of the shared expert (moe_load_shared), set before its
  *                               first load; 0 (the default) = the context's inter.  A context holding a
  *                               slice of every routed expert's units (inter = the slice) still loads the
- *                               whole shared expert: set this to its full width. */
+ *                               whole shared expert: set this to its full width.
+ *   MOE_OPT_Q8_UNIT_COST        tuning: how much of the fused kernel's stream one int8 unit counts for
+ *                               when a call's units are cut into per-CTA shares, per mille of its bytes
+ *                               (500..4000; 0 = the default, 2500).  Shares are balanced by this cost
+ *                               rather than by bytes, because dequantising an int8 unit takes longer
+ *                               per byte than streaming it.
+ *   MOE_OPT_REDUCERS            tuning: in a stream of fused calls (a device-buffer call whose planner
+ *                               finds the previous call still running), how many CTAs (the last to
+ *                               finish their share) reduce the partial sums into the output; the others
+ *                               leave at once and the next call's CTAs take their SMs.  Raised as
+ *                               needed so that a reducer's slice of the partial sums fits on chip
+ *                               (default 48).  Calls made alone, host-buffer calls and block calls use
+ *                               every CTA.  0: every call uses every CTA and even shares, so output
+ *                               bits never depend on timing (otherwise a streamed call's shares, and
+ *                               with them the fp32 summation order, differ from a lone call's).
+ *   MOE_OPT_LATE_BYTES          tuning: in a stream of fused calls, the last CTAs by index (as many as
+ *                               reduce), which start only when the previous call's reducers leave
+ *                               their SMs, get shares smaller by this many bytes of the bf16 stream
+ *                               (default 688128, 28 Solar units). */
 #define MOE_OPT_FUSED_DECODE 1
 #define MOE_OPT_WAIT_TIMEOUT_US 2
 #define MOE_OPT_INJECT_WAIT_TIMEOUT 3
@@ -273,6 +291,9 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 #define MOE_OPT_PREFILL_TC 8
 #define MOE_OPT_LAYER_SLOTS 9
 #define MOE_OPT_SHARED_INTER 10
+#define MOE_OPT_Q8_UNIT_COST 11
+#define MOE_OPT_REDUCERS 12
+#define MOE_OPT_LATE_BYTES 13
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
 /* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see

@@ -51,6 +51,12 @@ __host__ __device__ __forceinline__ size_t unit_pitch(int kind, int H) {
 __host__ __device__ __forceinline__ size_t unit_bytes(int kind, int H) {
     return kind == kKindQ8 ? (size_t)3 * H + 16 : (size_t)6 * H;
 }
+// Planning cost of one unit, in bytes of the bf16 stream: a bf16 unit costs its bytes; an int8 unit
+// costs q8_cost (its bytes are half, but its dequantising dots take longer per byte, so a byte
+// balance would leave the CTAs holding int8 units last to finish).
+__host__ __device__ __forceinline__ long long unit_cost(int kind, int H, int q8_cost) {
+    return kind == kKindQ8 ? (long long)q8_cost : (long long)6 * H;
+}
 
 // Element offsets of gate row f and up row f inside w1.
 __host__ __device__ __forceinline__ size_t gate_row(const ExpDesc& d, int f, int H, int F) {

@@ -53,6 +53,11 @@ static_assert(4 * 32 * kProdRegs + 8 * 32 * kConsRegs <= kDecThreads * 168, "reg
 constexpr int kMaxNS = 16;
 constexpr size_t kSmemCap = 227 * 1024;
 constexpr uint32_t kStageTarget = 49152;  // default bytes per ring stage
+// Default planning cost of an int8 unit, per mille of its bytes: the consumers spend about as long on
+// an int8 unit's dequantising dots as on streaming a bf16 unit (measured on B200 at the Solar shape,
+// batch 1, a layer of 96 int8 and 32 bf16 experts: 66.1 us per layer with shares cut by bytes, 49.6 us
+// at 2500).
+constexpr int kQ8CostDefault = 2500;
 constexpr int kBatch = 4;  // units per exchange (a batch may span ring stages)
 // Exchange buffers.  A warp writes buffer k % kXB for batch k + kXB after its exchange wait for batch
 // k + kXB - 1, i.e. after every warp arrived for that batch; each warp arrives for batch k + 1 only
@@ -542,13 +547,30 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             }
         }
     }
-    if (tid == 0) c.use_pub = a.pub && ld_acquire_gpu(a.pub_flag) == a.stamp;
+    // A call with a planner always takes the published plan (only the planner may cut late shares,
+    // so every CTA of the call must see its cut); a call without one plans in every CTA.
+    if (tid == 0) {
+        c.use_pub = 0;
+        if (a.pub) {
+            const uint64_t dl = globaltimer_ns() + a.timeout_ns;
+            while (ld_acquire_gpu(a.pub_flag) != a.stamp) {
+                if (globaltimer_ns() > dl) {
+                    c.abort_flag = 1;
+                    atomicOr(a.err, kErrTimeout);
+                    break;
+                }
+                __nanosleep(64);
+            }
+            c.use_pub = 1;
+        }
+    }
     __syncthreads();  // also makes the barrier initialisation visible
     if (c.abort_flag) {  // the inputs never arrived: write nothing, the call reports MOE_ETIMEOUT
         snapshot_err();
         return;
     }
     if (c.use_pub) {  // the planner got ahead: this CTA's share, as published
+        if (tl && tid == 0) tl[6] = 1;  // (timeline: marks a published plan; plan_call stamps slot 6 otherwise)
         const int4* src = reinterpret_cast<const int4*>(&a.pub->cta[s]);
         int4* dst = reinterpret_cast<int4*>(&c.me);
         for (int q = tid; q < (int)(sizeof(PlanCta) / 16); q += kDecThreads) dst[q] = __ldcg(src + q);
@@ -571,6 +593,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         pin.gmax = a.gmax;
         pin.ups_bf16 = a.ups_bf16;
         pin.ups_q8 = a.ups_q8;
+        pin.q8_cost = a.q8_cost;
+        pin.nlate = 0;  // CTAs that plan for themselves cannot know whether the previous call still runs:
+        pin.late_cost = 0;  // even shares, every CTA reduces
+        pin.nred = G;
         // the planning scratch aliases the ring: no copy is issued before plan_call returns
         plan_call(pin, c.P, *reinterpret_cast<PlanScratch*>(ring), c.sh, c.me, tl);
     }
@@ -614,10 +640,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     setmaxnreg_inc<kConsRegs>();
     const uint64_t deadline = globaltimer_ns() + a.timeout_ns;
     const unsigned long long cbase = (unsigned long long)a.epoch * (unsigned long long)G;
-    // the previous calls' reducers have staged their partial sums: the partial-sum buffer is free
-    // (their exchanges and output writes may still run: this call's reducers wait for those below)
+    // Partial sums alternate between two buffers by call parity (the host passes call e's buffer).
+    // Call e - 2, the last user of this call's buffer, has staged its partial sums
+    // (cnt[2] >= (e - 1) * G): the buffer is free.  The previous call may still be arriving and
+    // reducing (this call's reducers wait for it below).
+    float* const part = a.part;
     if (tid == 0) {
-        while (ld_acquire_gpu_u64(&a.cnt[2]) < cbase) {
+        const unsigned long long free_at = cbase >= (unsigned long long)G ? cbase - (unsigned long long)G : 0ull;
+        while (ld_acquire_gpu_u64(&a.cnt[2]) < free_at) {
             if (timed_out(c, a.err, deadline)) break;
             __nanosleep(32);
         }
@@ -644,29 +674,45 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     // A CTA whose partial sums are written takes a ticket and, unless it is among the last nred to
     // arrive, exits at once: its SM is free for the next call (whose CTAs plan and start their weight
     // stream while this call's reduction finishes).  Reducer r owns output quads [r*H/4/nred, ...).
+    // Arrival counts alternate by call parity (cnt[0] even calls, cnt[3] odd calls): a CTA of the next
+    // call can finish its share before a straggler of this call arrives.  Call e owns the counts
+    // [(e / 2) * G, (e / 2 + 1) * G) of its counter.
+    unsigned long long* const arr = &a.cnt[(a.epoch & 1) ? 3 : 0];
+    const unsigned long long abase = (unsigned long long)(a.epoch >> 1) * (unsigned long long)G;
     __threadfence();
     named_bar_sync(1, kCThreads);
-    if (tid == 0) c.ticket = ok && !*(volatile int*)&c.abort_flag ? (int)(atomicAdd(&a.cnt[0], 1ull) - cbase) : -1;
+    if (tid == 0) c.ticket = ok && !*(volatile int*)&c.abort_flag ? (int)(atomicAdd(arr, 1ull) - abase) : -1;
     named_bar_sync(1, kCThreads);
-    const int NR = a.nred, tk = c.ticket;
+    const int NR = min(max(c.me.nred, 1), G), tk = c.ticket;
     if (tk < 0) {  // gave up (its error is raised): leave the error bits for host callers
         if (tid == 0) griddep_wait();
         if (a.err_host && tid == 0) *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
         return;
     }
-    if (tk < G - NR) {
-        if (tid == 0) griddep_wait();
+    // Every CTA of a call adds one to cnt[2] (partial sums read, or none to read) and one to cnt[1]
+    // (outputs written, or none to write); the CTA that completes cnt[1] leaves the call's error bits
+    // for host callers.
+    auto count_finished = [&]() {
+        if (atomicAdd(&a.cnt[1], 1ull) == cbase + (unsigned long long)(G - 1) && a.err_host)
+            *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+    };
+    if (tk < G - NR) {  // not a reducer: its SM is free for the next call
+        if (tid == 0) {
+            atomicAdd(&a.cnt[2], 1ull);
+            griddep_wait();  // this grid completes after its predecessor (the call's planner)
+            count_finished();
+        }
         if (tl && tid == 0) tl[4] = tl[5] = globaltimer_ns();
         return;
     }
     const int rr = tk - (G - NR);
-    // the last reducer to finish leaves the call's error bits for host callers
     auto reducer_done = [&]() {
         __threadfence();  // this reducer's outputs before its count (the next call waits for the count)
         named_bar_sync(1, kCThreads);
-        if (tid == 0) griddep_wait();  // this grid completes after its predecessor (the call's planner)
-        if (tid == 0 && atomicAdd(&a.cnt[1], 1ull) == cbase + (unsigned long long)(NR - 1) && a.err_host)
-            *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+        if (tid == 0) {
+            griddep_wait();  // this grid completes after its predecessor (the call's planner)
+            count_finished();
+        }
     };
     // the reduction's segment tables (the same in every CTA) while the last CTAs arrive: published
     // with the plan, or built here
@@ -681,9 +727,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         plan_tables(c.P, c.sh, G, a.F, a.H, a.gmax, tid, kCThreads, 1);
     }
     named_bar_sync(1, kCThreads);
+
     if (tid == 0) {
-        const unsigned long long target = cbase + (unsigned long long)G + (a.inject_timeout ? 1ull : 0ull);
-        while (!*(volatile int*)&c.abort_flag && ld_acquire_gpu_u64(&a.cnt[0]) < target) {
+        const unsigned long long target = abase + (unsigned long long)G + (a.inject_timeout ? 1ull : 0ull);
+        while (!*(volatile int*)&c.abort_flag && ld_acquire_gpu_u64(arr) < target) {
             if (timed_out(c, a.err, deadline)) break;
             __nanosleep(32);
         }
@@ -714,7 +761,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
                 if (f < ntask) {
                     const int k = f / nq, q = f % nq, rows = c.sh.segrows[k];
                     const float4* src =
-                        reinterpret_cast<const float4*>(a.part + (size_t)c.P.segslot[k] * kGroupMax * H) + q0 + q;
+                        reinterpret_cast<const float4*>(part + (size_t)c.P.segslot[k] * kGroupMax * H) + q0 + q;
 #pragma unroll
                     for (int i = 0; i < kGroupMax; i++)
                         if (i < rows) v[u][i] = __ldcg(src + (size_t)i * H4);
@@ -856,6 +903,7 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     const size_t ubf = unit_bytes(kKindBF16, a.H), uq = unit_bytes(kKindQ8, a.H);
     a.ups_bf16 = (int)std::max<size_t>(1, target / ubf);
     a.ups_q8 = (int)std::max<size_t>(1, target / uq);
+    if (a.q8_cost <= 0) a.q8_cost = (int)(uq * kQ8CostDefault / 1000);
     const size_t slot = up128(std::max(a.ups_bf16 * ubf, a.ups_q8 * uq));
     a.slot_bytes = (uint32_t)slot;
     const size_t ctrl = up128(sizeof(Ctrl));
@@ -883,11 +931,22 @@ bool plan_decode(DecodeArgs& a, int grid, size_t* smem_bytes) {
     // extra segment per share boundary.  (Letting only the last CTAs to arrive reduce, so that the
     // others free their SMs early, measured slower: the next call's CTAs that land on the reducers'
     // SMs start late with full-size shares and become its stragglers.)
+    // Reducers: the requested count (a.nred on entry; 0 = every CTA) raised until a reducer's slice
+    // of the partial sums fits the ring.  With fewer reducers than CTAs the last nred CTAs by index
+    // get shares smaller by a.late_cost (requested on entry): in a stream of calls they take the SMs
+    // of the previous call's reducers and start that much later.
     const size_t npt = (size_t)np + a.T;
     const size_t rows = npt + (size_t)(grid - 1) * std::min(a.gmax, a.T);
-    const size_t nqr = (size_t)(a.H / 4 + grid - 1) / grid;
-    a.nred = (rows * nqr + npt * nqr + (size_t)a.T * nqr) * 16 <= (size_t)ns * slot ? grid : 0;
-    if (a.nred == 0 || sizeof(PlanScratch) > (size_t)ns * slot) return false;
+    auto fits = [&](int nr) {
+        const size_t nqr = (size_t)(a.H / 4 + nr - 1) / nr;
+        return (rows * nqr + npt * nqr + (size_t)a.T * nqr) * 16 <= (size_t)ns * slot;
+    };
+    int nr = a.nred > 0 ? std::min(a.nred, grid) : grid;
+    while (nr < grid && !fits(nr)) nr++;
+    if (!fits(nr) || sizeof(PlanScratch) > (size_t)ns * slot) return false;
+    a.nred = nr;
+    a.nlate = nr < grid ? nr : 0;
+    if (a.nlate == 0 || a.late_cost < 0) a.late_cost = 0;
     a.NS = ns;
     *smem_bytes = ctrl + (size_t)ns * slot;
     return true;
@@ -970,6 +1029,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) planner_kernel(const DecodeArg
     pin.gmax = a.gmax;
     pin.ups_bf16 = a.ups_bf16;
     pin.ups_q8 = a.ups_q8;
+    pin.q8_cost = a.q8_cost;
+    // Late shares only when the previous call is still running: then the last CTAs of this call start
+    // when its reducers leave their SMs.  (A call whose inputs come from the previous call's outputs
+    // is planned after that call finished: every CTA starts at once and shares stay even.)
+    const bool prev_running = a.epoch > 0 && ld_acquire_gpu_u64(&a.cnt[1]) < (unsigned long long)a.epoch * (unsigned long long)G;
+    pin.nlate = prev_running ? a.nlate : 0;
+    pin.late_cost = prev_running ? a.late_cost : 0;
+    pin.nred = prev_running ? a.nred : G;  // fewer reducers free SMs for the next call; alone, all reduce
     plan_call(pin, m.P, m.R, m.sh, m.me);
     plan_tables(m.P, m.sh, G, a.F, a.H, a.gmax, tid, kDecThreads, 1);
     named_bar_sync(1, kDecThreads);

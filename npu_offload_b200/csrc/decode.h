@@ -11,6 +11,12 @@ constexpr int kMaxGroups = kDecodeMaxPairs;
 constexpr int kPlanMaxGrid = 256;  // largest decode grid
 constexpr int kSegPerCta = 8;      // segments (runs of one token group's units) per decode CTA
 constexpr int kMaxSegTotal = kPlanMaxGrid + kMaxGroups;  // segments of one call: <= grid + groups
+// Fused decode defaults: reducing CTAs (0 = every CTA) and how much smaller (in bf16 stream bytes)
+// the shares of the CTAs that start when the previous call's reducers leave their SMs are.  Measured
+// on B200 at the Solar shape, back-to-back layers: batch 1 49.5 -> 43.8 us per layer against every
+// CTA reducing (flat within 1 us for 32-64 reducers and 24-40 units), batch 4 124 -> 98 us.
+constexpr int kReducersDefault = 48;
+constexpr long long kLateBytesDefault = 28 * 24576;
 constexpr int kTimelineSlots = 16;  // per-CTA stamps recorded when DecodeArgs::timeline is set
 constexpr int kStageLogMax = 1024;  // stages of CTA 0 recorded in DecodeArgs::stage_log
 
@@ -27,7 +33,8 @@ struct __align__(16) Seg {
 struct __align__(16) PlanCta {
     int nseg, nstage, q0, q1;          // segments, ring stages, output quads [q0, q1) of H/4
     int seg_stage[kSegPerCta + 1];     // first ring stage of each segment
-    int pad[3];
+    int nred;                          // the call's reducing CTAs (the last nred to arrive)
+    int pad[2];
     Seg seg[kSegPerCta];
 };
 
@@ -87,15 +94,24 @@ struct DecodeArgs {
     uint32_t* hctr;
     const uint16_t* x;     // [T, H] bf16
     float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
-    float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums: block s * kSegPerCta + k
-                           //   holds the k-th segment of CTA s's share
-    unsigned long long* cnt; // [3] monotonic over the context's fused calls: CTAs arrived, reducers finished,
-                             //   reducers that staged their partial sums.  Call `epoch` on G CTAs owns the
-                             //   counts [epoch * G, (epoch + 1) * G).  Its CTAs write partial sums once the
-                             //   previous calls' reducers staged theirs (cnt[2] >= epoch * G), and its
-                             //   reducers write outputs once those finished (cnt[1] >= epoch * G), so a
-                             //   call streams while the previous one exchanges and no grid waits for a planner
-    int nred;              // reducing CTAs: the last nred CTAs to arrive reduce one output slice each
+    float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums of this call (one of two
+                           //   buffers, by call parity): block s * kSegPerCta + k holds the k-th segment
+                           //   of CTA s's share
+    unsigned long long* cnt; // [4] monotonic over the context's fused calls: [0] / [3] CTAs arrived (even /
+                             //   odd calls; call e owns [(e/2) * G, (e/2 + 1) * G) of its counter),
+                             //   [1] CTAs finished (outputs written, or none to write), [2] CTAs past their
+                             //   partial-sum reads.  Call e on G CTAs owns [e * G, (e + 1) * G) of [1] and
+                             //   [2].  Its CTAs write partial sums once call e - 2 staged its own
+                             //   (cnt[2] >= (e - 1) * G), and its reducers write outputs once call e - 1
+                             //   finished (cnt[1] >= e * G), so a call streams while the previous one
+                             //   reduces and exchanges, and no grid waits for a planner
+    int nred;              // streamed calls' reducing CTAs: the last nred CTAs to arrive reduce one output
+                           //   slice each, the others exit at once, freeing their SMs for the next call.
+                           //   The planner applies it (PlanCta::nred) when it finds the previous call
+                           //   still running; every other call reduces on all CTAs
+    int nlate;             // streamed calls: the last nlate CTAs (by index) get shares smaller by
+                           //   late_cost: they start when the previous call's reducers leave their SMs
+    long long late_cost;   // (unit_cost units)
     uint32_t* err;
     uint32_t* err_host;    // optional host-mapped word: CTA 0 stores the error bits there when it exits
     int T, E, K, H, F, scoring, accumulate;
@@ -112,6 +128,8 @@ struct DecodeArgs {
     uint64_t* stage_log;   // optional [3][kStageLogMax] issue / landed / released stamps of CTA 0's stages
     int ns_cap;            // tuning: cap on ring stages (0 = as many as shared memory allows)
     uint32_t stage_target; // tuning: target bytes per ring stage (0 = default)
+    int q8_cost;           // planning cost of one int8 unit in bf16-stream bytes (0 = default,
+                           //   kQ8CostDefault per mille of the unit's bytes)
     EpExchange ep;         // cross-rank combine (ep.world > 1 with peers attached), else world = 0
     // block calls (plan with a shared expert): instead of out, x_next = bf16((y + extra) + routed)
     // with y = bf16(x2 + shared); y_out (optional) receives y; extra may be null
@@ -146,6 +164,7 @@ cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* o
                                uint32_t* err, uint64_t timeout_ns, int grid, cudaStream_t st);
 
 // Partial-sum floats the decode path needs for hidden size H on a grid of G CTAs.
+// Floats of one partial-sum buffer (a context holds two, used by alternate calls).
 inline size_t decode_part_floats(int H, int G) { return (size_t)G * kSegPerCta * kGroupMax * H; }
 
 }  // namespace moe

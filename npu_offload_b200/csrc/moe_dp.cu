@@ -126,8 +126,9 @@ struct moe_ctx {
     int64_t launches = 0;
     uint32_t latched = 0;
     // fused decode kernel state
-    unsigned long long* d_cnt = nullptr;  // [3] fused decode calls: arrived, reducers finished, partials staged
-    float* d_part = nullptr;    // fused decode partial sums
+    unsigned long long* d_cnt = nullptr;  // [4] fused decode calls: arrived (even calls), finished, past their
+                                          //   partial-sum reads, arrived (odd calls)
+    float* d_part = nullptr;    // fused decode partial sums: two buffers, used by alternate calls
     // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
     uint64_t* d_xbuf = nullptr;         // [2][world][kEpMaxT][H] words {epoch, fp32}: this rank's receive buffer
     uint64_t** d_peer_x = nullptr;      // [kEpMaxWorld] device copy of every rank's buffer pointer
@@ -165,6 +166,9 @@ struct moe_ctx {
     uint64_t* d_timeline = nullptr;  // [sm_count][kTimelineSlots] when MOE_OPT_TIMELINE is on
     int ns_cap = 0;
     uint32_t stage_target = 0;  // fused kernel bytes per ring stage (0: default)
+    int q8_cost_pm = 0;         // planning cost of an int8 unit, per mille of its bytes (0: default)
+    int reducers = kReducersDefault;     // fused decode: CTAs that reduce (0: all)
+    long long late_bytes = kLateBytesDefault;  // fused decode: share reduction of the late CTAs
     // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_ev;  // kProfMarks events per profiled call
@@ -209,8 +213,9 @@ void queue_err_readback(moe_ctx* c, cudaStream_t st) {
 
 // After a fused call gave up, its counts fall short: every call so far counts as finished.
 int reset_counters(moe_ctx* c) {
-    const unsigned long long v = (unsigned long long)c->epoch * (unsigned long long)(c->sm_count - 1);
-    const unsigned long long h[3] = {v, v, v};
+    const unsigned long long G = (unsigned long long)(c->sm_count - 1), e = c->epoch;
+    const unsigned long long v = e * G;
+    const unsigned long long h[4] = {(e + 1) / 2 * G, v, v, e / 2 * G};  // even calls so far, all, all, odd calls
     CUDA_TRY(cudaMemcpy(c->d_cnt, h, sizeof(h), cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
     return MOE_OK;
@@ -364,6 +369,9 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
     da.stage_log = c->d_timeline ? reinterpret_cast<uint64_t*>(c->d_timeline + (size_t)c->sm_count * kTimelineSlots) : nullptr;
     da.ns_cap = c->ns_cap;
     da.stage_target = c->stage_target;
+    da.q8_cost = c->q8_cost_pm ? (int)(unit_bytes(kKindQ8, da.H) * (size_t)c->q8_cost_pm / 1000) : 0;
+    da.nred = c->reducers;
+    da.late_cost = c->late_bytes;
     return plan_decode(da, dgrid, dsmem);
 }
 
@@ -375,6 +383,7 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     const int E = c->cfg.n_experts, dgrid = c->sm_count - 1;
     da.ep = next_ep(c);
     da.epoch = c->epoch++;
+    da.part = c->d_part + (size_t)(da.epoch & 1) * decode_part_floats(c->cfg.hidden, c->sm_count);
     da.bias = c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr;
     da.desc = c->d_desc + (size_t)layer * E;
     da.shared = shared;
@@ -607,14 +616,14 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_hidden, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
-    if (!st) st = dalloc(&c->d_cnt, 3);
-    if (!st) st = dalloc(&c->d_part, decode_part_floats(k.hidden, c->sm_count));
+    if (!st) st = dalloc(&c->d_cnt, 4);
+    if (!st) st = dalloc(&c->d_part, 2 * decode_part_floats(k.hidden, c->sm_count));
     if (!st) st = dalloc(&c->d_hctr, 2);
     if (!st) st = dalloc(reinterpret_cast<char**>(&c->d_pub), 4 * pub_plan_bytes());
     if (!st) st = dalloc(&c->d_pub_flag, 4);
     if (!st && cudaMemset(c->d_pub_flag, 0, 4 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
-    if (!st && cudaMemset(c->d_cnt, 0, sizeof(unsigned long long) * 3) != cudaSuccess)
+    if (!st && cudaMemset(c->d_cnt, 0, sizeof(unsigned long long) * 4) != cudaSuccess)
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && cudaMallocHost((void**)&c->h_errsnap, 16) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
@@ -1271,6 +1280,9 @@ static int ensure_shared(moe_ctx* c) {
     s->prefill_tc = c->prefill_tc;
     s->ns_cap = c->ns_cap;
     s->stage_target = c->stage_target;
+    s->q8_cost_pm = c->q8_cost_pm;
+    s->reducers = c->reducers;
+    s->late_bytes = c->late_bytes;
     const size_t NT = c->cfg.max_tokens, H = c->cfg.hidden, E = c->cfg.n_experts;
     if (!st) st = dalloc(&c->d_blk_zero, NT);
     if (!st) st = dalloc(&c->d_blk_logits, NT * E);
@@ -1502,6 +1514,19 @@ static int set_option_one(moe_ctx* c, int option, int64_t value) {
         case MOE_OPT_STAGE_BYTES:
             if (value < 0 || value > 196608) return fail(MOE_EINVAL, "stage bytes %lld not in [0,196608]", (long long)value);
             c->stage_target = (uint32_t)value;
+            return MOE_OK;
+        case MOE_OPT_Q8_UNIT_COST:
+            if (value != 0 && (value < 500 || value > 4000))
+                return fail(MOE_EINVAL, "int8 unit cost %lld not 0 or in [500,4000] per mille", (long long)value);
+            c->q8_cost_pm = (int)value;
+            return MOE_OK;
+        case MOE_OPT_REDUCERS:
+            if (value < 0 || value > kPlanMaxGrid) return fail(MOE_EINVAL, "reducers %lld not in [0,%d]", (long long)value, kPlanMaxGrid);
+            c->reducers = (int)value;
+            return MOE_OK;
+        case MOE_OPT_LATE_BYTES:
+            if (value < 0 || value > (64ll << 20)) return fail(MOE_EINVAL, "late bytes %lld not in [0, 64 MiB]", (long long)value);
+            c->late_bytes = value;
             return MOE_OK;
         case MOE_OPT_TIMELINE: {
             DeviceGuard dg(c->dev);

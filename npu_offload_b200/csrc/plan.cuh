@@ -42,13 +42,15 @@ struct __align__(16) CallPlan {
     int jg0[kPlanJobs + 1];                 // group offsets of the jobs
     const unsigned char* jw1[kPlanJobs];    // unit 0 of the job's table
     const float* jsc[kPlanJobs];            // int8 scales (null for bf16)
-    long long jb0[kPlanJobs + 1];           // unit-stream bytes of the jobs before job j
+    long long jb0[kPlanJobs + 1];           // unit-stream cost (unit_cost) of the jobs before job j
     int gjob[kMaxGroups];                   // job of group g
     int uf[kPlanMaxGrid + 1];               // first unit of every share (uf[G] = all units)
     int nseg[kPlanMaxGrid];                 // segments of every share
     int seg0[kPlanMaxGrid + 1];             // call-wide index of every share's first segment
     int segslot[kMaxSegTotal];              // partial-sum slot (s * kSegPerCta + k) of call-wide segment i
-    int nj, np, ngrp, pad;
+    int nj, np, ngrp, q8c;                  // q8c: planning cost of an int8 unit (unit_cost)
+    long long late_cost;                    // the last nlate shares are smaller by this cost
+    int nlate, pad2;
 };
 
 // Scratch of the planning steps; aliases the ring (no weight copy is issued before the plan exists).
@@ -79,22 +81,42 @@ struct PlanIn {
     float* w_out;          // [T, K] router weights, or null
     uint32_t* err;
     int T, E, K, H, F, scoring, G, gmax, ups_bf16, ups_q8;
+    int q8_cost;           // planning cost of an int8 unit in bf16-stream bytes (unit_cost)
+    int nlate;             // the last nlate CTAs' shares are smaller by late_cost (they start late)
+    long long late_cost;
+    int nred;              // the call's reducing CTAs (PlanCta::nred)
 };
 
-// First unit of share ss: the first unit starting at or after byte ss * total / G of the stream.
+// Cost at which share ss starts.  Shares 0 .. G - nlate - 1 get cost S each, the last nlate shares
+// max(0, S - late) each, with S chosen so that the shares add up to the total (costs: unit_cost, i.e.
+// bytes for bf16 units).  With nlate == 0 this is ss * total / G.
+__device__ __forceinline__ long long plan_share_start(long long total, int ss, int G, int nlate, long long late) {
+    if (nlate <= 0 || late <= 0) return (long long)ss * total / G;
+    const int ne = G - nlate;  // early shares
+    // S >= late: G*S - nlate*late = total; else the late shares are empty and ne*S = total
+    if (total + (long long)nlate * late >= (long long)G * late) {
+        const long long num = total + (long long)nlate * late;  // G * S
+        const long long lo = (long long)min(ss, ne) * num / G;
+        if (ss <= ne) return lo;
+        return (long long)ss * num / G - (long long)(ss - ne) * late;
+    }
+    return ss >= ne ? total : (long long)ss * total / ne;
+}
+
+// First unit of share ss: the first unit starting at or after the share's starting cost.
 __device__ __forceinline__ int plan_unit_at(const CallPlan& P, int ss, int G, int F, int H) {
     const int nj = P.nj;
     const long long total = P.jb0[nj];
     if (ss >= G || total <= 0) return P.jg0[nj] * F;
-    const long long B = (long long)ss * total / G;
+    const long long B = plan_share_start(total, ss, G, P.nlate, P.late_cost);
     int lo = 0, hi = nj - 1;  // job j with jb0[j] <= B < jb0[j+1]
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (P.jb0[mid] <= B) lo = mid;
         else hi = mid - 1;
     }
-    const long long ub = (long long)unit_bytes(P.jkind[lo], H);
-    const long long off = B - P.jb0[lo];  // < the job's bytes
+    const long long ub = unit_cost(P.jkind[lo], H, P.q8c);
+    const long long off = B - P.jb0[lo];  // < the job's cost
     return P.jg0[lo] * F + (int)((off + ub - 1) / ub);
 }
 
@@ -265,7 +287,7 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             const unsigned msk = __ballot_sync(0xffffffffu, local);
             const int n = local ? R.counts[e] : 0;
             const int ngj = (n + GM - 1) / GM;
-            const long long bj = local ? (long long)ngj * F * (long long)unit_bytes(kind, H) : 0;
+            const long long bj = local ? (long long)ngj * F * unit_cost(kind, H, a.q8_cost) : 0;
             int incl = n, gincl = ngj;
             long long bincl = bj;
 #pragma unroll
@@ -306,7 +328,7 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
                 P.jb0[nj] = nb;
                 sh.sp0 = np;
                 if (d.kind != kKindBF16 && d.kind != kKindQ8 && s == 0) atomicOr(a.err, kErrBadExpert);
-                nb += (long long)((T + GM - 1) / GM) * F * (long long)unit_bytes(d.kind, H);
+                nb += (long long)((T + GM - 1) / GM) * F * unit_cost(d.kind, H, a.q8_cost);
                 nj++;
                 np += T;
                 ng += (T + GM - 1) / GM;
@@ -314,6 +336,9 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             P.nj = nj;
             P.np = np;
             P.ngrp = ng;
+            P.q8c = a.q8_cost;
+            P.nlate = a.nlate;
+            P.late_cost = a.late_cost;
             P.jp0[nj] = np;
             P.jg0[nj] = ng;
             P.jb0[nj] = nb;
@@ -405,6 +430,7 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             if (ue > uf && (ue - 1) / F - uf / F + 1 > kSegPerCta) atomicOr(a.err, kErrBadIndex);  // never expected
             if (nseg == 0) me.seg_stage[0] = me.nstage = 0;
             me.nseg = nseg;
+            me.nred = a.nred;
             const int H4 = H / 4;
             me.q0 = (int)((long long)s * H4 / G);
             me.q1 = (int)((long long)(s + 1) * H4 / G);
@@ -455,6 +481,7 @@ __device__ void plan_share_seq(const PlanIn& a, const CallPlan& P, const PlanSha
     me.seg_stage[nseg] = stage;
     me.nstage = stage;
     me.nseg = nseg;
+    me.nred = a.nred;
     const int H4 = H / 4;
     me.q0 = (int)((long long)s * H4 / G);
     me.q1 = (int)((long long)(s + 1) * H4 / G);
