@@ -253,12 +253,16 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               fp32); 0: they stay on the CUDA-core multi-kernel path.
  *   MOE_OPT_LAYER_SLOTS         HBM expert slots per layer for layers not yet loaded (0, the default:
  *                               one per local expert); see moe_evict_expert.
- *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 16
+ *   MOE_OPT_TIMELINE            instrumentation: 1 records, per CTA of the latest fused launch, 24
  *                               globaltimer / cycle slots (0 start, 1 plan share loaded, 2 all stages
  *                               issued, 3 all segments done, 4 grid-wide arrival seen, 5 reduction
  *                               done; for consumer warp 0, SM cycles (8) waiting for ring stages,
- *                               (9) working on them, (10) of which in the cross-warp exchange) and
- *                               CTA 0's per-stage stamps; read them with moe_timeline_read.
+ *                               (9) working on them, (10) of which in the cross-warp exchange; when
+ *                               the CTA plans: 16 plan decision made, 17 logits and expert table
+ *                               loaded, 18 top-k chosen, 6 routed, 7 jobs, 15 pairs and share), the
+ *                               planner kernel's stamps in the row after the grid's (0 start,
+ *                               1 planned, 2 published, 3 predecessor complete) and CTA 0's per-stage
+ *                               stamps; read them with moe_timeline_read.
  *   MOE_OPT_SHARED_INTER        intermediate size of the shared expert (moe_load_shared), set before its
  *                               first load; 0 (the default) = the context's inter.  A context holding a
  *                               slice of every routed expert's units (inter = the slice) still loads the
@@ -294,9 +298,10 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
 #define MOE_OPT_Q8_UNIT_COST 11
 #define MOE_OPT_REDUCERS 12
 #define MOE_OPT_LATE_BYTES 13
+#define MOE_OPT_PLANNER 14
 MOE_API int moe_set_option(moe_ctx* ctx, int option, int64_t value);
 
-/* Copies up to cap stamps to host memory (synchronises): [SM count][16] per-CTA stamps (see
+/* Copies up to cap stamps to host memory (synchronises): [SM count][24] per-CTA stamps (see
  * MOE_OPT_TIMELINE) followed by CTA 0's per-stage issue / landed / released stamps ([3][1024]). */
 MOE_API int moe_timeline_read(moe_ctx* ctx, uint64_t* out, int cap);
 

@@ -18,6 +18,7 @@ MOE_KIND_NONE, MOE_KIND_BF16, MOE_KIND_Q8 = 0, 1, 2
 MOE_OPT_FUSED_DECODE, MOE_OPT_WAIT_TIMEOUT_US, MOE_OPT_INJECT_WAIT_TIMEOUT, MOE_OPT_TIMELINE = 1, 2, 3, 4
 MOE_OPT_RING_STAGES, MOE_OPT_STAGE_BYTES, MOE_OPT_PREFILL_MIN_T, MOE_OPT_PREFILL_TC = 5, 6, 7, 8
 MOE_OPT_LAYER_SLOTS, MOE_OPT_SHARED_INTER, MOE_OPT_Q8_UNIT_COST, MOE_OPT_REDUCERS, MOE_OPT_LATE_BYTES = 9, 10, 11, 12, 13
+MOE_OPT_PLANNER = 14
 MOE_EP_RECORD_BYTES = 256
 
 STATUS_NAMES = {0: "MOE_OK", 1: "MOE_EINVAL", 2: "MOE_ENONFINITE", 3: "MOE_ECUDA", 4: "MOE_ENOMEM",

@@ -594,9 +594,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         pin.ups_bf16 = a.ups_bf16;
         pin.ups_q8 = a.ups_q8;
         pin.q8_cost = a.q8_cost;
-        pin.nlate = 0;  // CTAs that plan for themselves cannot know whether the previous call still runs:
-        pin.late_cost = 0;  // even shares, every CTA reduces
-        pin.nred = G;
+        pin.nlate = a.nlate;  // applied when the call is streamed (the previous call's reducers hold SMs)
+        pin.late_cost = a.late_cost;
+        pin.nred = a.nred;
+        pin.decide = a.decide;
+        pin.cnt1 = &a.cnt[1];
+        pin.epoch = a.epoch;
         // the planning scratch aliases the ring: no copy is issued before plan_call returns
         plan_call(pin, c.P, *reinterpret_cast<PlanScratch*>(ring), c.sh, c.me, tl);
     }
@@ -734,6 +737,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             if (timed_out(c, a.err, deadline)) break;
             __nanosleep(32);
         }
+    } else if (tid == 32) {
+        // meanwhile: the previous calls' reducers are done with the outputs and the exchange buffer
+        // (this call writes them only after staging, below)
+        while (!*(volatile int*)&c.abort_flag && ld_acquire_gpu_u64(&a.cnt[1]) < cbase) {
+            if (globaltimer_ns() > deadline) {
+                *(volatile int*)&c.abort_flag = 1;
+                atomicOr(a.err, kErrTimeout);
+                break;
+            }
+            __nanosleep(32);
+        }
     }
     named_bar_sync(1, kCThreads);
     if (*(volatile int*)&c.abort_flag) {
@@ -780,15 +794,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         }
     }
     named_bar_sync(1, kCThreads);
-    if (tid == 0) {
-        atomicAdd(&a.cnt[2], 1ull);  // this reducer's partial sums are read: the next call may overwrite them
-        // outputs and the exchange buffer after the previous calls' reducers are done with theirs
-        while (ld_acquire_gpu_u64(&a.cnt[1]) < cbase) {
-            if (timed_out(c, a.err, deadline)) break;
-            __nanosleep(32);
-        }
-    }
-    named_bar_sync(1, kCThreads);
+    if (tid == 0) atomicAdd(&a.cnt[2], 1ull);  // this reducer's partial sums are read: the next call may overwrite them
     for (int f = tid; f < np * nq; f += kCThreads) {
         const int p = f / nq, q = f % nq, g = min(max(c.sh.pgrp[p], 0), kMaxGroups - 1);
         const int row = min(max(c.sh.prow[p], 0), kGroupMax - 1);
@@ -991,13 +997,14 @@ cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* o
 }
 
 // The planner: one CTA computes the whole plan of a call with the decode CTAs' own code and
-// publishes it (st.release of the stamp).  It lets its decode grid launch at once, and before exiting
-// it waits for its own predecessor grid; its decode grid waits for it only as its last step, so the
-// completion of a decode grid implies that of every grid before it in the stream while no decode
-// CTA's start waits for a planner.  The planner runs on the SM the decode grid leaves free.  Plans
-// rotate over four buffers: a decode grid reads its plan before its reducers finish, and a call's
-// CTAs wait for the previous call's reducers, so the planner of call e + 4 never meets a grid still
-// reading plan e.
+// publishes it (st.release of the stamp); it lets its decode grid launch at once and runs on the SM
+// that grid leaves free, while the previous call still streams.  Before exiting it waits for its
+// predecessor grid: that keeps the spare SM from the decode CTAs (measured: a planner that leaves at
+// once hands its SM to a decode CTA, and the next planner starts late), and the completion of a
+// decode grid implies that of every grid before it in the stream.  Plans rotate over four buffers:
+// the planner of call e + 4 starts only once every CTA of call e + 3 started, i.e. once the CTAs of
+// call e + 2 left their SMs, each after waiting for call e to finish staging its partial sums; plan e
+// is read before that.
 struct __align__(16) PlannerSmem {
     CallPlan P;
     PlanShared sh;
@@ -1011,6 +1018,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) planner_kernel(const DecodeArg
     PlannerSmem& m = *reinterpret_cast<PlannerSmem*>(psm);
     const int tid = threadIdx.x;
     if (tid == 0) griddep_launch_dependents();
+    // optional stamps in the timeline row after the decode grid's: 0 start, 1 planned, 2 published,
+    // 3 predecessor complete
+    uint64_t* ptl = a.timeline ? a.timeline + (size_t)G * kTimelineSlots : nullptr;
+    if (ptl && tid == 0) ptl[0] = globaltimer_ns();
     PlanIn pin;
     pin.logits = a.logits;
     pin.bias = a.bias;
@@ -1037,17 +1048,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) planner_kernel(const DecodeArg
     pin.nlate = prev_running ? a.nlate : 0;
     pin.late_cost = prev_running ? a.late_cost : 0;
     pin.nred = prev_running ? a.nred : G;  // fewer reducers free SMs for the next call; alone, all reduce
+    pin.decide = nullptr;                  // decided here
+    pin.cnt1 = nullptr;
+    pin.epoch = a.epoch;
     plan_call(pin, m.P, m.R, m.sh, m.me);
+    if (ptl && tid == 0) ptl[1] = globaltimer_ns();
     plan_tables(m.P, m.sh, G, a.F, a.H, a.gmax, tid, kDecThreads, 1);
     named_bar_sync(1, kDecThreads);
-    for (int ss = tid; ss < G; ss += kDecThreads) {  // every share, straight to the published plan
-        PlanCta pc;
-        plan_share_seq(pin, m.P, m.sh, ss, pc);
-        const int4* src = reinterpret_cast<const int4*>(&pc);
-        int4* dst = reinterpret_cast<int4*>(&out->cta[ss]);
-        const int n16 = (int)((offsetof(PlanCta, seg) + (size_t)pc.nseg * sizeof(Seg)) / 16);
-        for (int q = 0; q < n16; q++) dst[q] = src[q];
-    }
+    for (int ss = tid >> 5; ss < G; ss += kDecThreads / 32)  // every share, a warp each, straight to the plan
+        plan_share_warp(pin, m.P, ss, &out->cta[ss]);
     {
         const int4* s1 = reinterpret_cast<const int4*>(&m.P);
         int4* d1 = reinterpret_cast<int4*>(&out->P);
@@ -1060,7 +1069,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) planner_kernel(const DecodeArg
     __syncthreads();
     if (tid == 0) {
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(stamp) : "memory");
-        griddep_wait();  // complete only after the preceding grid (see above)
+        if (ptl) ptl[2] = globaltimer_ns();
+        griddep_wait();  // hold this SM until the preceding grid completes (see above)
+        if (ptl) ptl[3] = globaltimer_ns();
     }
 }
 

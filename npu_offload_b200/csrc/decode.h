@@ -16,8 +16,9 @@ constexpr int kMaxSegTotal = kPlanMaxGrid + kMaxGroups;  // segments of one call
 // on B200 at the Solar shape, back-to-back layers: batch 1 49.5 -> 43.8 us per layer against every
 // CTA reducing (flat within 1 us for 32-64 reducers and 24-40 units), batch 4 124 -> 98 us.
 constexpr int kReducersDefault = 48;
+constexpr bool kPlannerDefault = true;
 constexpr long long kLateBytesDefault = 28 * 24576;
-constexpr int kTimelineSlots = 16;  // per-CTA stamps recorded when DecodeArgs::timeline is set
+constexpr int kTimelineSlots = 24;  // per-CTA stamps recorded when DecodeArgs::timeline is set
 constexpr int kStageLogMax = 1024;  // stages of CTA 0 recorded in DecodeArgs::stage_log
 
 // One segment: units [f0, f0 + nu) of one token group's expert, a contiguous run of the unit table.
@@ -105,6 +106,9 @@ struct DecodeArgs {
                              //   (cnt[2] >= (e - 1) * G), and its reducers write outputs once call e - 1
                              //   finished (cnt[1] >= e * G), so a call streams while the previous one
                              //   reduces and exchanges, and no grid waits for a planner
+    unsigned long long* decide; // [4] calls planned in every CTA: word e % 4 holds (e << 8) | streamed, set by
+                                //   the first CTA of call e (compare-and-swap) from whether call e - 1 was still
+                                //   running, so every CTA cuts the same shares
     int nred;              // streamed calls' reducing CTAs: the last nred CTAs to arrive reduce one output
                            //   slice each, the others exit at once, freeing their SMs for the next call.
                            //   The planner applies it (PlanCta::nred) when it finds the previous call

@@ -126,6 +126,7 @@ struct moe_ctx {
     int64_t launches = 0;
     uint32_t latched = 0;
     // fused decode kernel state
+    unsigned long long* d_decide = nullptr;  // [4] fused decode: per-call share-cut decisions (call mod 4)
     unsigned long long* d_cnt = nullptr;  // [4] fused decode calls: arrived (even calls), finished, past their
                                           //   partial-sum reads, arrived (odd calls)
     float* d_part = nullptr;    // fused decode partial sums: two buffers, used by alternate calls
@@ -168,6 +169,7 @@ struct moe_ctx {
     uint32_t stage_target = 0;  // fused kernel bytes per ring stage (0: default)
     int q8_cost_pm = 0;         // planning cost of an int8 unit, per mille of its bytes (0: default)
     int reducers = kReducersDefault;     // fused decode: CTAs that reduce (0: all)
+    bool use_planner = kPlannerDefault;  // fused decode: a planner kernel per device-buffer call
     long long late_bytes = kLateBytesDefault;  // fused decode: share reduction of the late CTAs
     // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
     bool prof_on = false;
@@ -355,6 +357,7 @@ bool prepare_fused(moe_ctx* c, int T, int flags, DecodeArgs& da, size_t* dsmem) 
     da = DecodeArgs{};
     da.part = c->d_part;
     da.cnt = c->d_cnt;
+    da.decide = c->d_decide;
     da.err = c->d_err;
     da.T = T;
     da.E = c->cfg.n_experts;
@@ -403,7 +406,7 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     da.pub_flag = nullptr;
     da.stamp = da.epoch + 1;
     cudaError_t e = cudaSuccess;
-    if (!x_host && planner) {  // the planner publishes the plan if it gets ahead of the decode CTAs
+    if (!x_host && planner && c->use_planner) {  // a planner kernel publishes the call's plan
         PubPlan* pub = reinterpret_cast<PubPlan*>(reinterpret_cast<char*>(c->d_pub) + (da.epoch & 3) * pub_plan_bytes());
         uint32_t* flag = c->d_pub_flag + (da.epoch & 3);
         e = launch_planner(da, dgrid, pub, flag, da.stamp, st);
@@ -617,6 +620,8 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     if (!st) st = dalloc(&c->d_logits, (size_t)k.max_tokens * E);
     if (!st) st = dalloc(&c->d_out, (size_t)k.max_tokens * k.hidden);
     if (!st) st = dalloc(&c->d_cnt, 4);
+    if (!st) st = dalloc(&c->d_decide, 4);
+    if (!st && cudaMemset(c->d_decide, 0, 4 * sizeof(unsigned long long)) != cudaSuccess) st = fail(MOE_ECUDA, "memset failed");
     if (!st) st = dalloc(&c->d_part, 2 * decode_part_floats(k.hidden, c->sm_count));
     if (!st) st = dalloc(&c->d_hctr, 2);
     if (!st) st = dalloc(reinterpret_cast<char**>(&c->d_pub), 4 * pub_plan_bytes());
@@ -671,7 +676,7 @@ int moe_destroy(moe_ctx* c) {
     void* ps[] = {c->d_desc, c->d_bias, c->d_idx, c->d_w, c->d_counts, c->d_offsets, c->d_perm, c->d_jobord,
                   c->d_nj, c->d_nlj, c->d_ptok, c->d_pw, c->d_pairpos, c->d_comb_off, c->d_comb_p, c->d_jobs,
                   c->d_act, c->d_y, c->d_err, c->d_hidden, c->d_logits, c->d_out, c->d_cnt, c->d_hctr,
-                  c->d_part, c->d_route_scratch, c->d_pub, c->d_pub_flag};
+                  c->d_part, c->d_route_scratch, c->d_pub, c->d_pub_flag, c->d_decide};
     for (void* p : ps) cudaFree(p);
     for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_yf, (void*)c->d_tc_sched,
                     (void*)c->d_tc_items, (void*)c->d_tc_cnt})
@@ -1282,6 +1287,7 @@ static int ensure_shared(moe_ctx* c) {
     s->stage_target = c->stage_target;
     s->q8_cost_pm = c->q8_cost_pm;
     s->reducers = c->reducers;
+    s->use_planner = c->use_planner;
     s->late_bytes = c->late_bytes;
     const size_t NT = c->cfg.max_tokens, H = c->cfg.hidden, E = c->cfg.n_experts;
     if (!st) st = dalloc(&c->d_blk_zero, NT);
@@ -1519,6 +1525,9 @@ static int set_option_one(moe_ctx* c, int option, int64_t value) {
             if (value != 0 && (value < 500 || value > 4000))
                 return fail(MOE_EINVAL, "int8 unit cost %lld not 0 or in [500,4000] per mille", (long long)value);
             c->q8_cost_pm = (int)value;
+            return MOE_OK;
+        case MOE_OPT_PLANNER:
+            c->use_planner = value != 0;
             return MOE_OK;
         case MOE_OPT_REDUCERS:
             if (value < 0 || value > kPlanMaxGrid) return fail(MOE_EINVAL, "reducers %lld not in [0,%d]", (long long)value, kPlanMaxGrid);

@@ -70,6 +70,7 @@ struct __align__(16) PlanScratch {
     uint32_t tokmask[kMaxExperts];
     int jmap[kMaxExperts];
     int bad;
+    int streamed;                                      // the call's share-cut decision (PlanIn::decide)
 };
 
 struct PlanIn {
@@ -85,7 +86,29 @@ struct PlanIn {
     int nlate;             // the last nlate CTAs' shares are smaller by late_cost (they start late)
     long long late_cost;
     int nred;              // the call's reducing CTAs (PlanCta::nred)
+    // Calls planned in every CTA: decide (non-null) holds one word per call (call mod 4),
+    // (epoch << 8) | streamed, set by compare-and-swap by the first CTA to decide from whether call
+    // epoch - 1 still runs (cnt1 < epoch * G).  Streamed calls use nlate / late_cost / nred, the
+    // others even shares on every reducing CTA.  With decide null the values apply as given.
+    unsigned long long* decide;
+    const unsigned long long* cnt1;
+    unsigned long long epoch;
 };
+
+// The call's share-cut decision (PlanIn::decide): two global round trips, made by one thread while
+// the other warps route.
+__device__ __forceinline__ int plan_decide(unsigned long long* dw, const unsigned long long* cnt1,
+                                          unsigned long long epoch, int G) {
+    const unsigned long long tagged = epoch << 8;
+    unsigned long long v = atomicAdd(dw, 0ull);
+    const bool pr = epoch > 0 && ld_acquire_gpu_u64(cnt1) < epoch * (unsigned long long)G;
+    const unsigned long long mine = tagged | (pr ? 1ull : 0ull);
+    for (int tries = 0; (v & ~0xffull) != tagged && tries < 64; tries++) {
+        const unsigned long long old = atomicCAS(dw, v, mine);
+        v = old == v ? mine : old;
+    }
+    return (v & ~0xffull) == tagged ? (int)(v & 1ull) : 0;
+}
 
 // Cost at which share ss starts.  Shares 0 .. G - nlate - 1 get cost S each, the last nlate shares
 // max(0, S - late) each, with S chosen so that the shares add up to the total (costs: unit_cost, i.e.
@@ -135,9 +158,16 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
         if (tl && tid == 0) tl[i] = globaltimer_ns();
     };
 
+    // The routing steps P0-P2 run on warps 0 .. kNW - 2 (named barrier 2); the last warp makes the
+    // call's share-cut decision meanwhile.
+    constexpr int NWP = kNW - 1, TPP = NWP * 32;
+    if (warp == NWP) {
+        if (lane == 0) R.streamed = a.decide ? plan_decide(a.decide + (a.epoch & 3), a.cnt1, a.epoch, G) : 1;
+        if (tl && lane == 0) tl[16] = globaltimer_ns();
+    } else {
     // ---- P0: one global round trip: logits (a warp per token, which also takes the max) and the
     // layer's expert table into shared memory ----
-    for (int t = warp; t < T; t += kNW) {
+    for (int t = warp; t < T; t += NWP) {
         float m = -INFINITY;  // f32::max fold: NaN never replaces the running max
         for (int i = lane; i < E; i += 32) {
             const float v = a.logits[(size_t)t * E + i];
@@ -151,7 +181,7 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
         }
         if (lane == 0) R.mx[t] = m;
     }
-    for (int e = tid; e < E; e += kPlanThr) {
+    for (int e = tid; e < E; e += TPP) {
         const ExpDesc d = a.desc[e];
         R.dw1[e] = d.w1;
         R.dsc[e] = d.sc;
@@ -162,10 +192,11 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
         R.jmap[e] = -1;
     }
     if (tid == 0) R.bad = 0;
-    __syncthreads();
+    named_bar_sync(2, TPP);
+    stamp(17);
 
     // ---- P1: per (token, 32-expert slice): softmax numerators, or sigmoid values and keys ----
-    for (int it = warp; it < NIT; it += kNW) {
+    for (int it = warp; it < NIT; it += NWP) {
         const int t = it / S32, i = (it % S32) * 32 + lane;
         if (i >= E) continue;
         if (softmax) {
@@ -178,11 +209,11 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             R.ck[t][i] = ((unsigned long long)ordered_bits(k != k ? -INFINITY : k) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)i);
         }
     }
-    __syncthreads();
+    named_bar_sync(2, TPP);
 
     // ---- P2: a warp per token: (softmax) the sequential sum in index order, probabilities and keys;
     // then the top K by key ("larger value first, ties to the lower index") ----
-    for (int t = warp; t < T; t += kNW) {
+    for (int t = warp; t < T; t += NWP) {
         constexpr int SM = kMaxExperts / 32;
         unsigned long long key[SM];
         if (softmax) {
@@ -249,7 +280,12 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             }
         }
     }
+    }  // routing warps
     __syncthreads();
+    stamp(18);
+    const bool streamed = R.streamed != 0;
+    const int nlate = streamed ? a.nlate : 0, nred = streamed ? a.nred : G;
+    const long long late_cost = streamed ? a.late_cost : 0;
 
     // ---- P4: per pair (t, k): renormalised weight (sum in k order), grouping counts ----
     for (int q = tid; q < NP; q += kPlanThr) {
@@ -337,8 +373,8 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             P.np = np;
             P.ngrp = ng;
             P.q8c = a.q8_cost;
-            P.nlate = a.nlate;
-            P.late_cost = a.late_cost;
+            P.nlate = nlate;
+            P.late_cost = late_cost;
             P.jp0[nj] = np;
             P.jg0[nj] = ng;
             P.jb0[nj] = nb;
@@ -430,7 +466,7 @@ __device__ void plan_call(const PlanIn& a, CallPlan& P, PlanScratch& R, PlanShar
             if (ue > uf && (ue - 1) / F - uf / F + 1 > kSegPerCta) atomicOr(a.err, kErrBadIndex);  // never expected
             if (nseg == 0) me.seg_stage[0] = me.nstage = 0;
             me.nseg = nseg;
-            me.nred = a.nred;
+            me.nred = nred;
             const int H4 = H / 4;
             me.q0 = (int)((long long)s * H4 / G);
             me.q1 = (int)((long long)(s + 1) * H4 / G);
@@ -450,20 +486,22 @@ struct __align__(16) PubPlan {
     PlanCta cta[kPlanMaxGrid];
 };
 
-// Share s's segments, built by one thread (the planner's: a thread per share), after plan_tables
-// filled P.uf.  The same segments as plan_call's P7 builds for its own share.
-__device__ void plan_share_seq(const PlanIn& a, const CallPlan& P, const PlanShared& sh, int s, PlanCta& me) {
+// Share s's segments written straight to `out` by one warp (the planner's: a warp per share), lane k
+// building segment k, after plan_tables filled P.uf.  The same segments as plan_call's P7 builds
+// for its own share.
+__device__ void plan_share_warp(const PlanIn& a, const CallPlan& P, int s, PlanCta* out) {
+    const int lane = threadIdx.x & 31;
     const int H = a.H, F = a.F, G = a.G, GM = a.gmax;
     const int uf = P.uf[s], ue = P.uf[s + 1];
     const int nseg = min(kSegPerCta, ue > uf ? (ue - 1) / F - uf / F + 1 : 0);
-    int stage = 0;
-    for (int k = 0; k < nseg; k++) {
-        const int g = uf / F + k, j = P.gjob[g], kind = P.jkind[j];
+    int nst = 0;  // ring stages of this lane's segment
+    if (lane < nseg) {
+        const int k = lane, g = uf / F + k, j = P.gjob[g], kind = P.jkind[j];
         const int f0 = k == 0 ? uf % F : 0;
         const int fend = g == (ue - 1) / F ? (ue - 1) % F + 1 : F;
         const int r0 = (g - P.jg0[j]) * GM;
         const int nt = min(GM, P.jp0[j + 1] - P.jp0[j] - r0);
-        Seg& sg = me.seg[k];
+        Seg sg;
         sg.src = P.jw1[j] + (size_t)f0 * unit_bytes(kind, H);
         sg.sc = kind == kKindQ8 ? P.jsc[j] : nullptr;
         sg.kind = kind;
@@ -473,19 +511,28 @@ __device__ void plan_share_seq(const PlanIn& a, const CallPlan& P, const PlanSha
         sg.gidx = s * kSegPerCta + k;
         sg.grp = g;
         sg.pad0 = sg.pad1 = 0;
+#pragma unroll
         for (int i = 0; i < kGroupMax; i++) sg.tok[i] = P.ptok[P.jp0[j] + r0 + min(i, nt - 1)];
-        me.seg_stage[k] = stage;
+        out->seg[k] = sg;
         const int ups = kind == kKindQ8 ? a.ups_q8 : a.ups_bf16;
-        stage += (sg.nu + ups - 1) / ups;
+        nst = (sg.nu + ups - 1) / ups;
     }
-    me.seg_stage[nseg] = stage;
-    me.nstage = stage;
-    me.nseg = nseg;
-    me.nred = a.nred;
-    const int H4 = H / 4;
-    me.q0 = (int)((long long)s * H4 / G);
-    me.q1 = (int)((long long)(s + 1) * H4 / G);
-    (void)sh;
+    int incl = nst;  // stage prefix over the segments
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane <= nseg) out->seg_stage[lane] = incl - nst;  // lane nseg: the total
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+        out->nseg = nseg;
+        out->nstage = total;
+        out->nred = a.nred;
+        const int H4 = H / 4;
+        out->q0 = (int)((long long)s * H4 / G);
+        out->q1 = (int)((long long)(s + 1) * H4 / G);
+    }
 }
 
 // The reduction's segment tables: every share's boundaries, segment counts and call-wide numbering,

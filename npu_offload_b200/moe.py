@@ -348,13 +348,13 @@ class MoEDataPlane:
         check(lib().moe_set_option(self._h, int(option), int(value)))
 
     def timeline(self):
-        """Per-CTA phase stamps of the latest fused launch (MOE_OPT_TIMELINE on): [SMs, 16] ns."""
+        """Per-CTA phase stamps of the latest fused launch (MOE_OPT_TIMELINE on): [SMs, 24] ns."""
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        n = sms * 16 + 3 * 1024
+        n = sms * 24 + 3 * 1024
         buf = np.zeros(n, np.uint64)
         check(lib().moe_timeline_read(self._h, buf.ctypes.data_as(ctypes.c_void_p), n))
-        self.stage_log = buf[sms * 16:].reshape(3, 1024)
-        return buf[:sms * 16].reshape(-1, 16)
+        self.stage_log = buf[sms * 24:].reshape(3, 1024)
+        return buf[:sms * 24].reshape(-1, 24)
 
     def profile(self, enable=True):
         check(lib().moe_profile(self._h, int(bool(enable))))
