@@ -523,7 +523,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     // (griddepcontrol.wait) first: host calls here, the consumers before their first segment.
     if (a.x_src) {  // host call: each CTA moves a slice of the pinned inputs to the device
         griddep_wait();
-        if (s == 0 && tid == 0) a.hctr[par ^ 1] = 0;  // the previous call's counter, for the next call
         const int nx = a.T * a.H / 8, nl = a.T * a.E;
         const int x0 = (int)((long long)s * nx / G), x1 = (int)((long long)(s + 1) * nx / G);
         const int l0 = (int)((long long)s * nl / G), l1 = (int)((long long)(s + 1) * nl / G);
@@ -534,10 +533,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         for (int i = l0 + tid; i < l1; i += kDecThreads) ld[i] = a.lg_src[i];
         __threadfence();
         __syncthreads();
+        // every CTA plans from the device copy of the logits: wait for every slice (reading the pinned
+        // logits from every CTA instead queues 147 CTAs' reads on the host link: ~20 us, measured)
         if (tid == 0) {
-            atomicAdd(&a.hctr[par], 1u);
+            atomicAdd(a.hctr, 1u);
             const uint64_t dl = globaltimer_ns() + a.timeout_ns;
-            while (ld_acquire_gpu(&a.hctr[par]) < (uint32_t)G) {
+            while ((int)(ld_acquire_gpu(a.hctr) - (a.hbase + (uint32_t)G)) < 0) {
                 if (globaltimer_ns() > dl) {
                     c.abort_flag = 1;
                     atomicOr(a.err, kErrTimeout);
@@ -696,8 +697,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     // (outputs written, or none to write); the CTA that completes cnt[1] leaves the call's error bits
     // for host callers.
     auto count_finished = [&]() {
-        if (atomicAdd(&a.cnt[1], 1ull) == cbase + (unsigned long long)(G - 1) && a.err_host)
+        if (atomicAdd(&a.cnt[1], 1ull) == cbase + (unsigned long long)(G - 1) && a.err_host) {
+            // host callers: the error bits, then the call's completion tag (every CTA's outputs were
+            // made visible system-wide before its count)
             *(volatile uint32_t*)a.err_host = atomicOr(a.err, 0u);
+            __threadfence_system();
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.err_host + 1), "r"(a.epoch + 1u) : "memory");
+        }
     };
     if (tk < G - NR) {  // not a reducer: its SM is free for the next call
         if (tid == 0) {
@@ -710,7 +716,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     }
     const int rr = tk - (G - NR);
     auto reducer_done = [&]() {
-        __threadfence();  // this reducer's outputs before its count (the next call waits for the count)
+        // this reducer's outputs before its count (the next call waits for the count; for host
+        // callers the CTA that counts last fences at system scope before the completion tag, which
+        // covers every output ordered before its count)
+        __threadfence();
         named_bar_sync(1, kCThreads);
         if (tid == 0) {
             griddep_wait();  // this grid completes after its predecessor (the call's planner)
@@ -794,6 +803,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
         }
     }
     named_bar_sync(1, kCThreads);
+    if (tl && tid == 0) tl[19] = globaltimer_ns();
     if (tid == 0) atomicAdd(&a.cnt[2], 1ull);  // this reducer's partial sums are read: the next call may overwrite them
     for (int f = tid; f < np * nq; f += kCThreads) {
         const int p = f / nq, q = f % nq, g = min(max(c.sh.pgrp[p], 0), kMaxGroups - 1);

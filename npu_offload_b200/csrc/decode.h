@@ -89,10 +89,12 @@ struct DecodeArgs {
     int32_t* idx_out;      // [T, K] router indices (written by CTA 0), or null
     float* w_out;          // [T, K] router weights, or null
     // host calls: pinned host sources the CTAs copy (a slice each) into x / logits before routing;
-    // hctr [2] counts the CTAs whose slice is in place (parity double-buffered like ctr)
+    // hctr counts, over the context's host calls, the CTAs whose slice is in place: this call's
+    // slices are all in once it reaches hbase + G (wrapping 32-bit arithmetic)
     const uint16_t* x_src;
     const float* lg_src;
     uint32_t* hctr;
+    uint32_t hbase;
     const uint16_t* x;     // [T, H] bf16
     float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
     float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums of this call (one of two
@@ -117,7 +119,8 @@ struct DecodeArgs {
                            //   late_cost: they start when the previous call's reducers leave their SMs
     long long late_cost;   // (unit_cost units)
     uint32_t* err;
-    uint32_t* err_host;    // optional host-mapped word: CTA 0 stores the error bits there when it exits
+    uint32_t* err_host;    // optional host-mapped words: [0] the call's error bits, [1] its completion tag
+                           //   (epoch + 1), stored (release, system scope) by the CTA that finishes last
     int T, E, K, H, F, scoring, accumulate;
     uint32_t epoch;        // call counter: selects the counter parity
     int NS;                // ring stages

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -157,7 +158,9 @@ struct moe_ctx {
     uint16_t* d_blk_y = nullptr;        // [max_tokens, H] y = bf16(x2 + shared)
     uint16_t* d_blk_io = nullptr;       // [3][max_tokens, H] host-buffer calls: h2, x2, x_next
     float* d_blk_extra = nullptr;       // [max_tokens, H] host-buffer calls: extra
-    uint32_t* d_hctr = nullptr;     // [2] host calls: CTAs whose slice of the inputs is on the device
+    uint32_t* d_hctr = nullptr;     // [2] host calls: [0] CTAs whose slice of the inputs is on the device,
+                                    //   counted over the context's host calls
+    uint32_t hcalls = 0;            // host fused calls launched since the count was last cleared
     PubPlan* d_pub = nullptr;       // [4] plans published by the planner kernel (call number mod 4)
     uint32_t* d_pub_flag = nullptr; // [4] their stamps
     uint32_t epoch = 0;
@@ -174,6 +177,8 @@ struct moe_ctx {
     // per-stage event timing of moe_forward (moe_profile / moe_profile_read)
     bool prof_on = false;
     std::vector<cudaEvent_t> prof_ev;  // kProfMarks events per profiled call
+    cudaEvent_t dec_ev = nullptr;      // recorded after every fused decode launch (is the last call still running?)
+    bool dec_ev_used = false;
     size_t prof_calls = 0;
 };
 
@@ -220,6 +225,7 @@ int reset_counters(moe_ctx* c) {
     const unsigned long long h[4] = {(e + 1) / 2 * G, v, v, e / 2 * G};  // even calls so far, all, all, odd calls
     CUDA_TRY(cudaMemcpy(c->d_cnt, h, sizeof(h), cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemset(c->d_hctr, 0, 2 * sizeof(uint32_t)));
+    c->hcalls = 0;
     return MOE_OK;
 }
 
@@ -394,6 +400,7 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     da.w_out = c->d_w;
     da.hctr = c->d_hctr;
     if (x_host) {
+        da.hbase = c->hcalls++ * (uint32_t)dgrid;
         da.x_src = x_host;
         da.lg_src = lg;
         da.logits = c->d_logits;
@@ -406,7 +413,16 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     da.pub_flag = nullptr;
     da.stamp = da.epoch + 1;
     cudaError_t e = cudaSuccess;
-    if (!x_host && planner && c->use_planner) {  // a planner kernel publishes the call's plan
+    // A planner kernel publishes the call's plan only when the previous fused call is still running:
+    // then it plans while that call streams.  A call made alone plans faster in its own CTAs (the
+    // planner's few global round trips are on the critical path either way).
+    bool in_flight = false;
+    if (!x_host && planner && c->use_planner && c->dec_ev_used) {
+        const cudaError_t q = cudaEventQuery(c->dec_ev);
+        in_flight = q == cudaErrorNotReady;
+        if (q != cudaSuccess) cudaGetLastError();  // not-ready is not an error of this call
+    }
+    if (in_flight) {
         PubPlan* pub = reinterpret_cast<PubPlan*>(reinterpret_cast<char*>(c->d_pub) + (da.epoch & 3) * pub_plan_bytes());
         uint32_t* flag = c->d_pub_flag + (da.epoch & 3);
         e = launch_planner(da, dgrid, pub, flag, da.stamp, st);
@@ -419,6 +435,8 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     e = launch_decode(da, dgrid, dsmem, st);
     c->launches += 1;
     if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
+    if (cudaEventRecord(c->dec_ev, st) == cudaSuccess) c->dec_ev_used = true;
+    else cudaGetLastError();
     if (marks)
         for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
     return MOE_OK;
@@ -489,6 +507,44 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
 // the output over the bus and CTA 0 leaves the error bits in a pinned word.  No copy is issued on
 // the stream.  Unpinned (or, for the output, unaligned) buffers go through the context's pinned
 // staging.  One stream synchronisation ends the call.
+// Waits for a fused call launched with err_host = h_errsnap: the CTA that finishes last stores the
+// call's completion tag there, in pinned memory, after every output, so the call can return once it
+// is there (a stream synchronisation costs several microseconds more).  False when the stream ran
+// dry without the tag (a bounded wait gave up): the caller synchronises and reads the error word.
+bool wait_tag(moe_ctx* c, cudaStream_t st, uint32_t tag) {
+    volatile uint32_t* snap = c->h_errsnap;
+    bool tagged = false;
+    for (uint32_t spin = 1;; spin++) {
+        if (snap[1] == tag) {
+            tagged = true;
+            break;
+        }
+        if ((spin & 1023u) == 0) {
+            const cudaError_t q = cudaStreamQuery(st);
+            if (q != cudaErrorNotReady) break;  // done (or failed): the caller's synchronisation tells
+            cudaGetLastError();
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    return tagged;
+}
+
+// Error bits of a call that reported through h_errsnap (tagged or after a synchronisation): clears
+// the sticky device word and, after a timeout, the grid counters.
+int snap_status(moe_ctx* c, cudaStream_t st, bool tagged) {
+    uint32_t bits = c->h_errsnap[0] | c->latched;
+    c->latched = 0;
+    if (bits) {
+        if (tagged) CUDA_TRY(cudaStreamSynchronize(st));
+        CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(uint32_t)));
+        if (bits & kErrTimeout) {
+            int r = reset_counters(c);
+            if (r) return r;
+        }
+    }
+    return map_err(bits);
+}
+
 int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, const float* logits, float* out,
                        int32_t* topk_idx, float* topk_w, int flags, cudaStream_t st, DecodeArgs& da, size_t dsmem) {
     const int H = c->cfg.hidden, E = c->cfg.n_experts, K = c->cfg.top_k;
@@ -515,7 +571,8 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
         o = static_cast<float*>(c->out_stage.host);
         if (flags & MOE_F_ACCUMULATE) memcpy(o, out, ob);
     }
-    *c->h_errsnap = 0;
+    volatile uint32_t* snap = c->h_errsnap;
+    snap[0] = 0;
     da.x = c->d_hidden;
     da.out = o;
     da.err_host = c->h_errsnap;
@@ -523,18 +580,12 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
     if (!pin_x || !pin_l) c->in_stage.mark(st);
     if (topk_idx) CUDA_TRY(cudaMemcpyAsync(topk_idx, c->d_idx, sizeof(int32_t) * T * K, cudaMemcpyDeviceToHost, st));
     if (topk_w) CUDA_TRY(cudaMemcpyAsync(topk_w, c->d_w, sizeof(float) * T * K, cudaMemcpyDeviceToHost, st));
-    CUDA_TRY(cudaStreamSynchronize(st));
-    uint32_t bits = *(volatile uint32_t*)c->h_errsnap | c->latched;
-    c->latched = 0;
-    if (bits) {  // clear the sticky device word (and, after a timeout, the grid counters)
-        CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(uint32_t)));
-        if (bits & kErrTimeout) {
-            int r = reset_counters(c);
-            if (r) return r;
-        }
-    }
+    // Top-k copies, and kernels that end without a completion tag, take the stream synchronisation.
+    const bool tagged = !topk_idx && !topk_w && wait_tag(c, st, da.epoch + 1u);
+    if (!tagged) CUDA_TRY(cudaStreamSynchronize(st));
+    const int r = snap_status(c, st, tagged);
     if (!pin_o) memcpy(out, o, ob);
-    return map_err(bits);
+    return r;
 }
 
 }  // namespace
@@ -632,7 +683,8 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
         st = fail(MOE_ECUDA, "memset failed");
     if (!st && cudaMallocHost((void**)&c->h_err, sizeof(uint32_t)) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
     if (!st && cudaMallocHost((void**)&c->h_errsnap, 16) != cudaSuccess) st = fail(MOE_ENOMEM, "pinned error word");
-    if (!st && (cudaEventCreateWithFlags(&c->in_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
+    if (!st && (cudaEventCreateWithFlags(&c->dec_ev, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&c->in_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&c->out_stage.ev, cudaEventDisableTiming) != cudaSuccess ||
                 cudaEventCreateWithFlags(&c->job_stage.ev, cudaEventDisableTiming) != cudaSuccess))
         st = fail(MOE_ECUDA, "event creation failed");
@@ -687,6 +739,7 @@ int moe_destroy(moe_ctx* c) {
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_errsnap) cudaFreeHost(c->h_errsnap);
     for (cudaEvent_t ev : c->prof_ev) cudaEventDestroy(ev);
+    if (c->dec_ev) cudaEventDestroy(c->dec_ev);
     for (Staging* s : {&c->in_stage, &c->out_stage, &c->job_stage}) {
         if (s->host) cudaFreeHost(s->host);
         if (s->ev) cudaEventDestroy(s->ev);
@@ -873,10 +926,21 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         c->prof_calls++;
         CUDA_TRY(cudaEventRecord(marks[0], st));
     }
+    // a synchronous fused call on device buffers waits for its completion tag like a host call
+    const bool sync_tag = use_fused && !host && (flags & MOE_F_SYNC) && !topk_idx && !topk_w && !marks;
     if (use_fused) {
         da.x = x;
         da.out = o;
+        if (sync_tag) {
+            c->h_errsnap[0] = 0;
+            da.err_host = c->h_errsnap;
+        }
         if ((s = launch_fused(c, layer, lg, da, dsmem, st, marks))) return s;
+        if (sync_tag) {
+            const bool tagged = wait_tag(c, st, da.epoch + 1u);
+            if (!tagged) CUDA_TRY(cudaStreamSynchronize(st));
+            return snap_status(c, st, tagged);
+        }
     }
     if (T > 0 && !use_fused) {
         RouteArgs ra = route_args(c, T, lg, c->has_bias[layer] ? c->d_bias + (size_t)layer * E : nullptr);

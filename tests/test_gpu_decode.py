@@ -141,6 +141,26 @@ def test_host_buffers_errors_timeout_and_accumulate(layer):
     np.testing.assert_allclose(base.numpy(), ref + 0.5, atol=1e-6)
 
 
+def test_host_calls_interleaved_with_device_calls(layer):
+    """Host-buffer calls alternating with device-buffer calls on one context, each host call made
+    right after a device call: every host call must wait for all of its own input copies (a host call
+    must never see the copy count of an earlier one) and match the device call on the same inputs."""
+    p, _ = layer
+    T = 2
+    cases = []
+    for i in range(6):
+        x, lg, xd, lgd = _inputs(300 + i, T)
+        cases.append((torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory(),
+                      torch.from_numpy(lg).pin_memory(), xd, lgd))
+    refs = [p.forward(0, xd, lgd, sync=True).cpu().numpy() for _, _, xd, lgd in cases]
+    po = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    for rep in range(3):
+        for i, (px, pl, xd, lgd) in enumerate(cases):
+            p.forward(0, cases[(i + 1) % len(cases)][2], cases[(i + 1) % len(cases)][3])  # device call in flight
+            p.forward_host(0, px, pl, out=po)
+            np.testing.assert_array_equal(po.numpy(), refs[i])
+
+
 def test_expert_parallel_partials_sum_to_the_full_layer(layer):
     """Two expert-parallel rank contexts on one GPU: each computes its local experts only; the sum of
     the partials equals the unsharded layer."""
