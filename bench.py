@@ -43,7 +43,7 @@ METRIC = "MoE-layer decode tokens/s and achieved HBM GB/s vs peak"
 UNIT = "MoE-layer tokens/s"
 # DRAM bytes (read + write) per algorithmic byte of decode_kernel, from the committed ncu capture of
 # one T=1 layer (profiles/decode_kernel_T1.md); None until a capture exists.
-TRAFFIC_RATIO = 255.443 / 251.658
+TRAFFIC_RATIO = 255.503 / 251.658
 TRAFFIC_SOURCE = "profiles/decode_kernel_T1.md"
 
 
@@ -65,6 +65,8 @@ def parse():
                     help="configs[3] prefill measurement at N=1 (0 to skip)")
     ap.add_argument("--no-block", action="store_true", help="skip the moe_block_forward measurement")
     ap.add_argument("--no-int8", action="store_true", help="skip the configs[4] int8 measurement")
+    ap.add_argument("--int8-experts", type=int, default=96,
+                    help="int8 measurement: the N least popular experts of every layer stored int8 (configs[4]: 96)")
     ap.add_argument("--cold-slots", type=int, default=0,
                     help="HBM slots per layer for the host-cold tier measurement (0: skip)")
     ap.add_argument("--ep-shard", choices=["units", "experts"], default="units",
@@ -225,10 +227,16 @@ class Stack:
         self.x = torch.from_numpy(xs.view(np.int16)).view(torch.bfloat16).to(self.device)
         self.lg = torch.from_numpy(lgs).to(self.device)
         self.out = torch.empty(self.L, T, H, dtype=torch.float32, device=self.device)
-        # per (rotation, layer) ctypes arguments of moe_forward, so the timed loop is one C call per layer
+        # per (rotation, layer) ctypes arguments of moe_forward, and per rotation the argument arrays of
+        # moe_forward_layers, so the timed loop is one C call per step
         vp = ctypes.c_void_p
         self.args = [[(l, T, vp(self.x[r, l].data_ptr()), vp(self.lg[r, l].data_ptr()), vp(self.out[l].data_ptr()))
                       for l in range(self.L)] for r in range(self.R)]
+        L = self.L
+        self.step_args = [((ctypes.c_int32 * L)(*range(L)),
+                           (vp * L)(*[self.x[r, l].data_ptr() for l in range(L)]),
+                           (vp * L)(*[self.lg[r, l].data_ptr() for l in range(L)]),
+                           (vp * L)(*[self.out[l].data_ptr() for l in range(L)])) for r in range(self.R)]
         self.sp = vp(torch.cuda.current_stream(self.device).cuda_stream)
         # algorithmic bytes per (rotation, layer): this rank's distinct routed experts
         self.ubytes = np.zeros((self.R, self.L))
@@ -244,12 +252,16 @@ class Stack:
 
     def step(self, s):
         from npu_offload_b200._lib import check, lib
-        fn, h, sp = lib().moe_forward, self.plane.handle, self.sp
+        h, sp = self.plane.handle, self.sp
+        if self.ws == 1 or self.plane.ep_attached:  # every layer of the step in one C call
+            la, xa, ga, oa = self.step_args[s % self.R]
+            check(lib().moe_forward_layers(h, self.L, la, self.T, xa, ga, oa, 0, sp))
+            return
+        fn = lib().moe_forward
         for l, T, x, lg, out in self.args[s % self.R]:
             check(fn(h, l, T, x, lg, out, None, None, 0, sp))
-            if self.ws > 1 and not self.plane.ep_attached:
-                from npu_offload_b200.parallel import allreduce_partial
-                allreduce_partial(self.out[l])
+            from npu_offload_b200.parallel import allreduce_partial
+            allreduce_partial(self.out[l])
 
 
 def barrier(ws):
@@ -479,7 +491,7 @@ Q8_BYTES = 3 * H * F + (2 * F + H) * 4  # one int8 weight-only expert: q tables 
 
 
 def int8_run(stack, args, steps, warmup):
-    """the stack's 96 least popular experts of every layer (by the Zipf rank of the layer's
+    """the stack's --int8-experts (96) least popular experts of every layer (by the Zipf rank of the layer's
     routing bias) re-stored int8 weight-only (quantised on the GPU with the reference's quant_row
     rule), the top 32 kept bf16; decode batch 1, the same Zipf-routed inputs.  Roofline bytes: the
     routed experts' stored bytes (bf16 31,457,280 B; int8 15,728,640 B of tables + 26,624 B of scales)."""
@@ -489,7 +501,7 @@ def int8_run(stack, args, steps, warmup):
     cold = []
     for l in range(L):
         order = np.argsort(-synth.zipf_bias(args.seed + 31 * l, E), kind="stable")  # most popular first
-        c = set(order[32:].tolist())
+        c = set(order[E - args.int8_experts:].tolist()) if args.int8_experts > 0 else set()
         for e in sorted(c):
             stack.plane.quantize_expert_q8(l, e)
         cold.append(c)
@@ -509,8 +521,8 @@ def int8_run(stack, args, steps, warmup):
     tot = sum(nbytes[r].sum() for r in reps)
     gbs = tot / (ms / 1e3) / 1e9
     peak = peaks()[0]
-    return {"workload": f"configs[4]: {L}-layer stack, 96 least popular experts per layer int8 weight-only, "
-                        "top 32 bf16; decode batch 1, Zipf routing",
+    return {"workload": f"configs[4]: {L}-layer stack, {args.int8_experts} least popular experts per layer int8 "
+                        f"weight-only, top {E - args.int8_experts} bf16; decode batch 1, Zipf routing",
             "tokens_per_s": L * steps / (ms / 1e3), "us_per_layer": ms * 1e3 / (steps * L),
             "int8_experts_per_layer": float(n8.mean()), "bytes_per_layer": tot / (steps * L),
             "roofline": {"bound": "hbm", "kernel": "decode_kernel", "achieved": gbs, "peak": peak, "unit": "GB/s",

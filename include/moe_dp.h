@@ -137,6 +137,15 @@ MOE_API int moe_set_bias(moe_ctx* ctx, int layer, const float* bias, int flags);
 MOE_API int moe_forward(moe_ctx* ctx, int layer, int T, const uint16_t* hidden, const float* router_logits, float* out,
                 int32_t* topk_idx, float* topk_w, int flags, void* stream);
 
+/* n moe_forward calls enqueued by one call, in order: call i is layer layers[i] on hidden[i],
+ * router_logits[i] -> out[i] (device buffers, T tokens each; MOE_F_ACCUMULATE applies to every call,
+ * MOE_F_SYNC synchronises once after the last).  For a caller that issues several layers' MoE work
+ * back to back -- the engine's layer loop issuing moe_phase per layer (main.rs:267-289, moe_phase
+ * main.rs:149-209) with its inputs ready -- it keeps the caller's language off the per-layer path.
+ * Stops at the first failing call and returns its status. */
+MOE_API int moe_forward_layers(moe_ctx* ctx, int n, const int32_t* layers, int T, const uint16_t* const* hidden,
+                               const float* const* router_logits, float* const* out, int flags, void* stream);
+
 /* Router + token permutation alone (device pointers unless MOE_F_HOST; bias may be NULL):
  *   topk_idx/topk_w [T,K]; counts [E]; offsets [E+1] (expert-id order); perm [T*K] pair ids
  *   t*K+k grouped by expert, tokens ascending (runtime.py:343-347); job_order [E] experts in
@@ -259,7 +268,8 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               done; for consumer warp 0, SM cycles (8) waiting for ring stages,
  *                               (9) working on them, (10) of which in the cross-warp exchange; when
  *                               the CTA plans: 16 plan decision made, 17 logits and expert table
- *                               loaded, 18 top-k chosen, 6 routed, 7 jobs, 15 pairs and share), the
+ *                               loaded, 18 top-k chosen, 6 routed, 7 jobs, 15 pairs and share; when
+ *                               it reduces: 19 partial sums staged, 20 cross-rank exchange begun), the
  *                               planner kernel's stamps in the row after the grid's (0 start,
  *                               1 planned, 2 published, 3 predecessor complete) and CTA 0's per-stage
  *                               stamps; read them with moe_timeline_read.
@@ -272,19 +282,23 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               (500..4000; 0 = the default, 2500).  Shares are balanced by this cost
  *                               rather than by bytes, because dequantising an int8 unit takes longer
  *                               per byte than streaming it.
- *   MOE_OPT_REDUCERS            tuning: in a stream of fused calls (a device-buffer call whose planner
- *                               finds the previous call still running), how many CTAs (the last to
+ *   MOE_OPT_REDUCERS            tuning: in a stream of fused calls (a device-buffer call planned while
+ *                               the previous call on the context still runs), how many CTAs (the last to
  *                               finish their share) reduce the partial sums into the output; the others
  *                               leave at once and the next call's CTAs take their SMs.  Raised as
  *                               needed so that a reducer's slice of the partial sums fits on chip
- *                               (default 48).  Calls made alone, host-buffer calls and block calls use
+ *                               (default 48; 96 on expert-parallel contexts of eight or more ranks).  Calls made alone, host-buffer calls and block calls use
  *                               every CTA.  0: every call uses every CTA and even shares, so output
  *                               bits never depend on timing (otherwise a streamed call's shares, and
  *                               with them the fp32 summation order, differ from a lone call's).
+ *   MOE_OPT_PLANNER             1: a device-buffer fused call made while the previous one still runs is
+ *                               planned by a one-CTA planner kernel on the SM the decode grid leaves
+ *                               free; 0: every CTA plans for itself.  Default 1 on single-GPU
+ *                               contexts, 0 on expert-parallel ones (ep_world > 1).
  *   MOE_OPT_LATE_BYTES          tuning: in a stream of fused calls, the last CTAs by index (as many as
  *                               reduce), which start only when the previous call's reducers leave
  *                               their SMs, get shares smaller by this many bytes of the bf16 stream
- *                               (default 688128, 28 Solar units). */
+ *                               (default 688128, 28 Solar units; 1376256 on expert-parallel contexts). */
 #define MOE_OPT_FUSED_DECODE 1
 #define MOE_OPT_WAIT_TIMEOUT_US 2
 #define MOE_OPT_INJECT_WAIT_TIMEOUT 3

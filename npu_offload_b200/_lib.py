@@ -52,6 +52,7 @@ _SIGS = {
     "moe_evict_expert": (_i, [_vp, _i, _i]),
     "moe_set_bias": (_i, [_vp, _i, _vp, _i]),
     "moe_forward": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
+    "moe_forward_layers": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _i, _vp]),
     "moe_route": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
     "moe_experts": (_i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp]),
     "moe_ck_moe3": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _i, _vp]),

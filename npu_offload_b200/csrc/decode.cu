@@ -838,6 +838,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
             mine[f] = acc;
         }
         named_bar_sync(1, kCThreads);
+        if (tl && tid == 0) tl[20] = globaltimer_ns();
         ep_combine(a.ep, mine, a.out, a.T, H, q0, nq, a.accumulate, a.err, deadline, kCThreads, &c.abort_flag);
         if (tl && tid == 0) tl[5] = globaltimer_ns();
         reducer_done();

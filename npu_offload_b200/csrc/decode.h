@@ -16,8 +16,12 @@ constexpr int kMaxSegTotal = kPlanMaxGrid + kMaxGroups;  // segments of one call
 // on B200 at the Solar shape, back-to-back layers: batch 1 49.5 -> 43.8 us per layer against every
 // CTA reducing (flat within 1 us for 32-64 reducers and 24-40 units), batch 4 124 -> 98 us.
 constexpr int kReducersDefault = 48;
+constexpr int kReducersDefaultEp8 = 96;  // expert-parallel contexts of eight or more ranks
 constexpr bool kPlannerDefault = true;
 constexpr long long kLateBytesDefault = 28 * 24576;
+// expert-parallel contexts: the reducers also exchange with the other ranks, so the late CTAs start
+// later (measured on two B200, unit-sharded Solar layers: 29.7 us per layer at 56 units, 33.0 at 28)
+constexpr long long kLateBytesDefaultEp = 56 * 24576;
 constexpr int kTimelineSlots = 24;  // per-CTA stamps recorded when DecodeArgs::timeline is set
 constexpr int kStageLogMax = 1024;  // stages of CTA 0 recorded in DecodeArgs::stage_log
 

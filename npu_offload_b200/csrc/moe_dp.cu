@@ -435,8 +435,10 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     e = launch_decode(da, dgrid, dsmem, st);
     c->launches += 1;
     if (e != cudaSuccess) return fail(MOE_ECUDA, "decode launch: %s", cudaGetErrorString(e));
-    if (cudaEventRecord(c->dec_ev, st) == cudaSuccess) c->dec_ev_used = true;
-    else cudaGetLastError();
+    if (c->use_planner) {  // the next call asks whether this one still runs
+        if (cudaEventRecord(c->dec_ev, st) == cudaSuccess) c->dec_ev_used = true;
+        else cudaGetLastError();
+    }
     if (marks)
         for (int i = 2; i < kProfMarks; i++) cudaEventRecord(marks[i], st);
     return MOE_OK;
@@ -620,6 +622,15 @@ int moe_create(const moe_config* cfg, moe_ctx** out) {
     DeviceGuard dg(k.device);
     moe_ctx* c = new moe_ctx;
     c->cfg = k;
+    // expert-parallel ranks plan in their own CTAs: their layers stream for a fraction of a
+    // one-GPU layer, less than the planner kernel needs under load (measured on two B200: 29.6 us
+    // per unit-sharded Solar layer without it, 37.6 us with it)
+    c->use_planner = kPlannerDefault && k.ep_world <= 1;
+    c->late_bytes = k.ep_world > 1 ? kLateBytesDefaultEp : kLateBytesDefault;
+    // eight ranks: each layer streams a few microseconds per GPU; more reducers shorten the
+    // reduction + exchange (measured on eight B200, unit-sharded Solar layers: 22.2 us per layer with
+    // 96 reducers, 24.1 us with 48)
+    if (k.ep_world >= 8) c->reducers = kReducersDefaultEp8;
     c->cfg.shard_map = nullptr;
     c->dev = k.device;
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, k.device);
@@ -1012,6 +1023,24 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
         return finish_sync(c, st);
     }
     if (flags & MOE_F_SYNC) return finish_sync(c, st);
+    return MOE_OK;
+}
+
+int moe_forward_layers(moe_ctx* c, int n, const int32_t* layers, int T, const uint16_t* const* hidden,
+                       const float* const* logits, float* const* out, int flags, void* stream) {
+    if (!c) return fail(MOE_EINVAL, "null context");
+    if (n < 0) return fail(MOE_EINVAL, "n=%d < 0", n);
+    if (n > 0 && (!layers || !hidden || !logits || !out)) return fail(MOE_EINVAL, "null layer or buffer array");
+    if (flags & MOE_F_HOST) return fail(MOE_EINVAL, "moe_forward_layers takes device buffers (MOE_F_HOST: call moe_forward)");
+    for (int i = 0; i < n; i++) {
+        const int st = moe_forward(c, layers[i], T, hidden[i], logits[i], out[i], nullptr, nullptr,
+                                   flags & ~MOE_F_SYNC, stream);
+        if (st) return st;
+    }
+    if (flags & MOE_F_SYNC) {
+        DeviceGuard dg(c->dev);
+        return finish_sync(c, (cudaStream_t)stream);
+    }
     return MOE_OK;
 }
 

@@ -179,6 +179,26 @@ class MoEDataPlane:
                                 _stream_ptr(stream, x.device)))
         return (out, idx, w) if return_topk else out
 
+    def forward_layers(self, layers, hiddens, logits, outs, accumulate=False, stream=None, sync=False):
+        """Several layer calls enqueued by one C call (moe_forward_layers): layer layers[i] on
+        hiddens[i] [T,H] bf16 and logits[i] [T,E] fp32 into outs[i] [T,H] fp32, device tensors, in
+        order."""
+        n = len(layers)
+        assert len(hiddens) == len(logits) == len(outs) == n
+        T = hiddens[0].shape[0] if n else 0
+        for x, lg, o in zip(hiddens, logits, outs):
+            assert x.is_cuda and x.dtype == torch.bfloat16 and x.shape == (T, self.H)
+            assert lg.is_cuda and lg.dtype == torch.float32 and lg.shape == (T, self.E)
+            assert o.is_cuda and o.dtype == torch.float32 and o.shape == (T, self.H)
+        la = (ctypes.c_int32 * max(n, 1))(*layers)
+        xa = (ctypes.c_void_p * max(n, 1))(*[t.data_ptr() for t in hiddens])
+        ga = (ctypes.c_void_p * max(n, 1))(*[t.data_ptr() for t in logits])
+        oa = (ctypes.c_void_p * max(n, 1))(*[t.data_ptr() for t in outs])
+        flags = (MOE_F_ACCUMULATE if accumulate else 0) | (MOE_F_SYNC if sync else 0)
+        dev = hiddens[0].device if n else self.device
+        check(lib().moe_forward_layers(self._h, n, la, T, xa, ga, oa, flags, _stream_ptr(stream, dev)))
+        return outs
+
     # ---- the steps either side of the routed experts (one Solar MoE block, solar_engine/src/layer.rs:1-6) ----
     def load_shared(self, layer, gate=None, up=None, down=None, router=None):
         """Shared expert gate/up [Fs,H], down [H,Fs] and router weights [E,H] (bf16) of one layer.

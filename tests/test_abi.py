@@ -51,6 +51,7 @@ def test_null_arguments_return_status():
     L = nob.lib()
     assert L.moe_create(None, None) == _lib.MOE_EINVAL
     assert L.moe_forward(None, 0, 1, None, None, None, None, None, 0, None) == _lib.MOE_EINVAL
+    assert L.moe_forward_layers(None, 1, None, 1, None, None, None, 0, None) == _lib.MOE_EINVAL
     assert L.moe_route(None, 1, None, None, None, None, None, None, None, None, None, 0, None) == _lib.MOE_EINVAL
     assert L.moe_experts(None, 1, None, 0, None, None, None, None, None, None, 0, None) == _lib.MOE_EINVAL
     assert L.moe_status(None, None) == _lib.MOE_EINVAL

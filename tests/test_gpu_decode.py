@@ -141,6 +141,29 @@ def test_host_buffers_errors_timeout_and_accumulate(layer):
     np.testing.assert_allclose(base.numpy(), ref + 0.5, atol=1e-6)
 
 
+def test_forward_layers_matches_single_calls(layer):
+    """moe_forward_layers enqueues the calls moe_forward would make, in order: the same outputs (a
+    streamed call may cut its shares differently, so within fp32 summation order), and an error of a
+    later call (a NaN logit) is reported."""
+    from npu_offload_b200._lib import MOE_ENONFINITE, MoEError
+    p, _ = layer
+    ins = [_inputs(700 + i, 1 + i % 3) for i in range(6)]
+    for T in (1, 2, 3):
+        sel = [c for c in ins if c[2].shape[0] == T]
+        outs = [torch.empty(T, H, dtype=torch.float32, device="cuda") for _ in sel]
+        p.forward_layers([0] * len(sel), [c[2] for c in sel], [c[3] for c in sel], outs, sync=True)
+        for c, o in zip(sel, outs):
+            ref = p.forward(0, c[2], c[3], sync=True)
+            np.testing.assert_allclose(o.cpu().numpy(), ref.cpu().numpy(), rtol=1e-5, atol=1e-6)
+    bad = ins[1][3].clone()
+    bad[0, 3] = float("nan")
+    outs = [torch.empty(2, H, dtype=torch.float32, device="cuda") for _ in range(2)]
+    with pytest.raises(MoEError) as ei:
+        p.forward_layers([0, 0], [ins[4][2], ins[1][2]], [ins[4][3], bad], outs, sync=True)
+    assert ei.value.status == MOE_ENONFINITE
+    p.forward(0, ins[1][2], ins[1][3], sync=True)  # the error does not stick
+
+
 def test_host_calls_interleaved_with_device_calls(layer):
     """Host-buffer calls alternating with device-buffer calls on one context, each host call made
     right after a device call: every host call must wait for all of its own input copies (a host call
