@@ -495,7 +495,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NS = a.NS, G = gridDim.x;
     const int s = blockIdx.x;
-    const int par = a.epoch & 1;
 
     uint64_t* tl = a.timeline ? a.timeline + (size_t)s * kTimelineSlots : nullptr;  // optional phase stamps
     if (tl && tid == 0) tl[0] = globaltimer_ns();
