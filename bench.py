@@ -366,10 +366,12 @@ def e2e_run(stack, steps, warmup, ws):
     return T * L * steps / (ms / 1e3), h2d, d2h
 
 
-def prefill_run(stack, T, reps=5, warmup=2):
+def prefill_run(stack, T, reps=5, warmup=2, ws=1):
     """one MoE layer (layer 0 of the stack) at T prefill tokens with uniform routing
     (logits N(0,1), no popularity bias; ~T*K/E tokens per expert).  Device-resident inputs, CUDA
-    events around `reps` back-to-back layer calls."""
+    events around `reps` back-to-back layer calls; with ws > 1 every rank runs its share of the
+    experts (its slice of every expert's units under unit sharding) and the partial outputs are
+    combined across ranks, timed as the max over ranks."""
     import torch
     from npu_offload_b200 import synth
     x = torch.from_numpy(synth.hidden(99, T, H).view(np.int16)).view(torch.bfloat16).to(stack.device)
@@ -380,6 +382,7 @@ def prefill_run(stack, T, reps=5, warmup=2):
     for _ in range(warmup):
         stack.plane.forward(0, x, lg, out=out)
     torch.cuda.synchronize(stack.device)
+    barrier(ws)
     l0 = stack.plane.launch_count
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
@@ -387,12 +390,13 @@ def prefill_run(stack, T, reps=5, warmup=2):
         stack.plane.forward(0, x, lg, out=out)
     ev1.record()
     torch.cuda.synchronize(stack.device)
-    ms = ev0.elapsed_time(ev1) / reps
+    barrier(ws)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), ws) / reps
     flops = 2.0 * T * K * 3 * H * F
-    wbytes = experts * EXPERT_BYTES
+    wbytes = experts * EXPERT_BYTES / ws  # each rank's streamed weight bytes (an even split)
     return {"workload": f"configs[3]: 1 layer, {T} prefill tokens, uniform routing ({T * K / E:.0f} tokens/expert)",
             "tokens_per_s": T / (ms / 1e3), "ms_per_layer": ms, "tflops": flops / (ms / 1e3) / 1e12,
-            "weights_gbs": wbytes / (ms / 1e3) / 1e9, "experts": experts,
+            "weights_gbs": wbytes / (ms / 1e3) / 1e9, "experts": experts, "n_gpus": ws,
             "path": "tcgen05 kernels: gate/up with fused SwiGLU, down with fp32 output; gather + combine kernels",
             "gpu_launches_per_layer": (stack.plane.launch_count - l0) / reps}
 
@@ -727,8 +731,8 @@ def our_arm(args):
                       "experts_per_layer": float(np.mean([stack.ucount[r].mean() for r in reps]))})
     launches_all = int(sum_over_ranks(launches, ws))
     prefill = None
-    if ws == 1 and args.prefill_tokens > 0:
-        prefill = prefill_run(stack, args.prefill_tokens)
+    if args.prefill_tokens > 0:
+        prefill = prefill_run(stack, args.prefill_tokens, ws=ws)
     block = None
     if ws == 1 and not args.no_block:
         block = block_run(stack, max(1, args.steps // 4), min(args.warmup, 3))

@@ -458,7 +458,7 @@ __device__ bool ep_combine(const EpExchange& ep, const float4* mine, float* out,
     const float* mv = reinterpret_cast<const float*>(mine);
     for (int f = tid; f < W * ne; f += nthr) {  // this rank's values into every rank's buffer
         const int r = f / ne, i = f - r * ne, t = i / nv, j = i - t * nv;
-        uint64_t* dst = ep.peer_x[r] + ((size_t)(par * W + ep.rank) * kEpMaxT + t) * H + 4 * q0 + j;
+        uint64_t* dst = ep.peer_x[r] + ((size_t)(par * W + ep.rank) * ep.tstride + t) * H + 4 * q0 + j;
         st_relaxed_sys_u64(dst, tag | __float_as_uint(mv[i]));
     }
     bool ok = true;
@@ -467,7 +467,7 @@ __device__ bool ep_combine(const EpExchange& ep, const float4* mine, float* out,
         float* o = out + (size_t)t * H + 4 * q0 + j;
         float acc = accumulate ? *o : 0.f;
         for (int r = 0; r < W && ok; r++) {
-            const uint64_t* src = ep.x_local + ((size_t)(par * W + r) * kEpMaxT + t) * H + 4 * q0 + j;
+            const uint64_t* src = ep.x_local + ((size_t)(par * W + r) * ep.tstride + t) * H + 4 * q0 + j;
             uint64_t w = ld_relaxed_sys_u64(src);
             for (int spin = 0; (uint32_t)(w >> 32) != ep.epoch; spin++) {
                 if ((spin & 31) == 31 && (*(volatile int*)abort || globaltimer_ns() > deadline)) {
@@ -983,26 +983,53 @@ bool decode_register_split_fits() {
 }
 
 // Cross-rank combine for the multi-kernel path: CTA s owns the same output slice as decode CTA s.
-__global__ void __launch_bounds__(256) ep_exchange_kernel(const EpExchange ep, const float* part, float* out, int T,
+__global__ void __launch_bounds__(512) ep_exchange_kernel(const EpExchange ep, const float* part, float* out, int T,
                                                           int H, int accumulate, uint32_t* err, uint64_t timeout_ns) {
-    extern __shared__ __align__(16) float4 mine[];  // [T][nq]
     __shared__ int abort_flag;
-    const int s = blockIdx.x, G = gridDim.x, H4 = H / 4;
+    const int s = blockIdx.x, G = gridDim.x, H4 = H / 4, W = ep.world, par = ep.epoch & 1;
     const int q0 = (int)((long long)s * H4 / G), nq = (int)((long long)(s + 1) * H4 / G) - q0;
-    if (threadIdx.x == 0) abort_flag = 0;
-    for (int f = threadIdx.x; f < T * nq; f += blockDim.x) {
-        const int t = f / nq, q = f % nq;
-        mine[f] = reinterpret_cast<const float4*>(part + (size_t)t * H)[q0 + q];
+    const int nv = nq * 4, ne = T * nv, nthr = blockDim.x, tid = threadIdx.x;
+    const uint64_t tag = (uint64_t)ep.epoch << 32;
+    const uint64_t deadline = globaltimer_ns() + timeout_ns;
+    if (tid == 0) abort_flag = 0;
+    // every value of this rank's partial slice, straight from global memory, into every rank's buffer
+    // (all tokens of the call first, then the collection: one round of exchange latency)
+    for (int i = tid; i < ne; i += nthr) {
+        const int t = i / nv, j = i - t * nv;
+        const uint64_t w = tag | __float_as_uint(__ldcg(part + (size_t)t * H + 4 * q0 + j));
+        for (int r = 0; r < W; r++)
+            st_relaxed_sys_u64(ep.peer_x[r] + ((size_t)(par * W + ep.rank) * ep.tstride + t) * H + 4 * q0 + j, w);
     }
-    named_bar_sync(1, blockDim.x);
-    ep_combine(ep, mine, out, T, H, q0, nq, accumulate, err, globaltimer_ns() + timeout_ns, blockDim.x, &abort_flag);
+    named_bar_sync(1, nthr);
+    for (int i = tid; i < ne; i += nthr) {  // every rank adds the same values in rank order
+        const int t = i / nv, j = i - t * nv;
+        float* o = out + (size_t)t * H + 4 * q0 + j;
+        float acc = accumulate ? *o : 0.f;
+        bool ok = true;
+        for (int r = 0; r < W && ok; r++) {
+            const uint64_t* src = ep.x_local + ((size_t)(par * W + r) * ep.tstride + t) * H + 4 * q0 + j;
+            uint64_t w = ld_relaxed_sys_u64(src);
+            for (int spin = 0; (uint32_t)(w >> 32) != ep.epoch; spin++) {
+                if ((spin & 31) == 31 && (*(volatile int*)&abort_flag || globaltimer_ns() > deadline)) {
+                    atomicOr(err, kErrTimeout);
+                    *(volatile int*)&abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+                w = ld_relaxed_sys_u64(src);
+            }
+            acc += __uint_as_float((uint32_t)w);
+        }
+        if (!ok) break;
+        *o = acc;
+    }
 }
 
 cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* out, int T, int H, int accumulate,
                                uint32_t* err, uint64_t timeout_ns, int grid, cudaStream_t st) {
-    const int nq_max = (H / 4 + grid - 1) / grid + 1;
-    const size_t smem = (size_t)T * nq_max * 16;
-    ep_exchange_kernel<<<grid, 256, smem, st>>>(ep, part, out, T, H, accumulate, err, timeout_ns);
+    if (T > ep.tstride) return cudaErrorInvalidValue;
+    ep_exchange_kernel<<<grid, 512, 0, st>>>(ep, part, out, T, H, accumulate, err, timeout_ns);
     return cudaGetLastError();
 }
 

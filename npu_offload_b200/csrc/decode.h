@@ -60,20 +60,22 @@ static_assert(sizeof(Seg) == 64, "Seg layout");
 static_assert(sizeof(PlanShared) % 16 == 0 && sizeof(PlanCta) % 16 == 0, "plan structs are 16-byte multiples");
 
 // Expert-parallel combine over NVLink peer memory.  Every rank owns an exchange buffer
-// x[2][world][kEpMaxT][H] of 64-bit words (call parity, source rank, token, element).  For each
+// x[2][world][tstride][H] of 64-bit words (call parity, source rank, token, element).  For each
 // output slice (the quads one reducing CTA owns, the same slicing on every rank) a rank stores every
 // value of its partial into every rank's buffer as one word {epoch, fp32 bits} -- an aligned 64-bit
 // store is single-copy atomic, so a reader polls each word until it carries the call's epoch, with no
 // fence and no flag (the low-latency protocol of NCCL's LL transport) -- and adds the ranks' values
 // in rank order: every rank ends with the same full output, bit for bit.  Buffers alternate by call
 // parity, so a rank one call ahead never overwrites words a slower rank still reads.
-constexpr int kEpMaxT = 64;     // tokens per exchange (longer calls exchange in chunks)
+constexpr int kEpMaxT = 64;      // the exchange buffer holds at least this many tokens per slot
+constexpr int kEpMaxTcap = 2048; // and at most this many (longer calls exchange in chunks of it)
 constexpr int kEpMaxWorld = 8;  // ranks of one box
 struct EpExchange {
     uint64_t* const* peer_x;       // [world] every rank's exchange buffer (peer pointers; own = local)
     const uint64_t* x_local;       // this rank's exchange buffer
     int rank, world;
     uint32_t epoch;                // this call's exchange number (same on all ranks), >= 1
+    int tstride;                   // tokens per (parity, rank) slot of the buffers
 };
 
 struct PubPlan;
@@ -168,9 +170,11 @@ cudaError_t decode_set_smem_limit();
 // producer / consumer register split (otherwise the fused path must not be used).
 bool decode_register_split_fits();
 
-// Cross-rank combine of out[t0 .. t0+T) for a T <= kEpMaxT chunk already holding this rank's partial
-// (multi-kernel path): `part` is the local partial [T, H], `out` receives base (accumulate) + the sum
-// over ranks; grid = the decode grid size G (same output slicing on every rank).
+// Cross-rank combine of out[t0 .. t0+T) for a T <= ep.tstride chunk already holding this rank's
+// partial (multi-kernel and prefill paths): `part` is the local partial [T, H], `out` receives base
+// (accumulate) + the sum over ranks; grid = the decode grid size G (same output slicing on every
+// rank).  One launch pushes every value of the chunk to every rank, then collects: one round of
+// exchange latency per call however many tokens it has.
 cudaError_t launch_ep_exchange(const EpExchange& ep, const float* part, float* out, int T, int H, int accumulate,
                                uint32_t* err, uint64_t timeout_ns, int grid, cudaStream_t st);
 

@@ -132,7 +132,8 @@ struct moe_ctx {
                                           //   partial-sum reads, arrived (odd calls)
     float* d_part = nullptr;    // fused decode partial sums: two buffers, used by alternate calls
     // expert-parallel exchange over NVLink peer memory (moe_ep_export / moe_ep_import)
-    uint64_t* d_xbuf = nullptr;         // [2][world][kEpMaxT][H] words {epoch, fp32}: this rank's receive buffer
+    uint64_t* d_xbuf = nullptr;         // [2][world][ep_tcap][H] words {epoch, fp32}: this rank's receive buffer
+    int ep_tcap = kEpMaxT;              // tokens per (parity, rank) slot of the exchange buffers
     uint64_t** d_peer_x = nullptr;      // [kEpMaxWorld] device copy of every rank's buffer pointer
     float* d_xpart = nullptr;           // multi-kernel path: this rank's partial before the exchange
     std::vector<void*> ipc_opened;      // peer mappings to close
@@ -352,6 +353,7 @@ EpExchange next_ep(moe_ctx* c) {
     ep.rank = c->cfg.ep_rank;
     ep.world = c->cfg.ep_world;
     ep.epoch = ++c->xepoch;
+    ep.tstride = c->ep_tcap;
     return ep;
 }
 
@@ -994,8 +996,8 @@ int moe_forward(moe_ctx* c, int layer, int T, const uint16_t* hidden, const floa
             if (e != cudaSuccess) return fail(MOE_ECUDA, "expert launch: %s", cudaGetErrorString(e));
         }
         if (c->ep_attached)
-            for (int t0 = 0; t0 < T; t0 += kEpMaxT) {
-                const int tc = std::min(kEpMaxT, T - t0);
+            for (int t0 = 0; t0 < T; t0 += c->ep_tcap) {  // one exchange unless T exceeds the buffer
+                const int tc = std::min(c->ep_tcap, T - t0);
                 e = launch_ep_exchange(next_ep(c), c->d_xpart + (size_t)t0 * H, o + (size_t)t0 * H, tc, H, acc ? 1 : 0,
                                        c->d_err, c->timeout_ns, c->sm_count - 1, st);
                 c->launches += 1;
@@ -1303,7 +1305,9 @@ int moe_ep_export(moe_ctx* c, void* out, int cap) {
     const int W = c->cfg.ep_world, H = c->cfg.hidden;
     int st = MOE_OK;
     if (!c->d_xbuf) {
-        if (!st) st = dalloc(&c->d_xbuf, (size_t)2 * W * kEpMaxT * H);
+        // a slot holds a whole call of up to max_tokens tokens (2048 at most), so a call exchanges once
+        c->ep_tcap = std::max(kEpMaxT, std::min(kEpMaxTcap, c->cfg.max_tokens));
+        if (!st) st = dalloc(&c->d_xbuf, (size_t)2 * W * c->ep_tcap * H);
         if (!st) st = dalloc(&c->d_peer_x, (size_t)kEpMaxWorld);
         if (!st) st = dalloc(&c->d_xpart, (size_t)kEpMaxT * H * ((c->cfg.max_tokens + kEpMaxT - 1) / kEpMaxT));
         if (st) return st;
@@ -1311,7 +1315,7 @@ int moe_ep_export(moe_ctx* c, void* out, int cap) {
     // No word may carry an epoch of an earlier attachment (epochs restart at 1 on import).  Every rank
     // exports before the records are exchanged and imports after, so clearing here precedes every
     // rank's first call.
-    CUDA_TRY(cudaMemset(c->d_xbuf, 0, sizeof(uint64_t) * 2 * (size_t)W * kEpMaxT * H));
+    CUDA_TRY(cudaMemset(c->d_xbuf, 0, sizeof(uint64_t) * 2 * (size_t)W * c->ep_tcap * H));
     CUDA_TRY(cudaDeviceSynchronize());
     EpBlob b{};
     b.magic = kEpMagic;
