@@ -147,6 +147,7 @@ struct moe_ctx {
     bool prefill_tc = true;             // prefill batches on the tcgen05 kernels; else the CUDA-core path
     TcItem* d_tc_items = nullptr;       // tile lists of the tcgen05 kernels (gate/up, then down)
     int* d_tc_cnt = nullptr;            // [4] device-built counts: gate/up items, down items, local pairs
+    uint32_t* d_tc_mtdone = nullptr;    // per m-tile: gate/up epilogue warps done (the down GEMM starts early)
     uint32_t* d_tc_sched = nullptr;     // [4] tile-schedule counters (gate/up, down), left zero by each launch
     // MoE-block calls (moe_load_shared, moe_shared_router, moe_block_forward)
     moe_ctx* shared = nullptr;          // one-expert context holding each layer's shared expert
@@ -486,17 +487,20 @@ int run_prefill(moe_ctx* c, int layer, int T, const uint16_t* x, float* o, int a
         if (!c->d_tc_items) {
             int st2 = dalloc(&c->d_tc_items, (size_t)cap_gu + cap_dn);
             if (!st2) st2 = dalloc(&c->d_tc_cnt, 4);
+            if (!st2) st2 = dalloc(&c->d_tc_mtdone, (size_t)mt_max);
             if (st2) return st2;
         }
         TcItem* items_dn = c->d_tc_items + cap_gu;
         const int n_slots = c->arena_slots[layer];
         CUDA_TRY(launch_tc_items(c->d_jobs, c->d_nlj, E, c->arena[layer], c->stride, F, H, c->d_tc_items, cap_gu, items_dn,
-                                 cap_dn, c->d_tc_cnt, c->d_err, st));
+                                 cap_dn, c->d_tc_cnt, c->d_err, c->d_tc_mtdone, st));
         CUDA_TRY(launch_gather_rows(x, c->d_ptok, (int)NP, H, c->d_pf_x, c->sm_count, st, c->d_tc_cnt + 2));
         CUDA_TRY(launch_gateup_tc(c->d_pf_x, (int)NP, c->arena[layer], n_slots, c->stride, c->d_tc_items, 0, c->d_tc_cnt,
-                                  H, F, c->d_act, c->d_tc_sched, c->d_err, c->timeout_ns, c->sm_count, st));
+                                  H, F, c->d_act, c->d_tc_sched, c->d_err, c->timeout_ns, c->sm_count, c->d_tc_mtdone,
+                                  st));
         CUDA_TRY(launch_down_tc(c->d_act, (int)NP, c->arena[layer], n_slots, c->stride, items_dn, 0, c->d_tc_cnt + 1, H, F,
-                                c->d_pf_yf, c->d_tc_sched + 2, c->d_err, c->timeout_ns, c->sm_count, st));
+                                c->d_pf_yf, c->d_tc_sched + 2, c->d_err, c->timeout_ns, c->sm_count, c->d_tc_mtdone,
+                                st));
         CUDA_TRY(launch_combine_rows(c->d_pf_yf, c->d_pw, c->d_comb_off, c->d_comb_p, T, H, accumulate, o, st));
         c->launches += 5;
         *done = true;
@@ -744,7 +748,7 @@ int moe_destroy(moe_ctx* c) {
                   c->d_part, c->d_route_scratch, c->d_pub, c->d_pub_flag, c->d_decide};
     for (void* p : ps) cudaFree(p);
     for (void* q : {(void*)c->d_pf_x, (void*)c->d_pf_yf, (void*)c->d_tc_sched,
-                    (void*)c->d_tc_items, (void*)c->d_tc_cnt})
+                    (void*)c->d_tc_items, (void*)c->d_tc_cnt, (void*)c->d_tc_mtdone})
         if (q) cudaFree(q);
     for (void* q : c->ipc_opened) cudaIpcCloseMemHandle(q);
     for (void* q : {(void*)c->d_xbuf, (void*)c->d_peer_x, (void*)c->d_xpart})

@@ -142,8 +142,14 @@ template <bool DOWN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                    const TcItem* __restrict__ items, int n_items, const int* __restrict__ n_items_dev, int H, int F,
-                   void* __restrict__ out, uint32_t* sched, uint32_t* err, uint64_t timeout_ns) {
+                   void* __restrict__ out, uint32_t* sched, uint32_t* err, uint64_t timeout_ns, uint32_t* mt_done) {
+    // mt_done (nullable): per m-tile count of gate/up epilogue warps whose activation rows are stored.
+    // The gate/up grid lets the down grid launch at its start; a down CTA (on an SM a finished gate/up
+    // CTA left) loads an m-tile's activation rows once all of its gate/up tiles are stored, so the
+    // down GEMM fills the gate/up grid's last, partly empty wave.
+    if (!DOWN && mt_done && threadIdx.x == 0) griddep_launch_dependents();
     if (n_items_dev) n_items = *n_items_dev;  // tile list built on the device (every CTA reads it)
+    const uint32_t mt_full = (uint32_t)(F / 128) * kTcEpiWarps;  // counts of a finished m-tile
     extern __shared__ __align__(1024) unsigned char tsm[];
     unsigned char* ring = reinterpret_cast<unsigned char*>(((uintptr_t)tsm + 1023) & ~(uintptr_t)1023);
     TcCtrl& c = *reinterpret_cast<TcCtrl*>(ring + (size_t)kTcStages * kTcStage);
@@ -189,6 +195,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (i >= n_items) break;
                 const TcItem it = items[i];
                 const bool two = it.rows > 128;
+                if (DOWN && mt_done) {  // the m-tile's activation rows are all stored (bounded wait)
+                    const uint32_t* done = mt_done + i / (H / 256);
+                    while (ld_acquire_gpu(done) < mt_full) {
+                        if (*(volatile int*)&c.abort || globaltimer_ns() > deadline) {
+                            if (!*(volatile int*)&c.abort) atomicOr(err, kErrTimeout);
+                            *(volatile int*)&c.abort = 1;
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                    if (!ok) break;
+                    fence_proxy_async_global();  // generic-proxy stores of other CTAs, before these TMA reads
+                }
                 for (int k = 0; k < nk; k++, g++) {
                     const int s = g % kTcStages;
                     if (g >= kTcStages &&
@@ -314,6 +334,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             tc_fence_before();
+            if (!DOWN && mt_done) {  // this warp's activation rows of the tile are stored
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(mt_done + i / (F / 128), 1u);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&c.tfree);  // this warp's TMEM reads are complete
         }
@@ -345,7 +370,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // cnt[0] = gate/up items, cnt[1] = down items, cnt[2] = local pairs (rows of the gathered x).
 __global__ void __launch_bounds__(256) tc_items_kernel(const Job* __restrict__ jobs, const int* __restrict__ n_jobs, int E,
                                                        const char* arena, size_t stride, int F, int H, TcItem* gu,
-                                                       int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err) {
+                                                       int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err,
+                                                       uint32_t* mt_done) {
     __shared__ int n_s[kMaxExperts], order_s[kMaxExperts], off_s[kMaxExperts + 1];
     __shared__ int np_s;
     const int tid = threadIdx.x;
@@ -380,6 +406,8 @@ __global__ void __launch_bounds__(256) tc_items_kernel(const Job* __restrict__ j
     __syncthreads();
     const int nf = F / 128, nh = H / 256, mt = off_s[nj];
     const bool fits = mt * nf <= cap_gu && mt * nh <= cap_dn;
+    if (mt_done)
+        for (int m = tid; m < mt; m += blockDim.x) mt_done[m] = 0;
     if (fits)
         for (int r = tid; r < nj; r += blockDim.x) {
             const Job jb = jobs[order_s[r]];
@@ -399,10 +427,11 @@ __global__ void __launch_bounds__(256) tc_items_kernel(const Job* __restrict__ j
 }
 
 cudaError_t launch_tc_items(const Job* jobs, const int* n_jobs, int E, const void* arena, size_t stride, int F, int H,
-                            TcItem* gu, int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err, cudaStream_t st) {
+                            TcItem* gu, int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err, uint32_t* mt_done,
+                            cudaStream_t st) {
     if (E > kMaxExperts) return cudaErrorInvalidValue;
     tc_items_kernel<<<1, 256, 0, st>>>(jobs, n_jobs, E, static_cast<const char*>(arena), stride, F, H, gu, cap_gu, dn,
-                                       cap_dn, cnt, err);
+                                       cap_dn, cnt, err, mt_done);
     return cudaGetLastError();
 }
 
@@ -460,7 +489,8 @@ static bool encode_units(EncodeTiledFn enc, CUtensorMap* m, const void* arena, i
 
 cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, int n_slots, size_t slot_bytes,
                            const TcItem* items, int n_items, const int* n_items_dev, int H, int F, float* y,
-                           uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st) {
+                           uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, uint32_t* mt_done,
+                           cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     if (H % 256 || F % kTcBK || slot_bytes % 16 || ((uintptr_t)act | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
@@ -470,14 +500,31 @@ cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, in
         return cudaErrorInvalidValue;
     if (!n_items_dev && n_items <= 0) return cudaSuccess;
     const int grid = n_items_dev ? grid_max : std::min(n_items, grid_max);
-    tc_gemm_kernel<true><<<grid, kTcThreads, kTcSmem, st>>>(ma, md, items, n_items, n_items_dev, H, F, y, sched, err,
-                                                           timeout_ns);
-    return cudaGetLastError();
+    if (!mt_done) {
+        tc_gemm_kernel<true><<<grid, kTcThreads, kTcSmem, st>>>(ma, md, items, n_items, n_items_dev, H, F, y, sched,
+                                                               err, timeout_ns, nullptr);
+        return cudaGetLastError();
+    }
+    // programmatic dependent launch behind the gate/up grid (which triggers at its start): the CTAs
+    // take the SMs its finished CTAs leave and wait per m-tile for its activation rows
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<true>, ma, md, items, n_items, n_items_dev, H, F, (void*)y, sched,
+                              err, timeout_ns, mt_done);
 }
 
 cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, int n_slots, size_t slot_bytes,
                              const TcItem* items, int n_items, const int* n_items_dev, int H, int F, uint16_t* act,
-                             uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st) {
+                             uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, uint32_t* mt_done,
+                             cudaStream_t st) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return cudaErrorNotSupported;
     if (H % kTcBK || F % 128 || slot_bytes % 16 || ((uintptr_t)xg | (uintptr_t)arena) & 15) return cudaErrorInvalidValue;
@@ -488,7 +535,7 @@ cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, i
     if (!n_items_dev && n_items <= 0) return cudaSuccess;
     const int grid = n_items_dev ? grid_max : std::min(n_items, grid_max);
     tc_gemm_kernel<false><<<grid, kTcThreads, kTcSmem, st>>>(mx, mw, items, n_items, n_items_dev, H, F, act, sched, err,
-                                                            timeout_ns);
+                                                            timeout_ns, mt_done);
     return cudaGetLastError();
 }
 

@@ -24,20 +24,26 @@ cudaError_t tc_set_smem_limit();
 // them zero).  Launches sharing a counter pair must be stream-ordered.
 // n_items_dev (nullable): the item count in device memory (a tile list built on the device); the
 // grid is then grid_max CTAs and n_items is ignored.
+// mt_done (nullable): per-m-tile counters (zeroed by launch_tc_items); with them the gate/up grid
+// counts each m-tile's stored activation rows and lets the down grid launched right after it start
+// early (launch_down_tc with the same counters), so the down GEMM fills the gate/up tail.
 cudaError_t launch_gateup_tc(const uint16_t* xg, int xrows, const void* arena, int n_slots, size_t slot_bytes,
                              const TcItem* items, int n_items, const int* n_items_dev, int H, int F, uint16_t* act,
-                             uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st);
+                             uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, uint32_t* mt_done,
+                             cudaStream_t st);
 
 // y[p, h] (fp32) for every item (TcItem.f0 = first output h, 256 per tile).  act: [arows][F] bf16
 // activation rows; arena as above.  H % 256 == 0, F % 64 == 0.
 cudaError_t launch_down_tc(const uint16_t* act, int arows, const void* arena, int n_slots, size_t slot_bytes,
                            const TcItem* items, int n_items, const int* n_items_dev, int H, int F, float* y,
-                           uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, cudaStream_t st);
+                           uint32_t* sched, uint32_t* err, uint64_t timeout_ns, int grid_max, uint32_t* mt_done,
+                           cudaStream_t st);
 
 // Both tile lists from the permutation's local job list (jobs[0 .. *n_jobs)), heaviest job first:
 // gate/up items into gu[cap_gu], down items into dn[cap_dn]; cnt[0], cnt[1] = their counts,
 // cnt[2] = local pairs.  One CTA; E <= 256.
 cudaError_t launch_tc_items(const Job* jobs, const int* n_jobs, int E, const void* arena, size_t stride, int F, int H,
-                            TcItem* gu, int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err, cudaStream_t st);
+                            TcItem* gu, int cap_gu, TcItem* dn, int cap_dn, int* cnt, uint32_t* err, uint32_t* mt_done,
+                            cudaStream_t st);
 
 }  // namespace moe

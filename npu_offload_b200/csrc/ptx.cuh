@@ -17,6 +17,8 @@ __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier
 
 // Orders this thread's generic-proxy shared-memory accesses before later async-proxy (TMA) ones.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// global memory written through the generic proxy, before this thread's async-proxy (TMA) reads of it
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
