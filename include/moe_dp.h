@@ -252,7 +252,7 @@ MOE_API int64_t moe_launch_count(moe_ctx* ctx);
  *                               0 = as deep as shared memory allows, the default).
  *   MOE_OPT_STAGE_BYTES         tuning: target bytes per ring stage of the fused kernel (a stage holds
  *                               max(1, target / unit bytes) units; 0 = the default, 48 KiB).
- *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 8) run the expert FFN as
+ *   MOE_OPT_PREFILL_MIN_T       batches of at least this many tokens (default 10) run the expert FFN as
  *                               grouped tensor-core GEMMs (each routed expert read once) when every
  *                               local expert of the layer is bf16; smaller batches, and layers holding
  *                               int8 experts, take the fused decode kernel (T <= 16) or the CUDA-core

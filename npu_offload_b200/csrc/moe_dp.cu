@@ -141,7 +141,7 @@ struct moe_ctx {
     uint32_t xepoch = 0;
     // prefill: grouped GEMMs on the tcgen05 tensor cores between the gather and the combine
     bool prefill = true;
-    int prefill_min_t = 8;              // smallest batch that takes the tensor-core path
+    int prefill_min_t = 10;             // smallest batch that takes the tensor-core path (measured crossover)
     uint16_t* d_pf_x = nullptr;         // [NP, H] gathered token rows (job-major pairs)
     float* d_pf_yf = nullptr;           // [NP, H] down . act (fp32)
     bool prefill_tc = true;             // prefill batches on the tcgen05 kernels; else the CUDA-core path
@@ -448,9 +448,10 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
 }
 
 // True when the grouped tensor-core GEMMs take a T-token call of this layer: batches of at least
-// prefill_min_t tokens, every local expert of the layer bf16, a supported shape.  From 8 tokens on
-// they read each routed expert once, while the fused decode kernel streams an expert once per token
-// group of at most 4 tokens (measured on B200 at batch 16: 257 us against 335 us per Solar layer).
+// prefill_min_t tokens, every local expert of the layer bf16, a supported shape.  They read each
+// routed expert once, while the fused decode kernel streams an expert once per token group of at
+// most 4 tokens; the default threshold, 10, is the measured crossover on B200 (Solar layer: fused
+// faster at 8 tokens, 171.6 against 185.6 us; tensor cores faster at 10, 204.3 against 214.4 us).
 bool prefill_applies(moe_ctx* c, int layer, int T) {
     const int H = c->cfg.hidden, F = c->cfg.inter, E = c->cfg.n_experts;
     if (!c->prefill || !c->prefill_tc || T < c->prefill_min_t || !tc_available() || F % 128 || H % 256 || E > kMaxExperts)

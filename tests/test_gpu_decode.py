@@ -211,9 +211,10 @@ def test_expert_parallel_partials_sum_to_the_full_layer(layer):
 
 @pytest.mark.parametrize("T", [8, 16])
 def test_batches_from_8_tokens_take_the_tensor_core_path(layer, T):
-    """With the default threshold (MOE_OPT_PREFILL_MIN_T = 8) a bf16 layer's batch of 8 or more tokens
-    runs as grouped tensor-core GEMMs (each routed expert read once): the same top-k, the output
-    within the parity bar of the fused kernel's and of the oracle, and more than one launch."""
+    """With the threshold at 8 tokens (MOE_OPT_PREFILL_MIN_T; the default is 10) a bf16 layer's batch
+    of 8 or more tokens runs as grouped tensor-core GEMMs (each routed expert read once): the same
+    top-k, the output within the parity bar of the fused kernel's and of the oracle, and more than one
+    launch."""
     from npu_offload_b200._lib import MOE_OPT_PREFILL_MIN_T
     p, W = layer
     x, lg, xd, lgd = _inputs(1400 + T, T)
