@@ -520,24 +520,33 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     // writes, so the plan is made while the previous grid of the stream still finishes.  Everything
     // that grid may touch (hidden states, partial sums, counters, outputs) waits for its completion
     // (griddepcontrol.wait) first: host calls here, the consumers before their first segment.
-    if (a.x_src) {  // host call: each CTA moves a slice of the pinned inputs to the device
+    if (a.x_src) {  // host call: the pinned inputs move to the device
         griddep_wait();
-        const int nx = a.T * a.H / 8, nl = a.T * a.E;
+        // the logits, which every CTA's plan needs: CTA 0 copies them (16-byte reads) and publishes
+        // the call's number; every CTA copies a slice of the hidden states, which only the consumers
+        // read, after planning (waited for there).  (Each CTA reading the pinned logits itself queued
+        // 147 CTAs' small reads on the host link: plan ready at 22 us, measured.)
+        if (s == 0) {  // both buffers 16-byte aligned (the host stages unaligned pinned logits)
+            const int nl = a.T * a.E, nl4 = nl / 4;
+            float4* ld = reinterpret_cast<float4*>(const_cast<float*>(a.logits));
+            const float4* ls = reinterpret_cast<const float4*>(a.lg_src);
+            for (int i = tid; i < nl4; i += kDecThreads) ld[i] = ls[i];
+            for (int i = 4 * nl4 + tid; i < nl; i += kDecThreads) const_cast<float*>(a.logits)[i] = a.lg_src[i];
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hctr + 1), "r"(a.hidx + 1u) : "memory");
+        }
+        const int nx = a.T * a.H / 8;
         const int x0 = (int)((long long)s * nx / G), x1 = (int)((long long)(s + 1) * nx / G);
-        const int l0 = (int)((long long)s * nl / G), l1 = (int)((long long)(s + 1) * nl / G);
         uint4* xd = reinterpret_cast<uint4*>(const_cast<uint16_t*>(a.x));
         const uint4* xs = reinterpret_cast<const uint4*>(a.x_src);
         for (int i = x0 + tid; i < x1; i += kDecThreads) xd[i] = xs[i];
-        float* ld = const_cast<float*>(a.logits);
-        for (int i = l0 + tid; i < l1; i += kDecThreads) ld[i] = a.lg_src[i];
         __threadfence();
         __syncthreads();
-        // every CTA plans from the device copy of the logits: wait for every slice (reading the pinned
-        // logits from every CTA instead queues 147 CTAs' reads on the host link: ~20 us, measured)
         if (tid == 0) {
-            atomicAdd(a.hctr, 1u);
+            atomicAdd(a.hctr, 1u);  // this CTA's slice of the hidden states is in place
             const uint64_t dl = globaltimer_ns() + a.timeout_ns;
-            while ((int)(ld_acquire_gpu(a.hctr) - (a.hbase + (uint32_t)G)) < 0) {
+            while ((int)(ld_acquire_gpu(a.hctr + 1) - (a.hidx + 1u)) < 0) {  // the logits are in place
                 if (globaltimer_ns() > dl) {
                     c.abort_flag = 1;
                     atomicOr(a.err, kErrTimeout);
@@ -651,6 +660,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(const DecodeArgs
     if (tid == 0) {
         const unsigned long long free_at = cbase >= (unsigned long long)G ? cbase - (unsigned long long)G : 0ull;
         while (ld_acquire_gpu_u64(&a.cnt[2]) < free_at) {
+            if (timed_out(c, a.err, deadline)) break;
+            __nanosleep(32);
+        }
+        // host calls: every CTA's slice of the hidden states is on the device
+        while (a.x_src && (int)(ld_acquire_gpu(a.hctr) - (a.hbase + (uint32_t)G)) < 0) {
             if (timed_out(c, a.err, deadline)) break;
             __nanosleep(32);
         }

@@ -94,13 +94,15 @@ struct DecodeArgs {
                            //   pairs are every token with weight 1 (kept out of the routed sum)
     int32_t* idx_out;      // [T, K] router indices (written by CTA 0), or null
     float* w_out;          // [T, K] router weights, or null
-    // host calls: pinned host sources the CTAs copy (a slice each) into x / logits before routing;
-    // hctr counts, over the context's host calls, the CTAs whose slice is in place: this call's
-    // slices are all in once it reaches hbase + G (wrapping 32-bit arithmetic)
+    // host calls: pinned host sources copied into x / logits on the device.  hctr[0] counts, over the
+    // context's host calls, the CTAs whose slice of x is in place (this call's are all in once it
+    // reaches hbase + G); hctr[1] holds the number (hidx + 1) of the latest host call whose logits CTA 0
+    // copied (wrapping 32-bit arithmetic for both)
     const uint16_t* x_src;
     const float* lg_src;
     uint32_t* hctr;
     uint32_t hbase;
+    uint32_t hidx;
     const uint16_t* x;     // [T, H] bf16
     float* out;            // [T, H] fp32, 16-byte aligned (device or device-accessible pinned host memory)
     float* part;           // [grid * kSegPerCta, kGroupMax, H] fp32 partial sums of this call (one of two

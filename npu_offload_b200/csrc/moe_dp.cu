@@ -403,6 +403,7 @@ int launch_fused(moe_ctx* c, int layer, const float* lg, DecodeArgs& da, size_t 
     da.w_out = c->d_w;
     da.hctr = c->d_hctr;
     if (x_host) {
+        da.hidx = c->hcalls;
         da.hbase = c->hcalls++ * (uint32_t)dgrid;
         da.x_src = x_host;
         da.lg_src = lg;
@@ -558,7 +559,8 @@ int forward_host_fused(moe_ctx* c, int layer, int T, const uint16_t* hidden, con
                        int32_t* topk_idx, float* topk_w, int flags, cudaStream_t st, DecodeArgs& da, size_t dsmem) {
     const int H = c->cfg.hidden, E = c->cfg.n_experts, K = c->cfg.top_k;
     const size_t hb = (size_t)T * H * 2, lb = (size_t)T * E * 4, ob = (size_t)T * H * 4;
-    const bool pin_x = device_mapped(hidden) && ((uintptr_t)hidden & 15u) == 0, pin_l = device_mapped(logits);
+    const bool pin_x = device_mapped(hidden) && ((uintptr_t)hidden & 15u) == 0;
+    const bool pin_l = device_mapped(logits) && ((uintptr_t)logits & 15u) == 0;  // the kernel reads it by 16 bytes
     const bool pin_o = device_mapped(out) && ((uintptr_t)out & 15u) == 0;
     int s;
     const float* lg = logits;
