@@ -69,6 +69,8 @@ def parse():
                     help="int8 measurement: the N least popular experts of every layer stored int8 (configs[4]: 96)")
     ap.add_argument("--cold-slots", type=int, default=0,
                     help="HBM slots per layer for the host-cold tier measurement (0: skip)")
+    ap.add_argument("--no-alt-split", action="store_true",
+                    help="N > 1 with --ep-shard units: skip the expert-sharded split's batch-1 measurement")
     ap.add_argument("--ep-shard", choices=["units", "experts"], default="units",
                     help="N>1 split: every rank a slice of every expert's units, or whole experts per rank")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
@@ -743,6 +745,26 @@ def our_arm(args):
     if ws == 1 and not args.no_int8:  # last: it re-stores most of the stack's experts as int8
         int8 = int8_run(stack, args, max(1, args.steps // 4), min(args.warmup, 3))
 
+    alt = None
+    if ws > 1 and stack.shard == "units" and not args.no_alt_split:
+        # configs[2]'s own split beside the default one, same build and run: each rank owns 16 experts
+        # per layer (at N = 8) by the popularity stripe of the placement plan.  The unit-sharded stack
+        # is released first (after every rank is done with its peers' buffers).
+        barrier(ws)
+        stack.plane.close()
+        alt_args = argparse.Namespace(**vars(args))
+        alt_args.ep_shard = "experts"
+        astack = Stack(alt_args, ws, rank, device, 1, L)
+        ks = max(1, args.steps // 4)
+        ams, _, _ = timed(astack, ks, min(args.warmup, 3), ws, profile=False)
+        ams = max_over_ranks(ams, ws)
+        busiest = max_over_ranks(float(np.max(astack.ucount)), ws)
+        alt = {"ep_shard": "experts: popularity stripe (configs[2]: 16 experts per GPU per layer at N = 8)",
+               "batch": 1, "value": L * ks / (ams / 1e3), "us_per_layer": ams * 1e3 / (ks * L),
+               "routed_experts_busiest_rank_max": busiest}
+        barrier(ws)
+        stack = astack  # closed below like the main stack
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         def pool(P):
@@ -780,7 +802,7 @@ def our_arm(args):
                            "experts_per_layer": float(ucount_main.mean())},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches_all,
                 "clocks": clk.summary(), "cpu_baseline": cpu, "sweep": sweep, "prefill": prefill,
-                "block": block, "cold": cold, "int8": int8}
+                "block": block, "cold": cold, "int8": int8, "alt_split": alt}
         print(json.dumps(line), flush=True)
     if ws > 1:
         barrier(ws)  # no rank frees its exchange buffer while a peer may still use it
