@@ -1,6 +1,6 @@
-// Fused persistent decode kernel for the B200 MoE data plane: one launch per layer performs the
-// grouped SwiGLU expert GEMV (gate/up + down) and the weighted combine for a routing plan made by
-// plan_kernel (plan.cu).
+// Fused persistent decode kernel for the B200 MoE data plane: one launch per layer routes the call
+// (plan.cuh: in every CTA, or published by a one-CTA planner kernel while the previous call streams)
+// and performs the grouped SwiGLU expert GEMV (gate/up + down) and the weighted combine.
 //
 // Semantics are the reference's cold-expert path (solar_hybrid/cpu_moe.cpp:38-96, int8 weight-only
 // form cpu_kern.c:306-333) behind the layer surface of track2_opt/solar_engine/src/main.rs:149-209:
@@ -10,7 +10,7 @@
 // Work split.  Expert tables hold one unit per intermediate index f: [gate row f | up row f | down
 // column f].  A unit is self-contained -- act[f] needs only gate/up row f, and its contribution to
 // the output is act[f] * down column f -- so the plan cuts the stream of all units of the call into
-// one contiguous, byte-balanced share per CTA with no dependency between CTAs until the very end.
+// one contiguous, cost-balanced share per CTA with no dependency between CTAs until the very end.
 //   producer   one thread of its own warpgroup streams the CTA's units with 1-D bulk async copies
 //              (TMA engine) into an NS-deep shared-memory ring guarded by mbarriers (L2 evict-first:
 //              read once).  Issuing a copy can stall the issuing thread for a large part of a
@@ -24,13 +24,14 @@
 //              x and y of the segment's token group (<= 4 tokens) stay in registers.
 //   partials   at the end of a segment every warp stores its y slice as that segment's fp32 partial
 //              sums (int8 experts: times the down-row scales).
-//   reduction  after a grid-wide arrival counter, CTA s owns output quads [q0, q1): per pair it adds
-//              its group's segment partials in segment order, then per token the pairs in job order,
-//              weighted -- a fixed order, so results are deterministic for a given grid size.
+//   reduction  after a grid-wide arrival counter, the last nred CTAs to arrive each own a slice of
+//              output quads: per pair they add its group's segment partials in segment order, then
+//              per token the pairs in job order, weighted -- a fixed order, so results are
+//              deterministic for a given partition.  The other CTAs leave at once.
 // Every wait is bounded (globaltimer); a timeout raises kErrTimeout, stops the CTA, drains the bulk
-// copies in flight and returns.  Programmatic dependent launch lets the next layer's plan kernel and
-// weight streaming start while this grid finishes; everything that reads state written by the
-// previous grid (x, partials, counters, outputs) runs after griddepcontrol.wait.
+// copies in flight and returns.  Programmatic dependent launch lets the next call's CTAs take the SMs
+// this grid frees and start streaming while its reducers finish; the call counters (DecodeArgs::cnt)
+// order what one call writes and the next reads (partial sums, outputs, exchange buffers).
 #include <climits>
 #include <cstddef>
 

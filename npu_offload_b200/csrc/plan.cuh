@@ -9,7 +9,7 @@
 //                appends the shared expert as one more job (every token, weight 1)
 //   token groups each job's pairs split into groups of at most gmax tokens; a group is one pass
 //                over the job's unit table (F units: gate row f, up row f, down column f)
-//   own share    the unit stream (all groups' units, in group order) cut into G byte-balanced
+//   own share    the unit stream (all groups' units, in group order) cut into G cost-balanced
 //                contiguous shares at unit boundaries; CTA s computes only share s (two binary
 //                searches over the jobs), its segments (runs of one group's units) and their stages
 //   reduction    per pair: its group and row; per token: its pairs in job order; per group: its
