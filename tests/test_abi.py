@@ -79,3 +79,22 @@ def test_cpu_moe_dropin_validates_shapes_before_touching_gpu():
     # no experts -> zeros, like the reference (cpu_moe.cpp:42-43)
     out = gpu_moe(torch.zeros(3, 64, dtype=torch.bfloat16), [], [], [], [])
     assert out.shape == (3, 64) and out.dtype == torch.float32 and float(out.abs().sum()) == 0.0
+
+
+def test_header_constants_match_the_python_binding():
+    """Every status code, flag, scoring mode, expert kind and option number the header defines has
+    the same value in the Python binding, and the binding defines no option the header lacks."""
+    import re
+    from npu_offload_b200 import _lib
+    defs = {}
+    with open(_lib.HEADER) as f:
+        for line in f:
+            m = re.match(r"#define (MOE_[A-Z0-9_]+) (0x[0-9a-fA-F]+|\d+)\b", line)
+            if m and m.group(1) not in ("MOE_DP_ABI_VERSION",):
+                defs[m.group(1)] = int(m.group(2), 0)
+    assert len(defs) > 30
+    for name, value in defs.items():
+        assert hasattr(_lib, name), f"{name} missing from the binding"
+        assert getattr(_lib, name) == value, f"{name}: header {value}, binding {getattr(_lib, name)}"
+    py_opts = {n for n in dir(_lib) if n.startswith("MOE_OPT_")}
+    assert py_opts == {n for n in defs if n.startswith("MOE_OPT_")}
